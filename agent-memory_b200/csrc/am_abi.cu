@@ -1,0 +1,369 @@
+// C ABI of libamq4.so: argument validation, dispatch to the kernel launchers, and
+// per-thread error reporting.  The library allocates no device memory and keeps no
+// pointer after a call returns.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "am_common.cuh"
+#include "am_internal.h"
+
+namespace am {
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+void clear_error() { g_last_error[0] = '\0'; }
+
+static int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return AM_OK;
+  if (e == cudaErrorNotSupported) {
+    set_error("%s: no kernel for this configuration", what);
+    return AM_ERR_UNSUPPORTED;
+  }
+  set_error("%s: CUDA error %d (%s)", what, static_cast<int>(e), cudaGetErrorString(e));
+  return AM_ERR_CUDA;
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static bool valid_half_dtype(int d) { return d == AM_DTYPE_F16 || d == AM_DTYPE_BF16; }
+
+static int check_cache(const am_q4_cache* c, const char* fn) {
+  if (c == nullptr) {
+    set_error("%s: cache is NULL", fn);
+    return AM_ERR_INVALID;
+  }
+  if (!c->k_codes || !c->k_scales || !c->k_biases || !c->v_codes || !c->v_scales || !c->v_biases) {
+    set_error("%s: a cache buffer is NULL", fn);
+    return AM_ERR_INVALID;
+  }
+  if (!valid_half_dtype(c->scale_dtype)) {
+    set_error("%s: scale_dtype must be F16 or BF16", fn);
+    return AM_ERR_INVALID;
+  }
+  if (c->n_kv_heads <= 0 || c->k_dim <= 0 || c->v_dim <= 0 || c->k_dim % 64 || c->v_dim % 64) {
+    set_error("%s: n_kv_heads > 0 and head dims that are multiples of 64 required (got %d, %d, %d)",
+              fn, c->n_kv_heads, c->k_dim, c->v_dim);
+    return AM_ERR_INVALID;
+  }
+  if (!aligned(c->k_codes, 16) || !aligned(c->v_codes, 16) || !aligned(c->k_scales, 4) ||
+      !aligned(c->k_biases, 4) || !aligned(c->v_scales, 4) || !aligned(c->v_biases, 4)) {
+    set_error("%s: codes must be 16-byte and scales/biases 4-byte aligned", fn);
+    return AM_ERR_INVALID;
+  }
+  if (c->layout == AM_LAYOUT_CONTIGUOUS) {
+    if (c->capacity <= 0 || c->capacity % 16) {
+      set_error("%s: contiguous capacity must be a positive multiple of 16 (got %lld)", fn,
+                static_cast<long long>(c->capacity));
+      return AM_ERR_INVALID;
+    }
+  } else if (c->layout == AM_LAYOUT_PAGED) {
+    if (c->block_table == nullptr || c->block_table_stride <= 0 || c->capacity <= 0 ||
+        c->block_tokens <= 0 || c->block_tokens % 16) {
+      set_error("%s: paged cache needs a block table, num_blocks > 0 and block_tokens %% 16 == 0", fn);
+      return AM_ERR_INVALID;
+    }
+  } else {
+    set_error("%s: unknown layout %d", fn, c->layout);
+    return AM_ERR_INVALID;
+  }
+  return AM_OK;
+}
+
+static int check_args(const am_q4_cache* c, const am_attn_args* a, const char* fn) {
+  if (a == nullptr || a->q == nullptr || a->out == nullptr || a->kv_len == nullptr) {
+    set_error("%s: q, out and kv_len are required", fn);
+    return AM_ERR_INVALID;
+  }
+  if (!valid_half_dtype(a->q_dtype)) {
+    set_error("%s: q_dtype must be F16 or BF16", fn);
+    return AM_ERR_INVALID;
+  }
+  if (!(valid_half_dtype(a->out_dtype) || a->out_dtype == AM_DTYPE_F32)) {
+    set_error("%s: out_dtype must be F16, BF16 or F32", fn);
+    return AM_ERR_INVALID;
+  }
+  if (a->batch < 0 || a->n_q_heads <= 0 || a->q_len < 0 || a->n_q_heads % c->n_kv_heads) {
+    set_error("%s: n_q_heads (%d) must be a positive multiple of n_kv_heads (%d)", fn,
+              a->n_q_heads, c->n_kv_heads);
+    return AM_ERR_INVALID;
+  }
+  if (c->layout == AM_LAYOUT_CONTIGUOUS && a->batch > c->batch) {
+    set_error("%s: batch %d exceeds the cache's batch extent %d", fn, a->batch, c->batch);
+    return AM_ERR_INVALID;
+  }
+  if (a->max_kv_len < 0) {
+    set_error("%s: max_kv_len must be >= 0", fn);
+    return AM_ERR_INVALID;
+  }
+  if (a->mask_kind != AM_MASK_NONE) {
+    if (a->mask == nullptr) {
+      set_error("%s: mask_kind set but mask is NULL", fn);
+      return AM_ERR_INVALID;
+    }
+    if (a->mask_kind == AM_MASK_BOOL && a->mask_dtype != AM_DTYPE_U8) {
+      set_error("%s: boolean masks are u8", fn);
+      return AM_ERR_INVALID;
+    }
+    if (a->mask_kind == AM_MASK_ADDITIVE && !(valid_half_dtype(a->mask_dtype) ||
+                                              a->mask_dtype == AM_DTYPE_F32)) {
+      set_error("%s: additive masks are F16, BF16 or F32", fn);
+      return AM_ERR_INVALID;
+    }
+    if (a->mask_kind != AM_MASK_BOOL && a->mask_kind != AM_MASK_ADDITIVE) {
+      set_error("%s: unknown mask_kind %d", fn, a->mask_kind);
+      return AM_ERR_INVALID;
+    }
+  }
+  if (!std::isfinite(a->scale)) {
+    set_error("%s: scale must be finite", fn);
+    return AM_ERR_INVALID;
+  }
+  return AM_OK;
+}
+
+static int decode_geometry(const am_q4_cache* c, const am_attn_args* a, int* row_groups,
+                           int* chunk, int* n_chunks) {
+  const int n_rep = a->n_q_heads / c->n_kv_heads;
+  const int rows = n_rep * a->q_len;
+  *row_groups = (rows + 7) / 8;
+  int span = a->max_kv_len;
+  if (a->mask_kind == AM_MASK_NONE && a->window > 0) {
+    const long long w = (long long)a->window + a->q_len - 1;
+    if (w < span) span = static_cast<int>(w);
+  }
+  decode_plan(a->batch, c->n_kv_heads, *row_groups, span, chunk, n_chunks);
+  return rows;
+}
+
+static void fill_params(DecodeParams& p, const am_q4_cache* cache, const am_attn_args* a) {
+  const int n_rep = a->n_q_heads / cache->n_kv_heads;
+  p.kc = cache->k_codes;
+  p.ks = static_cast<const uint16_t*>(cache->k_scales);
+  p.kb = static_cast<const uint16_t*>(cache->k_biases);
+  p.vc = cache->v_codes;
+  p.vs = static_cast<const uint16_t*>(cache->v_scales);
+  p.vb = static_cast<const uint16_t*>(cache->v_biases);
+  p.capacity = cache->capacity;
+  p.table = cache->block_table;
+  p.table_stride = cache->block_table_stride;
+  p.block_tokens = cache->block_tokens;
+  p.hkv = cache->n_kv_heads;
+  p.k_dim = cache->k_dim;
+  p.v_dim = cache->v_dim;
+  p.hq = a->n_q_heads;
+  p.q_len = a->q_len;
+  p.n_rep = n_rep;
+  p.rows_per_head = n_rep * a->q_len;
+  p.q_bf16 = a->q_dtype == AM_DTYPE_BF16;
+  p.q = static_cast<const uint16_t*>(a->q);
+  p.qsb = a->q_stride_b;
+  p.qsh = a->q_stride_h;
+  p.qsl = a->q_stride_l;
+  p.out = a->out;
+  p.out_dtype = a->out_dtype;
+  p.osb = a->o_stride_b;
+  p.osh = a->o_stride_h;
+  p.osl = a->o_stride_l;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  p.kv_len = a->kv_len;
+  p.kv_start = a->kv_start;
+  p.causal = a->causal;
+  p.window = a->window;
+  p.mask_kind = a->mask_kind;
+  p.mask_dtype = a->mask_dtype;
+  p.mask = a->mask;
+  p.msb = a->mask_stride_b;
+  p.msh = a->mask_stride_h;
+  p.msl = a->mask_stride_l;
+  p.msn = a->mask_stride_n;
+  p.status = a->status;
+}
+
+}  // namespace am
+
+using namespace am;
+
+extern "C" {
+
+int am_abi_version(void) { return AM_ABI_VERSION; }
+
+const char* am_last_error(void) { return g_last_error; }
+
+int am_q4_quantize(const void* x, int32_t dtype, int64_t rows, int32_t dim, uint32_t* codes,
+                   void* scales, void* biases, void* stream) {
+  clear_error();
+  if (!valid_half_dtype(dtype) || rows < 0 || dim <= 0 || dim % 64) {
+    set_error("am_q4_quantize: dtype F16/BF16 and dim %% 64 == 0 required (dim=%d)", dim);
+    return AM_ERR_INVALID;
+  }
+  if (rows == 0) return AM_OK;
+  if (!x || !codes || !scales || !biases || !aligned(x, 16) || !aligned(codes, 4) ||
+      !aligned(scales, 2) || !aligned(biases, 2)) {
+    set_error("am_q4_quantize: null or misaligned buffer (x needs 16-byte alignment)");
+    return AM_ERR_INVALID;
+  }
+  return cuda_status(launch_quantize(x, dtype == AM_DTYPE_BF16, rows, dim, codes, scales, biases,
+                                     static_cast<cudaStream_t>(stream)),
+                     "am_q4_quantize");
+}
+
+int am_q4_dequantize(const uint32_t* codes, const void* scales, const void* biases,
+                     int32_t scale_dtype, int64_t rows, int32_t dim, void* out, int32_t out_dtype,
+                     void* stream) {
+  clear_error();
+  if (!valid_half_dtype(scale_dtype) || rows < 0 || dim <= 0 || dim % 64 ||
+      !(valid_half_dtype(out_dtype) || out_dtype == AM_DTYPE_F32)) {
+    set_error("am_q4_dequantize: bad dtype or dim");
+    return AM_ERR_INVALID;
+  }
+  if (rows == 0) return AM_OK;
+  if (!codes || !scales || !biases || !out) {
+    set_error("am_q4_dequantize: null buffer");
+    return AM_ERR_INVALID;
+  }
+  return cuda_status(launch_dequantize(codes, scales, biases, scale_dtype == AM_DTYPE_BF16, rows, dim,
+                                       out, out_dtype, static_cast<cudaStream_t>(stream)),
+                     "am_q4_dequantize");
+}
+
+int am_q4_append(const am_q4_cache* cache, const void* k, const void* v, int32_t dtype,
+                 int32_t batch, int32_t n_new, int64_t k_stride_b, int64_t k_stride_h,
+                 int64_t k_stride_l, int64_t v_stride_b, int64_t v_stride_h, int64_t v_stride_l,
+                 const int32_t* positions, int32_t* status, void* stream) {
+  clear_error();
+  int rc = check_cache(cache, "am_q4_append");
+  if (rc) return rc;
+  if (dtype != cache->scale_dtype) {
+    set_error("am_q4_append: input dtype must equal the cache's scale dtype");
+    return AM_ERR_INVALID;
+  }
+  if (batch < 0 || n_new < 0) {
+    set_error("am_q4_append: negative batch or n_new");
+    return AM_ERR_INVALID;
+  }
+  if (batch == 0 || n_new == 0) return AM_OK;
+  if (!k || !v || !positions || !aligned(k, 16) || !aligned(v, 16) ||
+      ((k_stride_b | k_stride_h | k_stride_l | v_stride_b | v_stride_h | v_stride_l) % 8)) {
+    set_error("am_q4_append: k/v must be 16-byte aligned with strides that are multiples of 8");
+    return AM_ERR_INVALID;
+  }
+  if (cache->layout == AM_LAYOUT_CONTIGUOUS && batch > cache->batch) {
+    set_error("am_q4_append: batch %d exceeds the cache's batch extent %d", batch, cache->batch);
+    return AM_ERR_INVALID;
+  }
+  AppendParams p{};
+  p.k = static_cast<const uint16_t*>(k);
+  p.v = static_cast<const uint16_t*>(v);
+  p.ksb = k_stride_b;
+  p.ksh = k_stride_h;
+  p.ksl = k_stride_l;
+  p.vsb = v_stride_b;
+  p.vsh = v_stride_h;
+  p.vsl = v_stride_l;
+  p.batch = batch;
+  p.hkv = cache->n_kv_heads;
+  p.n_new = n_new;
+  p.k_dim = cache->k_dim;
+  p.v_dim = cache->v_dim;
+  p.positions = positions;
+  p.kc = cache->k_codes;
+  p.ks = static_cast<uint16_t*>(cache->k_scales);
+  p.kb = static_cast<uint16_t*>(cache->k_biases);
+  p.vc = cache->v_codes;
+  p.vs = static_cast<uint16_t*>(cache->v_scales);
+  p.vb = static_cast<uint16_t*>(cache->v_biases);
+  p.layout = cache->layout;
+  p.capacity = cache->capacity;
+  p.block_tokens = cache->block_tokens;
+  p.table_stride = cache->block_table_stride;
+  p.table = cache->block_table;
+  p.status = status;
+  return cuda_status(launch_append(p, dtype == AM_DTYPE_BF16, static_cast<cudaStream_t>(stream)),
+                     "am_q4_append");
+}
+
+size_t am_q4_attention_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args) {
+  if (cache == nullptr || args == nullptr || cache->n_kv_heads <= 0 || args->n_q_heads <= 0)
+    return 0;
+  int row_groups, chunk, n_chunks;
+  decode_geometry(cache, args, &row_groups, &chunk, &n_chunks);
+  if (n_chunks <= 1) return 0;
+  const size_t rows_total = static_cast<size_t>(args->n_q_heads) * args->q_len;
+  return static_cast<size_t>(args->batch) * rows_total * n_chunks * (cache->v_dim + 2) * sizeof(float);
+}
+
+int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  clear_error();
+  int rc = check_cache(cache, "am_q4_decode");
+  if (rc) return rc;
+  rc = check_args(cache, a, "am_q4_decode");
+  if (rc) return rc;
+  if (!decode_supported(cache->k_dim, cache->v_dim)) {
+    set_error("am_q4_decode: no kernel for k_dim=%d v_dim=%d", cache->k_dim, cache->v_dim);
+    return AM_ERR_UNSUPPORTED;
+  }
+  const int n_rep = a->n_q_heads / cache->n_kv_heads;
+  if (n_rep * a->q_len > 64) {
+    set_error("am_q4_decode: n_rep * q_len = %d exceeds 64; use am_q4_prefill", n_rep * a->q_len);
+    return AM_ERR_UNSUPPORTED;
+  }
+  if (a->batch == 0 || a->q_len == 0) return AM_OK;
+  int row_groups, chunk, n_chunks;
+  decode_geometry(cache, a, &row_groups, &chunk, &n_chunks);
+  const size_t need = am_q4_attention_workspace_bytes(cache, a);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))) {
+    set_error("am_q4_decode: workspace of %zu bytes required (got %zu)", need, workspace_bytes);
+    return AM_ERR_WORKSPACE;
+  }
+  DecodeParams p{};
+  fill_params(p, cache, a);
+  p.chunk = chunk;
+  p.max_chunks = n_chunks;
+  p.ws = static_cast<float*>(workspace);
+  return cuda_status(launch_decode(p, a->batch, row_groups, cache->layout == AM_LAYOUT_PAGED,
+                                   cache->scale_dtype == AM_DTYPE_BF16,
+                                   static_cast<cudaStream_t>(stream)),
+                     "am_q4_decode");
+}
+
+int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* stream) {
+  clear_error();
+  int rc = check_cache(cache, "am_q4_prefill");
+  if (rc) return rc;
+  rc = check_args(cache, a, "am_q4_prefill");
+  if (rc) return rc;
+  if (!prefill_supported(cache->k_dim, cache->v_dim)) {
+    set_error("am_q4_prefill: no kernel for k_dim=%d v_dim=%d", cache->k_dim, cache->v_dim);
+    return AM_ERR_UNSUPPORTED;
+  }
+  if (a->batch == 0 || a->q_len == 0) return AM_OK;
+  DecodeParams p{};
+  fill_params(p, cache, a);
+  return cuda_status(launch_prefill(p, a->batch, cache->layout == AM_LAYOUT_PAGED,
+                                    cache->scale_dtype == AM_DTYPE_BF16,
+                                    static_cast<cudaStream_t>(stream)),
+                     "am_q4_prefill");
+}
+
+int am_q4_attention(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  if (cache != nullptr && a != nullptr && cache->n_kv_heads > 0 && a->n_q_heads > 0) {
+    const int n_rep = a->n_q_heads / cache->n_kv_heads;
+    if (n_rep * a->q_len > 64 || (a->q_len >= 16 && prefill_supported(cache->k_dim, cache->v_dim))) {
+      return am_q4_prefill(cache, a, stream);
+    }
+  }
+  return am_q4_decode(cache, a, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

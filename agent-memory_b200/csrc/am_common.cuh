@@ -1,0 +1,188 @@
+// Shared device helpers and launch-parameter structs for the Q4 attention kernels.
+// sm_100a only.  PTX used here: cp.async (LDGSTS), mma.sync m16n8k16, movmatrix,
+// ex2.approx, and in the prefill kernel tcgen05.* / mbarrier.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "am_q4.h"
+
+namespace am {
+
+constexpr int kGroup = 64;  // quantization group size along the head dimension
+
+// ---------------------------------------------------------------- error reporting (host)
+void set_error(const char* fmt, ...);
+void clear_error();
+
+// ---------------------------------------------------------------- 16-bit float loads
+template <bool BF16>
+__device__ __forceinline__ float h2f(uint16_t bits) {
+  if constexpr (BF16) {
+    return __uint_as_float(static_cast<uint32_t>(bits) << 16);
+  } else {
+    return __half2float(__ushort_as_half(bits));
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint16_t f2h(float v) {
+  if constexpr (BF16) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  } else {
+    return __half_as_ushort(__float2half_rn(v));
+  }
+}
+
+__device__ __forceinline__ float h2f_rt(uint16_t bits, bool bf16) {
+  return bf16 ? h2f<true>(bits) : h2f<false>(bits);
+}
+
+// Store one fp32 value as dtype (AM_DTYPE_F16 / BF16 / F32).
+__device__ __forceinline__ void store_out(void* base, int64_t idx, float v, int dtype) {
+  if (dtype == AM_DTYPE_F32) {
+    static_cast<float*>(base)[idx] = v;
+  } else if (dtype == AM_DTYPE_BF16) {
+    static_cast<uint16_t*>(base)[idx] = f2h<true>(v);
+  } else {
+    static_cast<uint16_t*>(base)[idx] = f2h<false>(v);
+  }
+}
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src));
+}
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(dst)), "l"(src));
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// D += A(16x16, f16, row) * B(16x8, f16, col), fp32 accumulators.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Transpose an 8x8 matrix of 16-bit values held in mma fragment layout across the warp.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void flag_status(int32_t* status, int bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+// ---------------------------------------------------------------- launch parameters
+
+// Quantize-on-append / plain quantize.  Rows are (b, h, l) triples of the source tensors.
+struct AppendParams {
+  const uint16_t* k;
+  const uint16_t* v;
+  int64_t ksb, ksh, ksl;  // element strides of the new K rows
+  int64_t vsb, vsh, vsl;
+  int32_t batch, hkv, n_new;
+  int32_t k_dim, v_dim;
+  const int32_t* positions;  // [batch] first destination position
+  // destination cache
+  uint32_t* kc;
+  uint16_t* ks;
+  uint16_t* kb;
+  uint32_t* vc;
+  uint16_t* vs;
+  uint16_t* vb;
+  int32_t layout;
+  int64_t capacity;  // contiguous rows per (b, h) or paged num_blocks
+  int32_t block_tokens;
+  int32_t table_stride;
+  const int32_t* table;
+  int32_t* status;
+};
+
+// Split-KV decode attention.
+struct DecodeParams {
+  const uint32_t* kc;
+  const uint16_t* ks;
+  const uint16_t* kb;
+  const uint32_t* vc;
+  const uint16_t* vs;
+  const uint16_t* vb;
+  int64_t capacity;
+  const int32_t* table;
+  int32_t table_stride;
+  int32_t block_tokens;
+  int32_t hkv;
+  int32_t k_dim;
+  int32_t v_dim;
+  int32_t hq;
+  int32_t q_len;
+  int32_t n_rep;
+  int32_t rows_per_head;  // n_rep * q_len
+  int32_t q_bf16;
+  const uint16_t* q;
+  int64_t qsb, qsh, qsl;
+  void* out;
+  int32_t out_dtype;
+  int64_t osb, osh, osl;
+  float scale_log2;  // softmax scale * log2(e)
+  const int32_t* kv_len;
+  const int32_t* kv_start;
+  int32_t causal;
+  int32_t window;
+  int32_t mask_kind;
+  int32_t mask_dtype;
+  const void* mask;
+  int64_t msb, msh, msl, msn;
+  int32_t* status;
+  int32_t chunk;       // tokens per split (multiple of 64)
+  int32_t max_chunks;  // grid.x
+  float* ws;           // partials [batch][hq*q_len][max_chunks][v_dim + 2]
+};
+
+// Visible key range of a sequence for the structured mask: keys outside [lo, hi) are
+// excluded for every query row.  lo is rounded down to a multiple of 16 (tile size).
+__device__ __forceinline__ void visible_range(int n, int st, int q_len, int window, bool dense_mask,
+                                              int& lo, int& hi) {
+  hi = n;
+  if (dense_mask) {
+    lo = 0;
+  } else {
+    lo = st;
+    if (window > 0) lo = max(lo, n - q_len - window + 1);
+    lo = max(lo, 0);
+  }
+  lo &= ~15;
+}
+
+}  // namespace am

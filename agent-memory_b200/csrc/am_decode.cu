@@ -1,0 +1,599 @@
+// Split-KV flash-decoding attention over a Q4 cache (contiguous or paged), sm_100a.
+//
+// One CTA = (KV split "chunk", KV head, row group, sequence).  A row group is up to 8
+// query rows of one KV head (the n_rep GQA heads times the query positions), so every
+// Q4 byte of the chunk is read once for all of them.  4 warps per CTA; each warp streams
+// 16-token tiles (tiles w, w+4, ...) through a private cp.async ring of NS stages and
+// keeps its own online-softmax state; the 4 warp states are merged through shared
+// memory and either written as the final output (single chunk) or as a partial
+// (m, l, O) that combine_kernel merges across chunks.
+//
+// Tensor-core use (mma.sync m16n8k16, fp16 in / fp32 accumulate), HBM-bound design:
+//  * S = K . Q^T with K as the A operand (16 tokens x 16 dims) and the 8 query rows as N.
+//    4-bit codes become fp16 operands with one AND each: the nibble pattern masked into
+//    a half's mantissa is the subnormal code * 2^-24 (or code * 2^-20 for the next
+//    nibble), so no int->float conversion is needed.  The head-dim order inside each
+//    k-step is permuted to match the nibble order (the query fragments carry the same
+//    permutation and the 1/16 factor), and each k-step stays inside one 64-dim group so
+//    S = sum_g scale_g * (codes_g . q) + bias_g * sum(q_g) applies the group scale and
+//    bias to 16x8 results instead of to every element.
+//  * O^T = V^T . P with V codes as the A operand (dims x tokens, gathered with one
+//    byte-permute per token pair) and B = P * scale_v (fp16, transposed in registers with
+//    movmatrix); the bias term sum_t P * bias_v is accumulated in fp32 on the side.
+// The dequantized K/V never exist in memory; per 16 tokens a warp issues DK/16 + DV/16
+// MMAs and ~1 ALU op per Q4 element.
+//
+// Reference semantics followed: mlx_fused_attention.py:69-139 (scale q, q.k^T, mask,
+// softmax, P.V; GQA head h -> KV head h / n_rep) and the Metal decode kernel's online
+// softmax (mlx_fused_attention.py:320-361).  Accumulation is fp32 throughout.
+#include <cfloat>
+
+#include "am_common.cuh"
+#include "am_internal.h"
+
+namespace am {
+
+constexpr int kWarps = 4;
+constexpr int kTile = 16;
+constexpr float kMaskedFinite = -1.0e30f;  // boolean-mask fill (finite: keeps uniform rows)
+
+template <int DK, int DV, int NS>
+struct DecodeLayout {
+  static constexpr int NGK = DK / 64, NGV = DV / 64;
+  static constexpr int KW = DK / 8, VW = DV / 8;
+  // Row strides chosen so the fragment reads below are bank-conflict free.
+  static constexpr int SK = ((DK / 2) % 128 == 32 || (DK / 2) % 128 == 96) ? DK / 2 : DK / 2 + 32;
+  static constexpr int SV = DV / 2 + 16;
+  static constexpr int OFF_V = 16 * SK;
+  static constexpr int OFF_KS = OFF_V + 16 * SV;
+  static constexpr int OFF_KB = OFF_KS + 32 * NGK;
+  static constexpr int OFF_VS = OFF_KB + 32 * NGK;
+  static constexpr int OFF_VB = OFF_VS + 32 * NGV;
+  static constexpr int STAGE = OFF_VB + 32 * NGV;
+  static constexpr int RING = NS * STAGE + 16;  // + per-stage tile-valid words
+  static constexpr int SMEM = kWarps * RING;
+  static_assert(STAGE % 16 == 0, "stage must keep 16-byte alignment");
+  static_assert(8 * DK * 4 <= SMEM, "query staging must fit in the ring space");
+  static_assert(8 * (DV + 2) * 4 <= RING, "warp result must fit in its ring");
+};
+
+template <int NG>
+__device__ __forceinline__ void load_scales(const uint8_t* base, int tok, float (&out)[NG],
+                                            bool bf16) {
+  const uint16_t* p = reinterpret_cast<const uint16_t*>(base) + tok * NG;
+  if constexpr (NG % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < NG; i += 2) {
+      const uint32_t u = *reinterpret_cast<const uint32_t*>(p + i);
+      out[i] = h2f_rt(static_cast<uint16_t>(u & 0xffffu), bf16);
+      out[i + 1] = h2f_rt(static_cast<uint16_t>(u >> 16), bf16);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NG; ++i) out[i] = h2f_rt(p[i], bf16);
+  }
+}
+
+__device__ __forceinline__ float load_mask(const DecodeParams& p, int b, int hq, int l, int tok) {
+  const int64_t idx = (int64_t)b * p.msb + (int64_t)hq * p.msh + (int64_t)l * p.msl +
+                      (int64_t)tok * p.msn;
+  if (p.mask_kind == AM_MASK_BOOL) return static_cast<const uint8_t*>(p.mask)[idx] ? 1.0f : 0.0f;
+  if (p.mask_dtype == AM_DTYPE_F32) return static_cast<const float*>(p.mask)[idx];
+  return h2f_rt(static_cast<const uint16_t*>(p.mask)[idx], p.mask_dtype == AM_DTYPE_BF16);
+}
+
+template <int DK, int DV, bool SBF16, bool PAGED, int NS>
+__global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
+  using LY = DecodeLayout<DK, DV, NS>;
+  constexpr int NGK = LY::NGK, NGV = LY::NGV;
+  constexpr int KW = LY::KW, VW = LY::VW;
+  constexpr int SK = LY::SK, SV = LY::SV;
+  constexpr int KSTEPS = DK / 16;
+  constexpr int MT = DV / 16;
+
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int b = blockIdx.z;
+  const int row_groups = gridDim.y / p.hkv;
+  const int h = blockIdx.y / row_groups;
+  const int rg = blockIdx.y % row_groups;
+  const int chunk = blockIdx.x;
+
+  const int n = p.kv_len[b];
+  const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
+  const bool dense_mask = p.mask_kind != AM_MASK_NONE;
+  int lo, hi;
+  visible_range(n, st, p.q_len, p.window, dense_mask, lo, hi);
+  const int span = max(0, hi - lo);
+  const int n_chunks_b = max(1, (span + p.chunk - 1) / p.chunk);
+  if (chunk >= n_chunks_b) return;
+  const int c_lo = lo + chunk * p.chunk;
+  const int c_hi = min(c_lo + p.chunk, hi);
+  const int n_tiles = c_hi > c_lo ? (c_hi - c_lo + kTile - 1) / kTile : 0;
+
+  // ------------------------------------------------------------------ stage queries
+  float* qs = reinterpret_cast<float*>(smem);                      // [8][DK]
+  float* qsum_s = reinterpret_cast<float*>(smem + 8 * DK * 4);     // [8][NGK]
+  float* qmax_s = qsum_s + 8 * NGK;                                // [8][NGK]
+  // (qsum/qmax live just past the query block; the static_assert above guarantees space
+  // for the query block, and the ring is at least 2x larger for every instantiation.)
+  for (int i = tid; i < 8 * DK; i += 128) {
+    const int r = i / DK, d = i % DK;
+    const int rr = rg * 8 + r;
+    float v = 0.0f;
+    if (rr < p.rows_per_head) {
+      const int l = rr / p.n_rep;
+      const int hq = h * p.n_rep + rr % p.n_rep;
+      v = h2f_rt(p.q[(int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl + d],
+                 p.q_bf16 != 0);
+    }
+    qs[i] = v;
+  }
+  __syncthreads();
+  if (tid < 8 * NGK) {
+    const int r = tid / NGK, G = tid % NGK;
+    float s = 0.0f, m = 0.0f;
+    for (int d = 0; d < 64; ++d) {
+      const float v = qs[r * DK + G * 64 + d];
+      s += v;
+      m = fmaxf(m, fabsf(v));
+    }
+    qsum_s[tid] = s;
+    qmax_s[tid] = m;
+  }
+  __syncthreads();
+
+  // Per-row power-of-two prescale so fp16 MMA operands keep full precision (bf16 queries).
+  auto row_pow2 = [&](int r) -> float {
+    float m = 0.0f;
+#pragma unroll
+    for (int G = 0; G < NGK; ++G) m = fmaxf(m, qmax_s[r * NGK + G]);
+    if (!(m > 0.0f) || !isfinite(m)) return 1.0f;
+    int e;
+    frexpf(m, &e);  // m in [2^(e-1), 2^e)
+    return ldexpf(1.0f, 15 - e);
+  };
+
+  // B fragments of Q for S = K . Q^T (row g = CTA query row g).
+  uint32_t qf[KSTEPS][2];
+  {
+    const float pw = row_pow2(g);
+    const float* qr = qs + g * DK;
+#pragma unroll
+    for (int G = 0; G < NGK; ++G) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int s = 4 * G + 2 * j + e;
+          const int w = 8 * G + 2 * t + j;
+          const float* q8 = qr + 8 * w + 2 * e;
+          qf[s][0] = pack_half2(q8[0] * pw, q8[4] * pw);
+          qf[s][1] = pack_half2(q8[1] * pw * 0.0625f, q8[5] * pw * 0.0625f);
+        }
+      }
+    }
+  }
+  // Per-column (query row 2t, 2t+1) constants.
+  float fac[2], qb[2][NGK];
+  int pos_c[2], l_c[2], hq_c[2];
+  bool col_ok[2];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const int r = 2 * t + c;
+    const float pw = row_pow2(r);
+    fac[c] = 16777216.0f / pw * p.scale_log2;  // 2^24 undoes the subnormal code encoding
+#pragma unroll
+    for (int G = 0; G < NGK; ++G) qb[c][G] = qsum_s[r * NGK + G] * p.scale_log2;
+    const int rr = rg * 8 + r;
+    col_ok[c] = rr < p.rows_per_head;
+    const int rrc = col_ok[c] ? rr : p.rows_per_head - 1;
+    l_c[c] = rrc / p.n_rep;
+    hq_c[c] = h * p.n_rep + rrc % p.n_rep;
+    pos_c[c] = n - p.q_len + l_c[c];
+  }
+  int pos_min, pos_max;
+  {
+    const int r0 = rg * 8;
+    const int r1 = min(rg * 8 + 7, p.rows_per_head - 1);
+    pos_min = n - p.q_len + r0 / p.n_rep;
+    pos_max = n - p.q_len + r1 / p.n_rep;
+  }
+  __syncthreads();  // queries consumed: the ring may now overwrite the staging area
+
+  // ------------------------------------------------------------------ streaming loop
+  uint8_t* ring = smem + warp * LY::RING;
+  int32_t* tile_ok = reinterpret_cast<int32_t*>(ring + NS * LY::STAGE);
+  const int my_tiles = n_tiles > warp ? (n_tiles - warp + kWarps - 1) / kWarps : 0;
+
+  auto issue = [&](int k) {
+    if (k < my_tiles) {
+      const int t0 = c_lo + (warp + kWarps * k) * kTile;
+      uint8_t* stg = ring + (k % NS) * LY::STAGE;
+      int64_t row0;
+      bool ok = true;
+      if constexpr (PAGED) {
+        const int bi = t0 / p.block_tokens;
+        int32_t blk = bi < p.table_stride ? p.table[(int64_t)b * p.table_stride + bi] : -1;
+        if (blk < 0 || blk >= p.capacity) {
+          ok = false;
+          blk = 0;
+          if (lane == 0) flag_status(p.status, AM_STATUS_BAD_BLOCK);
+        }
+        row0 = ((int64_t)blk * p.hkv + h) * p.block_tokens + (t0 % p.block_tokens);
+      } else {
+        row0 = ((int64_t)b * p.hkv + h) * p.capacity + t0;
+      }
+      if (lane == 0) tile_ok[k % NS] = ok ? 1 : 0;
+      const uint32_t* kc = p.kc + row0 * KW;
+      const uint32_t* vc = p.vc + row0 * VW;
+#pragma unroll
+      for (int i = lane; i < 16 * (KW / 4); i += 32) {
+        const int r = i / (KW / 4), c = i % (KW / 4);
+        cp_async16(stg + r * SK + c * 16, kc + r * KW + c * 4);
+      }
+#pragma unroll
+      for (int i = lane; i < 16 * (VW / 4); i += 32) {
+        const int r = i / (VW / 4), c = i % (VW / 4);
+        cp_async16(stg + LY::OFF_V + r * SV + c * 16, vc + r * VW + c * 4);
+      }
+      // scales / biases: 16 rows x NG halves = 8*NG 4-byte granules each
+      const uint16_t* ks = p.ks + row0 * NGK;
+      const uint16_t* kb = p.kb + row0 * NGK;
+      const uint16_t* vs = p.vs + row0 * NGV;
+      const uint16_t* vb = p.vb + row0 * NGV;
+      constexpr int GK = 8 * NGK, GV = 8 * NGV;
+#pragma unroll
+      for (int i = lane; i < 2 * GK + 2 * GV; i += 32) {
+        if (i < GK) {
+          cp_async4(stg + LY::OFF_KS + i * 4, ks + i * 2);
+        } else if (i < 2 * GK) {
+          cp_async4(stg + LY::OFF_KB + (i - GK) * 4, kb + (i - GK) * 2);
+        } else if (i < 2 * GK + GV) {
+          cp_async4(stg + LY::OFF_VS + (i - 2 * GK) * 4, vs + (i - 2 * GK) * 2);
+        } else {
+          cp_async4(stg + LY::OFF_VB + (i - 2 * GK - GV) * 4, vb + (i - 2 * GK - GV) * 2);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+
+#pragma unroll
+  for (int k = 0; k < NS - 1; ++k) issue(k);
+
+  float o[MT][4];
+#pragma unroll
+  for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.0f, 0.0f};
+  float vbias[2][NGV];
+#pragma unroll
+  for (int G = 0; G < NGV; ++G) vbias[0][G] = vbias[1][G] = 0.0f;
+
+  for (int k = 0; k < my_tiles; ++k) {
+    cp_async_wait<NS - 2>();
+    __syncwarp();
+    const uint8_t* stg = ring + (k % NS) * LY::STAGE;
+    const int t0 = c_lo + (warp + kWarps * k) * kTile;
+    const bool ok = tile_ok[k % NS] != 0;
+    __syncwarp();
+    issue(k + NS - 1);
+
+    // ---- S = K . Q^T (per group accumulators) ----
+    float acc[NGK][4];
+#pragma unroll
+    for (int G = 0; G < NGK; ++G) {
+      acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.0f;
+      const uint2 wa = *reinterpret_cast<const uint2*>(stg + g * SK + G * 32 + t * 8);
+      const uint2 wb = *reinterpret_cast<const uint2*>(stg + (g + 8) * SK + G * 32 + t * 8);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t xa = j ? wa.y : wa.x;
+        uint32_t xb = j ? wb.y : wb.x;
+        const int s0 = 4 * G + 2 * j;
+        mma_f16_16816(acc[G], xa & 0x000F000Fu, xb & 0x000F000Fu, xa & 0x00F000F0u,
+                      xb & 0x00F000F0u, qf[s0][0], qf[s0][1]);
+        xa >>= 8;
+        xb >>= 8;
+        mma_f16_16816(acc[G], xa & 0x000F000Fu, xb & 0x000F000Fu, xa & 0x00F000F0u,
+                      xb & 0x00F000F0u, qf[s0 + 1][0], qf[s0 + 1][1]);
+      }
+    }
+    // scores in log2 units: element e -> token (e < 2 ? g : g + 8), column 2t + (e & 1)
+    float sk[2][NGK], bk[2][NGK];
+    load_scales<NGK>(stg + LY::OFF_KS, g, sk[0], SBF16);
+    load_scales<NGK>(stg + LY::OFF_KS, g + 8, sk[1], SBF16);
+    load_scales<NGK>(stg + LY::OFF_KB, g, bk[0], SBF16);
+    load_scales<NGK>(stg + LY::OFF_KB, g + 8, bk[1], SBF16);
+    float s2[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int tr = e >> 1, c = e & 1;
+      float x = 0.0f, y = 0.0f;
+#pragma unroll
+      for (int G = 0; G < NGK; ++G) {
+        x = fmaf(sk[tr][G], acc[G][e], x);
+        y = fmaf(bk[tr][G], qb[c][G], y);
+      }
+      s2[e] = fmaf(x, fac[c], y);
+    }
+    // ---- masking ----
+    const bool need_mask = !ok || t0 + kTile > n || t0 < st ||
+                           (p.causal && t0 + kTile - 1 > pos_min) ||
+                           (p.window > 0 && t0 <= pos_max - p.window) || dense_mask;
+    if (need_mask) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tok = t0 + g + 8 * (e >> 1);
+        const int c = e & 1;
+        bool keep = ok && tok < n && tok >= st;
+        if (p.causal && tok > pos_c[c]) keep = false;
+        if (p.window > 0 && tok <= pos_c[c] - p.window) keep = false;
+        float v = keep ? s2[e] : -INFINITY;
+        if (keep && dense_mask) {
+          const float mv = load_mask(p, b, hq_c[c], l_c[c], tok);
+          if (p.mask_kind == AM_MASK_BOOL) {
+            if (mv == 0.0f) v = kMaskedFinite;
+          } else {
+            v = fmaf(mv, 1.4426950408889634f, v);
+          }
+        }
+        s2[e] = v;
+      }
+    }
+    // ---- online softmax (per column) ----
+    float mt[2] = {fmaxf(s2[0], s2[2]), fmaxf(s2[1], s2[3])};
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      mt[c] = fmaxf(mt[c], __shfl_xor_sync(0xffffffffu, mt[c], 4));
+      mt[c] = fmaxf(mt[c], __shfl_xor_sync(0xffffffffu, mt[c], 8));
+      mt[c] = fmaxf(mt[c], __shfl_xor_sync(0xffffffffu, mt[c], 16));
+    }
+    const float mn0 = fmaxf(m_run[0], mt[0]), mn1 = fmaxf(m_run[1], mt[1]);
+    if (__any_sync(0xffffffffu, mn0 > m_run[0] || mn1 > m_run[1])) {
+      const float a0 = m_run[0] == -INFINITY ? 0.0f : ex2(m_run[0] - mn0);
+      const float a1 = m_run[1] == -INFINITY ? 0.0f : ex2(m_run[1] - mn1);
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+        o[i][0] *= a0;
+        o[i][2] *= a0;
+        o[i][1] *= a1;
+        o[i][3] *= a1;
+      }
+      l_run[0] *= a0;
+      l_run[1] *= a1;
+#pragma unroll
+      for (int G = 0; G < NGV; ++G) {
+        vbias[0][G] *= a0;
+        vbias[1][G] *= a1;
+      }
+      m_run[0] = mn0;
+      m_run[1] = mn1;
+    }
+    const float ms0 = m_run[0] == -INFINITY ? 0.0f : m_run[0];
+    const float ms1 = m_run[1] == -INFINITY ? 0.0f : m_run[1];
+    float pr[4];
+    pr[0] = ex2(s2[0] - ms0);
+    pr[1] = ex2(s2[1] - ms1);
+    pr[2] = ex2(s2[2] - ms0);
+    pr[3] = ex2(s2[3] - ms1);
+    l_run[0] += pr[0] + pr[2];
+    l_run[1] += pr[1] + pr[3];
+
+    // ---- O^T += V^T . (P * scale_v) ----
+    float sv[2][NGV], bv[2][NGV];
+    load_scales<NGV>(stg + LY::OFF_VS, g, sv[0], SBF16);
+    load_scales<NGV>(stg + LY::OFF_VS, g + 8, sv[1], SBF16);
+    load_scales<NGV>(stg + LY::OFF_VB, g, bv[0], SBF16);
+    load_scales<NGV>(stg + LY::OFF_VB, g + 8, bv[1], SBF16);
+    const uint8_t* vbase = stg + LY::OFF_V;
+#pragma unroll
+    for (int G = 0; G < NGV; ++G) {
+      vbias[0][G] = fmaf(pr[0], bv[0][G], fmaf(pr[2], bv[1][G], vbias[0][G]));
+      vbias[1][G] = fmaf(pr[1], bv[0][G], fmaf(pr[3], bv[1][G], vbias[1][G]));
+      const uint32_t blo = movmatrix_trans(pack_half2(pr[0] * sv[0][G], pr[1] * sv[0][G]));
+      const uint32_t bhi = movmatrix_trans(pack_half2(pr[2] * sv[1][G], pr[3] * sv[1][G]));
+      const int woff = (8 * G + g) * 4;
+      const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * SV + woff);
+      const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * SV + woff);
+      const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * SV + woff);
+      const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * SV + woff);
+#pragma unroll
+      for (int beta = 0; beta < 4; ++beta) {
+        const uint32_t sel = beta | ((4 + beta) << 8);
+        const uint32_t r01 = __byte_perm(v0, v1, sel);
+        const uint32_t r23 = __byte_perm(v2, v3, sel);
+        mma_f16_16816(o[4 * G + beta], r01 & 0x000F000Fu, r01 & 0x00F000F0u, r23 & 0x000F000Fu,
+                      r23 & 0x00F000F0u, blo, bhi);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncwarp();
+
+  // ------------------------------------------------------------------ warp reduction
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l_run[c] += __shfl_xor_sync(0xffffffffu, l_run[c], off);
+#pragma unroll
+      for (int G = 0; G < NGV; ++G) vbias[c][G] += __shfl_xor_sync(0xffffffffu, vbias[c][G], off);
+    }
+  }
+  // warp result into this warp's (now idle) ring: m[8], l[8], O[8][DV]
+  float* wres = reinterpret_cast<float*>(ring);
+  if (g == 0) {
+    wres[2 * t] = m_run[0];
+    wres[2 * t + 1] = m_run[1];
+    wres[8 + 2 * t] = l_run[0];
+    wres[8 + 2 * t + 1] = l_run[1];
+  }
+  float* wo = wres + 16;
+#pragma unroll
+  for (int mt_i = 0; mt_i < MT; ++mt_i) {
+    const int G = mt_i / 4, beta = mt_i % 4;
+    const int d = 64 * G + 8 * g + 2 * beta;
+    wo[(2 * t) * DV + d] = fmaf(o[mt_i][0], 16777216.0f, vbias[0][G]);
+    wo[(2 * t + 1) * DV + d] = fmaf(o[mt_i][1], 16777216.0f, vbias[1][G]);
+    wo[(2 * t) * DV + d + 1] = fmaf(o[mt_i][2], 1048576.0f, vbias[0][G]);
+    wo[(2 * t + 1) * DV + d + 1] = fmaf(o[mt_i][3], 1048576.0f, vbias[1][G]);
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------ CTA combine
+  const int rows_total = p.hq * p.q_len;
+  for (int i = tid; i < 8 * DV; i += 128) {
+    const int r = i / DV, d = i % DV;
+    const int rr = rg * 8 + r;
+    if (rr >= p.rows_per_head) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, reinterpret_cast<const float*>(smem + w * LY::RING)[r]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float* wr = reinterpret_cast<const float*>(smem + w * LY::RING);
+      const float mw = wr[r];
+      const float sc = (mw == -INFINITY) ? 0.0f : ex2(mw - M);
+      L = fmaf(wr[8 + r], sc, L);
+      O = fmaf(wr[16 + r * DV + d], sc, O);
+    }
+    const int l = rr / p.n_rep;
+    const int hq = h * p.n_rep + rr % p.n_rep;
+    if (n_chunks_b == 1) {
+      const float val = L > 0.0f ? O / L : 0.0f;
+      store_out(p.out, (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + d, val,
+                p.out_dtype);
+    } else {
+      float* slot = p.ws + (((int64_t)b * rows_total + (int64_t)hq * p.q_len + l) * p.max_chunks +
+                            chunk) * (DV + 2);
+      slot[2 + d] = O;
+      if (d == 0) {
+        slot[0] = M;
+        slot[1] = L;
+      }
+    }
+  }
+}
+
+// Merge the per-chunk partials of sequences split into more than one chunk.
+template <int DV>
+__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows_total = p.hq * p.q_len;
+  const int row = blockIdx.x * 4 + warp;
+  const int b = blockIdx.y;
+  if (row >= rows_total) return;
+  const int n = p.kv_len[b];
+  const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
+  int lo, hi;
+  visible_range(n, st, p.q_len, p.window, p.mask_kind != AM_MASK_NONE, lo, hi);
+  const int span = max(0, hi - lo);
+  const int nc = max(1, (span + p.chunk - 1) / p.chunk);
+  if (nc <= 1) return;
+  const float* base = p.ws + ((int64_t)b * rows_total + row) * p.max_chunks * (DV + 2);
+  float M = -INFINITY;
+  for (int c = lane; c < nc; c += 32) M = fmaxf(M, base[(int64_t)c * (DV + 2)]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float L = 0.0f;
+  for (int c = lane; c < nc; c += 32) {
+    const float mc = base[(int64_t)c * (DV + 2)];
+    if (mc != -INFINITY) L = fmaf(base[(int64_t)c * (DV + 2) + 1], ex2(mc - M), L);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  const int hq = row / p.q_len, l = row % p.q_len;
+  for (int d = lane; d < DV; d += 32) {
+    float O = 0.0f;
+    for (int c = 0; c < nc; ++c) {
+      const float mc = base[(int64_t)c * (DV + 2)];
+      if (mc != -INFINITY) O = fmaf(base[(int64_t)c * (DV + 2) + 2 + d], ex2(mc - M), O);
+    }
+    const float val = L > 0.0f ? O / L : 0.0f;
+    store_out(p.out, (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + d, val,
+              p.out_dtype);
+  }
+}
+
+// ---------------------------------------------------------------------- host side
+
+bool decode_supported(int k_dim, int v_dim) {
+  return (k_dim == 64 && v_dim == 64) || (k_dim == 128 && v_dim == 128) ||
+         (k_dim == 128 && v_dim == 64) || (k_dim == 192 && v_dim == 128) ||
+         (k_dim == 256 && v_dim == 256);
+}
+
+void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int* chunk, int* n_chunks) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    sms = 148;
+    (void)cudaGetLastError();  // clear: this query must not poison a later launch check
+  }
+  const int64_t pairs = (int64_t)batch * n_kv_heads * row_groups;
+  const int64_t target = (int64_t)sms * 6;
+  const int64_t n_split = pairs >= target ? 1 : (target + pairs - 1) / pairs;
+  const int64_t span16 = (int64_t)span + 15;
+  int64_t c = (span16 + n_split - 1) / n_split;
+  c = (c + 63) / 64 * 64;
+  if (c < 128) c = 128;
+  if (c > 2048) c = 2048;
+  *chunk = static_cast<int>(c);
+  *n_chunks = static_cast<int>(span16 > 0 ? (span16 + c - 1) / c : 1);
+  if (*n_chunks < 1) *n_chunks = 1;
+}
+
+template <int DK, int DV, bool SBF16, bool PAGED>
+static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_groups,
+                                   cudaStream_t stream) {
+  constexpr int NS = DK >= 256 ? 3 : 4;
+  using LY = DecodeLayout<DK, DV, NS>;
+  auto kfn = decode_kernel<DK, DV, SBF16, PAGED, NS>;
+  static bool attr_done = false;  // per instantiation; idempotent if raced
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  dim3 grid(p.max_chunks, p.hkv * row_groups, batch);
+  kfn<<<grid, 128, LY::SMEM, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (p.max_chunks > 1) {
+    const int rows_total = p.hq * p.q_len;
+    dim3 g2((rows_total + 3) / 4, batch);
+    combine_kernel<DV><<<g2, 128, 0, stream>>>(p);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+template <int DK, int DV>
+static cudaError_t launch_decode_dims(const DecodeParams& p, int batch, int row_groups, bool paged,
+                                      bool sbf16, cudaStream_t stream) {
+  if (paged) {
+    return sbf16 ? launch_decode_t<DK, DV, true, true>(p, batch, row_groups, stream)
+                 : launch_decode_t<DK, DV, false, true>(p, batch, row_groups, stream);
+  }
+  return sbf16 ? launch_decode_t<DK, DV, true, false>(p, batch, row_groups, stream)
+               : launch_decode_t<DK, DV, false, false>(p, batch, row_groups, stream);
+}
+
+cudaError_t launch_decode(const DecodeParams& p, int batch, int row_groups, bool paged,
+                          bool scale_bf16, cudaStream_t stream) {
+  const int dk = p.k_dim, dv = p.v_dim;
+  if (dk == 64 && dv == 64) return launch_decode_dims<64, 64>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 128 && dv == 128) return launch_decode_dims<128, 128>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 128 && dv == 64) return launch_decode_dims<128, 64>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 192 && dv == 128) return launch_decode_dims<192, 128>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 256 && dv == 256) return launch_decode_dims<256, 256>(p, batch, row_groups, paged, scale_bf16, stream);
+  return cudaErrorNotSupported;
+}
+
+}  // namespace am

@@ -1,0 +1,34 @@
+// Internal launcher declarations shared by the kernel files and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "am_q4.h"
+
+namespace am {
+
+struct AppendParams;
+struct DecodeParams;
+
+cudaError_t launch_quantize(const void* x, bool bf16, int64_t rows, int dim, uint32_t* codes,
+                            void* scales, void* biases, cudaStream_t stream);
+cudaError_t launch_dequantize(const uint32_t* codes, const void* scales, const void* biases,
+                              bool bf16, int64_t rows, int dim, void* out, int out_dtype,
+                              cudaStream_t stream);
+cudaError_t launch_append(const AppendParams& p, bool bf16, cudaStream_t stream);
+
+// Decode: returns cudaErrorNotSupported (without launching) for head dims without a kernel.
+bool decode_supported(int k_dim, int v_dim);
+cudaError_t launch_decode(const DecodeParams& p, int batch, int row_groups, bool paged,
+                          bool scale_bf16, cudaStream_t stream);
+
+bool prefill_supported(int k_dim, int v_dim);
+cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16,
+                           cudaStream_t stream);
+
+// Split size (tokens per CTA chunk) and number of chunks for a decode call.
+void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int* chunk, int* n_chunks);
+
+}  // namespace am

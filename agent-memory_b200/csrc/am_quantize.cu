@@ -1,0 +1,252 @@
+// Affine 4-bit quantization (group 64) on the GPU: plain quantize, dequantize, and the
+// fused quantize-on-append that scatters into a contiguous or paged Q4 cache.
+//
+// Quantization rule (mlx 0.30.3 affine quantizer, restated; the reference calls it at
+// src/agent_memory/adapters/outbound/mlx_quantized_extensions.py:273-274), per 64-element
+// group in fp32 with IEEE-rounded division:
+//   scale = max((max - min) / 15, 1e-7); the endpoint with the larger magnitude is the
+//   "edge" (scale negated when the edge is the max); q0 = rint(edge / scale); when q0 != 0
+//   the scale becomes edge / q0 and the bias the edge (zero is then exactly representable),
+//   otherwise bias = 0; code = clamp(rint((w - bias) / scale), 0, 15).
+// Scale and bias are stored in the input dtype; codes are packed 8 per uint32, LSB first.
+//
+// Work mapping: 8 lanes own one 64-element group (16-byte load each, one output word
+// each); a warp covers 4 groups.  Min/max are reduced with 3 xor-shuffles inside the
+// 8-lane team.  The kernels are HBM-bound: 128 B read + 36 B written per group (fp16).
+#include <cstdarg>
+#include <cstdio>
+
+#include "am_common.cuh"
+#include "am_internal.h"
+
+namespace am {
+
+template <bool BF16>
+__device__ __forceinline__ void load8(const uint16_t* src, float (&w)[8]) {
+  const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src));
+  const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    w[2 * i] = h2f<BF16>(static_cast<uint16_t>(u[i] & 0xffffu));
+    w[2 * i + 1] = h2f<BF16>(static_cast<uint16_t>(u[i] >> 16));
+  }
+}
+
+// Quantize the 64-element group spread over the 8 lanes of a team (8 values per lane).
+// Every lane of the warp must call this (shuffles use the full mask).
+__device__ __forceinline__ uint32_t quantize_team(const float (&w)[8], float& scale_out,
+                                                  float& bias_out) {
+  float mn = w[0], mx = w[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) {
+    mn = fminf(mn, w[i]);
+    mx = fmaxf(mx, w[i]);
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const bool side = fabsf(mn) > fabsf(mx);
+  float scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), 1e-7f);
+  scale = side ? scale : -scale;
+  const float edge = side ? mn : mx;
+  const float q0 = rintf(__fdiv_rn(edge, scale));
+  float bias = 0.0f;
+  if (q0 != 0.0f) {
+    scale = __fdiv_rn(edge, q0);
+    bias = edge;
+  }
+  uint32_t packed = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float c = rintf(__fdiv_rn(__fsub_rn(w[i], bias), scale));
+    c = fminf(fmaxf(c, 0.0f), 15.0f);
+    packed |= static_cast<uint32_t>(c) << (4 * i);
+  }
+  scale_out = scale;
+  bias_out = bias;
+  return packed;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const uint16_t* __restrict__ x,
+                                                            int64_t n_groups, int dim,
+                                                            uint32_t* __restrict__ codes,
+                                                            uint16_t* __restrict__ scales,
+                                                            uint16_t* __restrict__ biases) {
+  const int lane = threadIdx.x & 31;
+  const int team = lane >> 3, sub = lane & 7;
+  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int64_t wg = warp0; wg * 4 < n_groups; wg += warps_total) {
+    const int64_t gi = wg * 4 + team;
+    const bool active = gi < n_groups;
+    float w[8];
+    if (active) {
+      load8<BF16>(x + gi * kGroup + sub * 8, w);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = 0.0f;
+    }
+    float s, b;
+    const uint32_t packed = quantize_team(w, s, b);
+    if (active) {
+      codes[gi * 8 + sub] = packed;
+      if (sub == 0) {
+        scales[gi] = f2h<BF16>(s);
+        biases[gi] = f2h<BF16>(b);
+      }
+    }
+  }
+  (void)dim;
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restrict__ codes,
+                                                         const uint16_t* __restrict__ scales,
+                                                         const uint16_t* __restrict__ biases,
+                                                         int64_t n_words, void* __restrict__ out,
+                                                         int out_dtype) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_words;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t word = codes[i];
+    const int64_t grp = i >> 3;
+    const float s = h2f<BF16>(scales[grp]);
+    const float b = h2f<BF16>(biases[grp]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      store_out(out, i * 8 + k, fmaf(static_cast<float>((word >> (4 * k)) & 0xfu), s, b),
+                out_dtype);
+    }
+  }
+}
+
+// Quantize-on-append: groups are enumerated as [K groups of all (b,h,l)] then [V groups].
+template <bool BF16>
+__global__ void __launch_bounds__(256) append_kernel(AppendParams p) {
+  const int lane = threadIdx.x & 31;
+  const int team = lane >> 3, sub = lane & 7;
+  const int ngk = p.k_dim / kGroup, ngv = p.v_dim / kGroup;
+  const int64_t rows = (int64_t)p.batch * p.hkv * p.n_new;
+  const int64_t gk = rows * ngk;
+  const int64_t n_groups = gk + rows * ngv;
+  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int64_t wg = warp0; wg * 4 < n_groups; wg += warps_total) {
+    int64_t gi = wg * 4 + team;
+    bool active = gi < n_groups;
+    const bool is_v = gi >= gk;
+    const int ng = is_v ? ngv : ngk;
+    const int64_t gl = is_v ? gi - gk : gi;
+    const int64_t row = gl / ng;
+    const int g = static_cast<int>(gl % ng);
+    const int l = static_cast<int>(row % p.n_new);
+    const int h = static_cast<int>((row / p.n_new) % p.hkv);
+    const int b = static_cast<int>(row / ((int64_t)p.n_new * p.hkv));
+    float w[8];
+    if (active) {
+      const uint16_t* src = is_v ? p.v + b * p.vsb + h * p.vsh + l * p.vsl
+                                 : p.k + b * p.ksb + h * p.ksh + l * p.ksl;
+      load8<BF16>(src + g * kGroup + sub * 8, w);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = 0.0f;
+    }
+    float s, bias;
+    const uint32_t packed = quantize_team(w, s, bias);
+    if (!active) continue;
+    // destination row
+    const int64_t pos = (int64_t)p.positions[b] + l;
+    int64_t drow;
+    if (p.layout == AM_LAYOUT_PAGED) {
+      const int64_t bi = pos / p.block_tokens;
+      if (pos < 0 || bi >= p.table_stride) {
+        if (sub == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
+        continue;
+      }
+      const int32_t blk = p.table[(int64_t)b * p.table_stride + bi];
+      if (blk < 0 || blk >= p.capacity) {
+        if (sub == 0) flag_status(p.status, AM_STATUS_BAD_BLOCK);
+        continue;
+      }
+      drow = ((int64_t)blk * p.hkv + h) * p.block_tokens + pos % p.block_tokens;
+    } else {
+      if (pos < 0 || pos >= p.capacity) {
+        if (sub == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
+        continue;
+      }
+      drow = ((int64_t)b * p.hkv + h) * p.capacity + pos;
+    }
+    uint32_t* codes = is_v ? p.vc : p.kc;
+    uint16_t* scales = is_v ? p.vs : p.ks;
+    uint16_t* biases = is_v ? p.vb : p.kb;
+    codes[drow * (ng * 8) + g * 8 + sub] = packed;
+    if (sub == 0) {
+      scales[drow * ng + g] = f2h<BF16>(s);
+      biases[drow * ng + g] = f2h<BF16>(bias);
+    }
+  }
+}
+
+static int grid_for(int64_t warps_needed, int warps_per_block) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    sms = 148;
+    (void)cudaGetLastError();  // clear: this query must not poison a later launch check
+  }
+  const int64_t blocks = (warps_needed + warps_per_block - 1) / warps_per_block;
+  const int64_t cap = (int64_t)sms * 16;  // grid-stride beyond 16 blocks of 256 per SM
+  return static_cast<int>(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
+}
+
+cudaError_t launch_quantize(const void* x, bool bf16, int64_t rows, int dim, uint32_t* codes,
+                            void* scales, void* biases, cudaStream_t stream) {
+  const int64_t n_groups = rows * (dim / kGroup);
+  if (n_groups == 0) return cudaSuccess;
+  const int grid = grid_for((n_groups + 3) / 4, 8);
+  if (bf16) {
+    quantize_rows_kernel<true><<<grid, 256, 0, stream>>>(
+        static_cast<const uint16_t*>(x), n_groups, dim, codes, static_cast<uint16_t*>(scales),
+        static_cast<uint16_t*>(biases));
+  } else {
+    quantize_rows_kernel<false><<<grid, 256, 0, stream>>>(
+        static_cast<const uint16_t*>(x), n_groups, dim, codes, static_cast<uint16_t*>(scales),
+        static_cast<uint16_t*>(biases));
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(const uint32_t* codes, const void* scales, const void* biases,
+                              bool bf16, int64_t rows, int dim, void* out, int out_dtype,
+                              cudaStream_t stream) {
+  const int64_t n_words = rows * (dim / 8);
+  if (n_words == 0) return cudaSuccess;
+  const int grid = grid_for((n_words + 31) / 32, 8);
+  if (bf16) {
+    dequantize_kernel<true><<<grid, 256, 0, stream>>>(
+        codes, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
+        n_words, out, out_dtype);
+  } else {
+    dequantize_kernel<false><<<grid, 256, 0, stream>>>(
+        codes, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
+        n_words, out, out_dtype);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_append(const AppendParams& p, bool bf16, cudaStream_t stream) {
+  const int64_t rows = (int64_t)p.batch * p.hkv * p.n_new;
+  const int64_t n_groups = rows * (p.k_dim / kGroup + p.v_dim / kGroup);
+  if (n_groups == 0) return cudaSuccess;
+  const int grid = grid_for((n_groups + 3) / 4, 8);
+  if (bf16) {
+    append_kernel<true><<<grid, 256, 0, stream>>>(p);
+  } else {
+    append_kernel<false><<<grid, 256, 0, stream>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace am

@@ -1,0 +1,61 @@
+"""Test configuration: the `gpu` marker, package import, shared helpers.
+
+Tests marked ``gpu`` need a CUDA device (B200) and the built libamq4.so; everything else
+runs on the CPU.  The oracle under oracle/ is the checker in both kinds of tests.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+from __graft_entry__ import load_package  # noqa: E402
+
+pkg = load_package()
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and libamq4.so")
+
+
+@pytest.fixture(scope="session")
+def am():
+    return pkg
+
+
+@pytest.fixture(scope="session")
+def orc():
+    from oracle import q4_oracle
+
+    q4_oracle.build()
+    return q4_oracle
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def assert_close(got, want, atol=2e-3, rtol=1e-3, what=""):
+    """The attention tolerance: |got - want| <= atol + rtol * |want| elementwise."""
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    assert got.shape == want.shape, f"{what}: shape {got.shape} != {want.shape}"
+    err = np.abs(got - want)
+    bound = atol + rtol * np.abs(want)
+    bad = err > bound
+    if bad.any():
+        i = np.unravel_index(np.argmax(err - bound), err.shape)
+        raise AssertionError(f"{what}: {bad.sum()} of {err.size} elements out of tolerance; "
+                             f"max err {err.max():.3e} at {i}: got {got[i]} want {want[i]}")

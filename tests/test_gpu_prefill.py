@@ -1,0 +1,100 @@
+"""GPU parity of the tcgen05 chunked-prefill kernel against the CPU oracle.
+
+Tolerance: |gpu - oracle| <= 2e-3 + 1e-3 * |oracle| (fp32 output), fp32 accumulation in
+TMEM.  The chunk's own K/V are quantized into the cache before attention, as in the
+reference's chunked prefill (quantize-on-append precedes the attention call).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_close, pkg
+from test_gpu_decode import _bits, make_case, oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("qdtype", [torch.float16, torch.bfloat16])
+def test_prefill_llama_gqa(cuda, orc, qdtype):
+    """Llama-3.1-8B head geometry (32/8, D128), 512-token chunk over a cached prefix."""
+    B, Hq, Hkv, D, L, P = 2, 32, 8, 128, 512, 600
+    N = P + L
+    q, kq, vq = make_case(B, Hq, Hkv, N, D, D, L=L, dtype=qdtype, cuda=cuda, seed=41)
+    view, n = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q.to(cuda), D ** -0.5, kv_len, N, causal=True,
+                                out_dtype=torch.float32, mode="prefill")
+    want = oracle(orc, q, kq, vq, D ** -0.5, causal=True)
+    assert_close(got.cpu().numpy(), want, what=f"prefill {qdtype}")
+
+
+def test_prefill_through_dropin_op(cuda, orc):
+    """The drop-in op routes L=64 with the causal string to the prefill kernel."""
+    q, kq, vq = make_case(1, 8, 8, 300, 128, 128, L=64, cuda=cuda, seed=3)
+    got = pkg.quantized_scaled_dot_product_attention(q.to(cuda), kq, vq, 0.08, "causal")
+    want = oracle(orc, q, kq, vq, 0.08, causal=True)
+    assert_close(got.float().cpu().numpy(), want, atol=3e-3, rtol=2e-3, what="drop-in prefill")
+
+
+def test_prefill_d64_mha_window_leftpad(cuda, orc):
+    B, H, D, L, N = 3, 4, 64, 200, 700
+    q, kq, vq = make_case(B, H, H, N, D, D, L=L, cuda=cuda, seed=8)
+    lp = torch.tensor([0, 5, 301])
+    view, _ = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q.to(cuda), 0.125, kv_len, N, causal=True, window=128,
+                                kv_start=lp.to(cuda), out_dtype=torch.float32, mode="prefill")
+    want = oracle(orc, q, kq, vq, 0.125, causal=True, window=128, kv_start=lp.numpy())
+    assert_close(got.cpu().numpy(), want, what="prefill window+leftpad")
+
+
+def test_prefill_dense_masks(cuda, orc):
+    B, H, D, L, N = 1, 4, 128, 130, 260
+    q, kq, vq = make_case(B, H, 2, N, D, D, L=L, cuda=cuda, seed=10)
+    g = torch.Generator().manual_seed(0)
+    keep = torch.rand(B, 1, L, N, generator=g) > 0.2
+    view, _ = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q.to(cuda), 0.1, kv_len, N, mask=keep.to(cuda),
+                                out_dtype=torch.float32, mode="prefill")
+    want = oracle(orc, q, kq, vq, 0.1, causal=False, mask=keep.numpy(), mask_kind=1)
+    assert_close(got.cpu().numpy(), want, what="prefill bool mask")
+
+
+def test_prefill_matches_decode_kernel(cuda):
+    """Both kernels agree on a 16-query block (the dispatch boundary)."""
+    q, kq, vq = make_case(2, 4, 1, 900, 128, 128, L=16, cuda=cuda, seed=12)
+    view, N = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((2,), N, dtype=torch.int32, device=cuda)
+    a = pkg.kernels.attention(view, q.to(cuda), 0.09, kv_len, N, causal=True,
+                              out_dtype=torch.float32, mode="prefill")
+    b = pkg.kernels.attention(view, q.to(cuda), 0.09, kv_len, N, causal=True,
+                              out_dtype=torch.float32, mode="decode")
+    assert torch.allclose(a, b, atol=2e-3, rtol=1e-3), (a - b).abs().max()
+
+
+def test_chunked_prefill_paged(cuda, orc):
+    """Config-4 flow at reduced size on the paged pool: append the chunk's K/V into
+    256-token blocks, then attend the chunk over prefix + chunk."""
+    A, Hq, Hkv, D, bt = 2, 32, 8, 128, 256
+    P, L = 700, 300
+    spec = pkg.ModelCacheSpec(n_layers=1, n_kv_heads=Hkv, head_dim=D, block_tokens=bt,
+                              layer_types=["global"])
+    alloc = pkg.shuffled_allocator(spec, 32, seed=1)
+    pool = pkg.PagedQ4Pool.for_spec(spec, 32, torch.bfloat16, cuda)
+    layer = pkg.PagedLayerCache(pool, alloc, 0, ["a0", "a1"], P + L)
+    g = torch.Generator().manual_seed(2)
+    kp = torch.randn(A, Hkv, P, D, generator=g).bfloat16()
+    vp = torch.randn(A, Hkv, P, D, generator=g).bfloat16()
+    layer.append(kp.to(cuda), vp.to(cuda))
+    kc = torch.randn(A, Hkv, L, D, generator=g).bfloat16()
+    vc = torch.randn(A, Hkv, L, D, generator=g).bfloat16()
+    layer.append(kc.to(cuda), vc.to(cuda))
+    q = torch.randn(A, Hq, L, D, generator=g).bfloat16()
+    got = layer.attention(q.to(cuda), D ** -0.5, mode="prefill")
+    table = layer._table_host.numpy()
+    want = orc.attention(q.float().numpy(), tuple(_bits(t) for t in pool.k),
+                         tuple(_bits(t) for t in pool.v), D ** -0.5, sdtype=1, n_kv_heads=Hkv,
+                         layout=1, block_table=table, kv_len=np.array(layer.lengths), causal=True)
+    assert_close(got.float().cpu().numpy(), want, atol=4e-3, rtol=4e-3, what="paged chunked prefill")
