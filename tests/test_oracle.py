@@ -171,5 +171,53 @@ def test_golden_fixture(orc, name):
         got = orc.attention(f["q"], kq, vq, float(f["scale"]), sdtype=int(f["sdtype"]),
                             causal=bool(f["causal"]), window=int(f["window"]), kv_start=kvs)
         np.testing.assert_allclose(got, f["out"], atol=1e-5, rtol=1e-5)
+    elif kind == "ref_sdpa":
+        # output of the reference's own patched quantized SDPA (mlx_fused_attention.py), run
+        # over the NumPy mlx stand-in: its fp16 intermediates stay within the attention
+        # tolerance of the fp32 oracle, which pins the oracle's mask / GQA / op-order rules
+        q = f["q"].view(np.float16).astype(np.float32)
+        kq = (f["kc"], f["ks"], f["kb"])
+        vq = (f["vc"], f["vs"], f["vb"])
+        mask, mk, causal = None, 0, False
+        if "mask_str" in f.files:
+            causal = True
+        elif "mask" in f.files:
+            mask = f["mask"]
+            mk = 1 if mask.dtype == bool else 2
+            mask = mask.astype(np.float32)
+        got = orc.attention(q, kq, vq, float(f["scale"]), causal=causal, mask=mask, mask_kind=mk)
+        ref = f["out"].view(np.float16).astype(np.float32)
+        assert np.all(np.abs(got - ref) <= 2e-3 + 1e-3 * np.abs(ref))
+    elif kind == "cache_lifecycle":
+        # the recorded inputs re-quantized by the oracle reproduce the reference cache's
+        # packed codes (the cache bookkeeping itself is replayed on the GPU)
+        meta = __import__("json").loads(str(f["meta"]))
+        assert [m["tag"] for m in meta][:3] == ["merge", "update1", "update2"]
+        c1 = orc.quantize(f["in_c1_k"], orc.F16)
+        np.testing.assert_array_equal(f["merge_kc"][0, :, meta[0]["left_padding"][0]:], c1[0][0])
     else:
-        pytest.skip(f"fixture kind {kind} is checked elsewhere")
+        pytest.fail(f"unknown fixture kind {kind}")
+
+
+def test_block_pool_replays_reference(am):
+    """tests/golden/ref_block_pool.json: the reference's BlockPool on a fixed op sequence."""
+    import json
+
+    log = json.loads((GOLDEN / "ref_block_pool.json").read_text())
+    spec = am.ModelCacheSpec(n_layers=4, n_kv_heads=8, head_dim=128, block_tokens=256,
+                             layer_types=["global"] * 4)
+    pool = am.BlockPool(spec, 32)
+    held = {}
+    for op in log:
+        if op[0] == "alloc":
+            got = pool.allocate(len(op[3]), op[2], op[1])
+            assert [b.block_id for b in got] == op[3]
+            held.setdefault(op[1], []).extend(got)
+        elif op[0] == "free":
+            blocks = [b for b in held[op[1]] if b.block_id in op[2]]
+            pool.free(blocks, op[1])
+        elif op[0] == "free_agent":
+            assert pool.free_agent_blocks(op[1]) == op[2]
+        elif op[0] == "state":
+            assert [pool.available_blocks(), pool.allocated_block_count(), pool.used_memory(),
+                    pool.max_batch_size(600)] == op[1:]
