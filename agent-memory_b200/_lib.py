@@ -39,7 +39,9 @@ EXPORTED_SYMBOLS = (
     "am_q4_decode",
     "am_q4_prefill",
     "am_q4_attention",
+    "am_q4_decode_noalloc",
 )
+STATIC_DECODE_SCRATCH_BYTES = 16 << 20
 
 c_void_p, c_int32, c_int64, c_float, c_size_t = (ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                                  ctypes.c_float, ctypes.c_size_t)
@@ -156,6 +158,9 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         f.restype = c_int32
     lib.am_q4_prefill.argtypes = [ctypes.POINTER(Q4CacheDesc), ctypes.POINTER(AttnArgs), c_void_p]
     lib.am_q4_prefill.restype = c_int32
+    lib.am_q4_decode_noalloc.argtypes = [ctypes.POINTER(Q4CacheDesc), ctypes.POINTER(AttnArgs),
+                                         c_void_p]
+    lib.am_q4_decode_noalloc.restype = c_int32
     ver = lib.am_abi_version()
     if ver != ABI_VERSION:
         raise Q4KernelUnavailable(f"{p} has ABI version {ver}, expected {ABI_VERSION}")

@@ -160,6 +160,19 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* args, void* works
                  size_t workspace_bytes, void* stream);
 
 /*
+ * Split-KV decode for callers that cannot allocate device memory (no counterpart in the
+ * reference, whose attention path never takes a caller-provided workspace).  Same
+ * arguments, checks and results as am_q4_decode, but the per-split scratch comes from one
+ * array of AM_STATIC_DECODE_SCRATCH_BYTES compiled into the library and held on every GPU
+ * that loads it until exit; calls needing more scratch return AM_ERR_WORKSPACE.  Nothing
+ * is allocated.  All calls share that scratch: calls that overlap on the GPU race and must
+ * be serialized by the caller.  The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress) with that device current; make it before any stream capture.
+ */
+#define AM_STATIC_DECODE_SCRATCH_BYTES (16u << 20)
+int am_q4_decode_noalloc(const am_q4_cache* cache, const am_attn_args* args, void* stream);
+
+/*
  * Chunked prefill attention on tcgen05 tensor cores (replaces the L>1 compiled path of
  * _fused_q4_sdpa, mlx_fused_attention.py:144-207, as driven by chunked prefill,
  * batch_engine.py:339-456).  Requires k_dim == v_dim in {64, 128}.
