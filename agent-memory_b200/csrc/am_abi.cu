@@ -156,6 +156,8 @@ static void fill_params(DecodeParams& p, const am_q4_cache* cache, const am_attn
   p.table = cache->block_table;
   p.table_stride = cache->block_table_stride;
   p.block_tokens = cache->block_tokens;
+  p.bt_shift = 0;
+  while (cache->block_tokens > 0 && (1 << p.bt_shift) < cache->block_tokens) ++p.bt_shift;
   p.hkv = cache->n_kv_heads;
   p.k_dim = cache->k_dim;
   p.v_dim = cache->v_dim;
@@ -311,6 +313,17 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
   if (!decode_supported(cache->k_dim, cache->v_dim)) {
     set_error("am_q4_decode: no kernel for k_dim=%d v_dim=%d", cache->k_dim, cache->v_dim);
     return AM_ERR_UNSUPPORTED;
+  }
+  if (cache->layout == AM_LAYOUT_PAGED &&
+      (cache->block_tokens < 32 || (cache->block_tokens & (cache->block_tokens - 1)))) {
+    set_error("am_q4_decode: paged decode needs block_tokens to be a power of two >= 32 (got %d)",
+              cache->block_tokens);
+    return AM_ERR_UNSUPPORTED;
+  }
+  if (!aligned(cache->k_scales, 16) || !aligned(cache->k_biases, 16) ||
+      !aligned(cache->v_scales, 16) || !aligned(cache->v_biases, 16)) {
+    set_error("am_q4_decode: scales and biases must be 16-byte aligned (bulk copies)");
+    return AM_ERR_INVALID;
   }
   const int n_rep = a->n_q_heads / cache->n_kv_heads;
   if (n_rep * a->q_len > 64) {

@@ -100,6 +100,65 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// ---------------------------------------------------------------- mbarrier / bulk copy
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// 1-D bulk copy global -> shared (TMA engine, no multicast); completes `bytes` on `bar`.
+// dst/src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+
+// Wait for phase `parity` of an mbarrier; gives up after `limit_ns` (returns false).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  uint64_t limit_ns = 2000000000ull) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (it == 0) {
+      t0 = globaltimer_ns();
+    } else if ((it & 63) == 0 && globaltimer_ns() - t0 > limit_ns) {
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void flag_status(int32_t* status, int bits) {
   if (status != nullptr) atomicOr(status, bits);
 }
@@ -142,6 +201,7 @@ struct DecodeParams {
   const int32_t* table;
   int32_t table_stride;
   int32_t block_tokens;
+  int32_t bt_shift;  // log2(block_tokens) for paged decode
   int32_t hkv;
   int32_t k_dim;
   int32_t v_dim;
@@ -171,7 +231,7 @@ struct DecodeParams {
 };
 
 // Visible key range of a sequence for the structured mask: keys outside [lo, hi) are
-// excluded for every query row.  lo is rounded down to a multiple of 16 (tile size).
+// excluded for every query row.  lo is rounded down to a multiple of 32 (stage size).
 __device__ __forceinline__ void visible_range(int n, int st, int q_len, int window, bool dense_mask,
                                               int& lo, int& hi) {
   hi = n;
@@ -182,7 +242,7 @@ __device__ __forceinline__ void visible_range(int n, int st, int q_len, int wind
     if (window > 0) lo = max(lo, n - q_len - window + 1);
     lo = max(lo, 0);
   }
-  lo &= ~15;
+  lo &= ~31;  // 32-token pipeline stages start on 32-token boundaries
 }
 
 }  // namespace am

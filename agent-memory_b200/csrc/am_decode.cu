@@ -34,26 +34,30 @@
 namespace am {
 
 constexpr int kWarps = 4;
-constexpr int kTile = 16;
+constexpr int kStage = 32;                 // tokens per pipeline stage (two 16-token MMA tiles)
+constexpr int kMaxChunk = 2048;            // tokens per CTA chunk (decode_plan never exceeds it)
+constexpr int kMaxBlk = kMaxChunk / 32 + 2;  // block ids a chunk can touch (block_tokens >= 32)
 constexpr float kMaskedFinite = -1.0e30f;  // boolean-mask fill (finite: keeps uniform rows)
 
 template <int DK, int DV, int NS>
 struct DecodeLayout {
   static constexpr int NGK = DK / 64, NGV = DV / 64;
   static constexpr int KW = DK / 8, VW = DV / 8;
-  // Row strides chosen so the fragment reads below are bank-conflict free.
-  static constexpr int SK = ((DK / 2) % 128 == 32 || (DK / 2) % 128 == 96) ? DK / 2 : DK / 2 + 32;
-  static constexpr int SV = DV / 2 + 16;
-  static constexpr int OFF_V = 16 * SK;
-  static constexpr int OFF_KS = OFF_V + 16 * SV;
-  static constexpr int OFF_KB = OFF_KS + 32 * NGK;
-  static constexpr int OFF_VS = OFF_KB + 32 * NGK;
-  static constexpr int OFF_VB = OFF_VS + 32 * NGV;
-  static constexpr int STAGE = OFF_VB + 32 * NGV;
-  static constexpr int RING = NS * STAGE + 16;  // + per-stage tile-valid words
-  static constexpr int SMEM = kWarps * RING;
-  static_assert(STAGE % 16 == 0, "stage must keep 16-byte alignment");
-  static_assert(8 * DK * 4 <= SMEM, "query staging must fit in the ring space");
+  static constexpr int KROW = DK / 2, VROW = DV / 2;  // bytes of codes per token row
+  // one stage: codes and scales of kStage rows, exactly as laid out in global memory
+  static constexpr int OFF_V = kStage * KROW;
+  static constexpr int OFF_KS = OFF_V + kStage * VROW;
+  static constexpr int OFF_KB = OFF_KS + kStage * NGK * 2;
+  static constexpr int OFF_VS = OFF_KB + kStage * NGK * 2;
+  static constexpr int OFF_VB = OFF_VS + kStage * NGV * 2;
+  static constexpr int STAGE = (OFF_VB + kStage * NGV * 2 + 127) / 128 * 128;
+  static constexpr int RING = NS * STAGE;
+  static constexpr int OFF_BAR = kWarps * RING;
+  static constexpr int OFF_OK = OFF_BAR + kWarps * NS * 8;
+  static constexpr int OFF_Q = (OFF_OK + kWarps * NS * 4 + 15) / 16 * 16;
+  static constexpr int OFF_QS = OFF_Q + 8 * DK * 4;
+  static constexpr int OFF_BLK = OFF_QS + 2 * 8 * NGK * 4;
+  static constexpr int SMEM = OFF_BLK + kMaxBlk * 4;
   static_assert(8 * (DV + 2) * 4 <= RING, "warp result must fit in its ring");
 };
 
@@ -87,7 +91,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   using LY = DecodeLayout<DK, DV, NS>;
   constexpr int NGK = LY::NGK, NGV = LY::NGV;
   constexpr int KW = LY::KW, VW = LY::VW;
-  constexpr int SK = LY::SK, SV = LY::SV;
+  constexpr int KROW = LY::KROW, VROW = LY::VROW;
   constexpr int KSTEPS = DK / 16;
   constexpr int MT = DV / 16;
 
@@ -112,37 +116,111 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   if (chunk >= n_chunks_b) return;
   const int c_lo = lo + chunk * p.chunk;
   const int c_hi = min(c_lo + p.chunk, hi);
-  const int n_tiles = c_hi > c_lo ? (c_hi - c_lo + kTile - 1) / kTile : 0;
+  const int n_stages = c_hi > c_lo ? (c_hi - c_lo + kStage - 1) / kStage : 0;
+  const int my_stages = n_stages > warp ? (n_stages - warp + kWarps - 1) / kWarps : 0;
+
+  uint8_t* ring = smem + warp * LY::RING;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR) + warp * NS;
+  int32_t* tile_ok = reinterpret_cast<int32_t*>(smem + LY::OFF_OK) + warp * NS;
+  int32_t* sblk = reinterpret_cast<int32_t*>(smem + LY::OFF_BLK);
+
+  // ------------------------------------------------------------------ barriers, block ids
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    fence_mbar_init();
+  }
+  int blk0 = 0;
+  if constexpr (PAGED) {
+    blk0 = c_lo >> p.bt_shift;
+    const int nblk = c_hi > c_lo ? ((c_hi - 1) >> p.bt_shift) - blk0 + 1 : 0;
+    for (int i = tid; i < nblk; i += 128) {
+      const int bi = blk0 + i;
+      int32_t v = bi < p.table_stride ? p.table[(int64_t)b * p.table_stride + bi] : -1;
+      if (v < 0 || v >= p.capacity) {
+        flag_status(p.status, AM_STATUS_BAD_BLOCK);
+        v = -1;
+      }
+      sblk[i] = v;
+    }
+  }
+  __syncthreads();
+
+  // Lane 0 of each warp fills its ring: one stage = kStage rows of K/V codes and scales,
+  // six 1-D bulk copies completing on the stage's mbarrier.
+  auto issue = [&](int k) {
+    if (k >= my_stages) return;
+    const int s = k % NS;
+    const int t0 = c_lo + (warp + kWarps * k) * kStage;
+    int64_t row0;
+    int nrows;
+    bool ok = true;
+    if constexpr (PAGED) {
+      const int32_t v = sblk[(t0 >> p.bt_shift) - blk0];
+      ok = v >= 0;
+      row0 = ((((int64_t)(ok ? v : 0)) * p.hkv + h) << p.bt_shift) + (t0 & (p.block_tokens - 1));
+      nrows = kStage;
+    } else {
+      row0 = ((int64_t)b * p.hkv + h) * p.capacity + t0;
+      nrows = min((int64_t)kStage, p.capacity - t0) >= kStage ? kStage : 16;
+    }
+    tile_ok[s] = ok ? 1 : 0;
+    const uint32_t bar = smem_u32(&bars[s]);
+    if (!ok) {
+      mbar_arrive(bar);
+      return;
+    }
+    const uint32_t bytes = nrows * (KROW + VROW + 4 * NGK + 4 * NGV);
+    mbar_arrive_expect_tx(bar, bytes);
+    uint8_t* stg = ring + s * LY::STAGE;
+    bulk_g2s(stg, p.kc + row0 * KW, nrows * KROW, bar);
+    bulk_g2s(stg + LY::OFF_V, p.vc + row0 * VW, nrows * VROW, bar);
+    bulk_g2s(stg + LY::OFF_KS, p.ks + row0 * NGK, nrows * NGK * 2, bar);
+    bulk_g2s(stg + LY::OFF_KB, p.kb + row0 * NGK, nrows * NGK * 2, bar);
+    bulk_g2s(stg + LY::OFF_VS, p.vs + row0 * NGV, nrows * NGV * 2, bar);
+    bulk_g2s(stg + LY::OFF_VB, p.vb + row0 * NGV, nrows * NGV * 2, bar);
+  };
+  if (lane == 0) {
+#pragma unroll
+    for (int k = 0; k < NS - 1; ++k) issue(k);
+  }
 
   // ------------------------------------------------------------------ stage queries
-  float* qs = reinterpret_cast<float*>(smem);                      // [8][DK]
-  float* qsum_s = reinterpret_cast<float*>(smem + 8 * DK * 4);     // [8][NGK]
-  float* qmax_s = qsum_s + 8 * NGK;                                // [8][NGK]
-  // (qsum/qmax live just past the query block; the static_assert above guarantees space
-  // for the query block, and the ring is at least 2x larger for every instantiation.)
-  for (int i = tid; i < 8 * DK; i += 128) {
-    const int r = i / DK, d = i % DK;
+  float* qs = reinterpret_cast<float*>(smem + LY::OFF_Q);    // [8][DK]
+  float* qsum_s = reinterpret_cast<float*>(smem + LY::OFF_QS);  // [8][NGK]
+  float* qmax_s = qsum_s + 8 * NGK;                            // [8][NGK]
+  for (int i = tid; i < 8 * (DK / 8); i += 128) {
+    const int r = i / (DK / 8), c8 = i % (DK / 8);
     const int rr = rg * 8 + r;
-    float v = 0.0f;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.0f;
     if (rr < p.rows_per_head) {
       const int l = rr / p.n_rep;
       const int hq = h * p.n_rep + rr % p.n_rep;
-      v = h2f_rt(p.q[(int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl + d],
-                 p.q_bf16 != 0);
+      const uint16_t* src = p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl + c8 * 8;
+      const uint4 raw = *reinterpret_cast<const uint4*>(src);
+      const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[2 * e] = h2f_rt(static_cast<uint16_t>(u[e] & 0xffffu), p.q_bf16 != 0);
+        v[2 * e + 1] = h2f_rt(static_cast<uint16_t>(u[e] >> 16), p.q_bf16 != 0);
+      }
     }
-    qs[i] = v;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qs[r * DK + c8 * 8 + e] = v[e];
   }
   __syncthreads();
   if (tid < 8 * NGK) {
     const int r = tid / NGK, G = tid % NGK;
-    float s = 0.0f, m = 0.0f;
+    float sm = 0.0f, mx = 0.0f;
     for (int d = 0; d < 64; ++d) {
       const float v = qs[r * DK + G * 64 + d];
-      s += v;
-      m = fmaxf(m, fabsf(v));
+      sm += v;
+      mx = fmaxf(mx, fabsf(v));
     }
-    qsum_s[tid] = s;
-    qmax_s[tid] = m;
+    qsum_s[tid] = sm;
+    qmax_s[tid] = mx;
   }
   __syncthreads();
 
@@ -157,7 +235,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     return ldexpf(1.0f, 15 - e);
   };
 
-  // B fragments of Q for S = K . Q^T (row g = CTA query row g).
+  // B fragments of Q for S = K . Q^T (row g = CTA query row g).  k-step s = 4G + 2j + e
+  // covers words 8G + 2t + j of this thread's column t; nibbles (2e, 2e+4) feed k-slots
+  // 2t, 2t+1 and nibbles (2e+1, 2e+5) feed 2t+8, 2t+9 (pre-divided by 16).
   uint32_t qf[KSTEPS][2];
   {
     const float pw = row_pow2(g);
@@ -180,7 +260,6 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   // Per-column (query row 2t, 2t+1) constants.
   float fac[2], qb[2][NGK];
   int pos_c[2], l_c[2], hq_c[2];
-  bool col_ok[2];
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const int r = 2 * t + c;
@@ -189,82 +268,22 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
 #pragma unroll
     for (int G = 0; G < NGK; ++G) qb[c][G] = qsum_s[r * NGK + G] * p.scale_log2;
     const int rr = rg * 8 + r;
-    col_ok[c] = rr < p.rows_per_head;
-    const int rrc = col_ok[c] ? rr : p.rows_per_head - 1;
+    const int rrc = rr < p.rows_per_head ? rr : p.rows_per_head - 1;
     l_c[c] = rrc / p.n_rep;
     hq_c[c] = h * p.n_rep + rrc % p.n_rep;
     pos_c[c] = n - p.q_len + l_c[c];
   }
-  int pos_min, pos_max;
+  // Stages entirely inside [mask_lo, mask_hi) need no per-element masking.
+  int mask_lo, mask_hi;
   {
-    const int r0 = rg * 8;
     const int r1 = min(rg * 8 + 7, p.rows_per_head - 1);
-    pos_min = n - p.q_len + r0 / p.n_rep;
-    pos_max = n - p.q_len + r1 / p.n_rep;
+    const int pos_min = n - p.q_len + (rg * 8) / p.n_rep;
+    const int pos_max = n - p.q_len + r1 / p.n_rep;
+    mask_lo = max(st, p.window > 0 ? pos_max - p.window + 1 : 0);
+    mask_hi = p.causal ? min(n, pos_min + 1) : n;
   }
-  __syncthreads();  // queries consumed: the ring may now overwrite the staging area
 
   // ------------------------------------------------------------------ streaming loop
-  uint8_t* ring = smem + warp * LY::RING;
-  int32_t* tile_ok = reinterpret_cast<int32_t*>(ring + NS * LY::STAGE);
-  const int my_tiles = n_tiles > warp ? (n_tiles - warp + kWarps - 1) / kWarps : 0;
-
-  auto issue = [&](int k) {
-    if (k < my_tiles) {
-      const int t0 = c_lo + (warp + kWarps * k) * kTile;
-      uint8_t* stg = ring + (k % NS) * LY::STAGE;
-      int64_t row0;
-      bool ok = true;
-      if constexpr (PAGED) {
-        const int bi = t0 / p.block_tokens;
-        int32_t blk = bi < p.table_stride ? p.table[(int64_t)b * p.table_stride + bi] : -1;
-        if (blk < 0 || blk >= p.capacity) {
-          ok = false;
-          blk = 0;
-          if (lane == 0) flag_status(p.status, AM_STATUS_BAD_BLOCK);
-        }
-        row0 = ((int64_t)blk * p.hkv + h) * p.block_tokens + (t0 % p.block_tokens);
-      } else {
-        row0 = ((int64_t)b * p.hkv + h) * p.capacity + t0;
-      }
-      if (lane == 0) tile_ok[k % NS] = ok ? 1 : 0;
-      const uint32_t* kc = p.kc + row0 * KW;
-      const uint32_t* vc = p.vc + row0 * VW;
-#pragma unroll
-      for (int i = lane; i < 16 * (KW / 4); i += 32) {
-        const int r = i / (KW / 4), c = i % (KW / 4);
-        cp_async16(stg + r * SK + c * 16, kc + r * KW + c * 4);
-      }
-#pragma unroll
-      for (int i = lane; i < 16 * (VW / 4); i += 32) {
-        const int r = i / (VW / 4), c = i % (VW / 4);
-        cp_async16(stg + LY::OFF_V + r * SV + c * 16, vc + r * VW + c * 4);
-      }
-      // scales / biases: 16 rows x NG halves = 8*NG 4-byte granules each
-      const uint16_t* ks = p.ks + row0 * NGK;
-      const uint16_t* kb = p.kb + row0 * NGK;
-      const uint16_t* vs = p.vs + row0 * NGV;
-      const uint16_t* vb = p.vb + row0 * NGV;
-      constexpr int GK = 8 * NGK, GV = 8 * NGV;
-#pragma unroll
-      for (int i = lane; i < 2 * GK + 2 * GV; i += 32) {
-        if (i < GK) {
-          cp_async4(stg + LY::OFF_KS + i * 4, ks + i * 2);
-        } else if (i < 2 * GK) {
-          cp_async4(stg + LY::OFF_KB + (i - GK) * 4, kb + (i - GK) * 2);
-        } else if (i < 2 * GK + GV) {
-          cp_async4(stg + LY::OFF_VS + (i - 2 * GK) * 4, vs + (i - 2 * GK) * 2);
-        } else {
-          cp_async4(stg + LY::OFF_VB + (i - 2 * GK - GV) * 4, vb + (i - 2 * GK - GV) * 2);
-        }
-      }
-    }
-    cp_async_commit();
-  };
-
-#pragma unroll
-  for (int k = 0; k < NS - 1; ++k) issue(k);
-
   float o[MT][4];
 #pragma unroll
   for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
@@ -273,80 +292,110 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   float vbias[2][NGV];
 #pragma unroll
   for (int G = 0; G < NGV; ++G) vbias[0][G] = vbias[1][G] = 0.0f;
+  bool aborted = false;
+  int consumed = 0;
 
-  for (int k = 0; k < my_tiles; ++k) {
-    cp_async_wait<NS - 2>();
-    __syncwarp();
-    const uint8_t* stg = ring + (k % NS) * LY::STAGE;
-    const int t0 = c_lo + (warp + kWarps * k) * kTile;
-    const bool ok = tile_ok[k % NS] != 0;
-    __syncwarp();
-    issue(k + NS - 1);
+  for (int k = 0; k < my_stages; ++k) {
+    const int s = k % NS;
+    if (lane == 0) {
+      fence_proxy_async_smem();  // earlier reads of the stage being refilled come first
+      issue(k + NS - 1);
+    }
+    const bool ready = mbar_wait_bounded(smem_u32(&bars[s]), (k / NS) & 1);
+    if (!__all_sync(0xffffffffu, ready)) {
+      aborted = true;
+      break;
+    }
+    consumed = k + 1;
+    const uint8_t* stg = ring + s * LY::STAGE;
+    const int t0 = c_lo + (warp + kWarps * k) * kStage;
+    const bool ok = tile_ok[s] != 0;
 
-    // ---- S = K . Q^T (per group accumulators) ----
-    float acc[NGK][4];
+    // ---- S = K . Q^T for the two 16-token halves (independent accumulator chains) ----
+    float acc[2][NGK][4];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int G = 0; G < NGK; ++G) acc[hh][G][0] = acc[hh][G][1] = acc[hh][G][2] = acc[hh][G][3] = 0.0f;
 #pragma unroll
     for (int G = 0; G < NGK; ++G) {
-      acc[G][0] = acc[G][1] = acc[G][2] = acc[G][3] = 0.0f;
-      const uint2 wa = *reinterpret_cast<const uint2*>(stg + g * SK + G * 32 + t * 8);
-      const uint2 wb = *reinterpret_cast<const uint2*>(stg + (g + 8) * SK + G * 32 + t * 8);
+      uint2 wa[2], wb[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        wa[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g) * KROW + G * 32 + t * 8);
+        wb[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g + 8) * KROW + G * 32 + t * 8);
+      }
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        uint32_t xa = j ? wa.y : wa.x;
-        uint32_t xb = j ? wb.y : wb.x;
+        uint32_t xa[2], xb[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          xa[hh] = j ? wa[hh].y : wa[hh].x;
+          xb[hh] = j ? wb[hh].y : wb[hh].x;
+        }
         const int s0 = 4 * G + 2 * j;
-        mma_f16_16816(acc[G], xa & 0x000F000Fu, xb & 0x000F000Fu, xa & 0x00F000F0u,
-                      xb & 0x00F000F0u, qf[s0][0], qf[s0][1]);
-        xa >>= 8;
-        xb >>= 8;
-        mma_f16_16816(acc[G], xa & 0x000F000Fu, xb & 0x000F000Fu, xa & 0x00F000F0u,
-                      xb & 0x00F000F0u, qf[s0 + 1][0], qf[s0 + 1][1]);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh)
+          mma_f16_16816(acc[hh][G], xa[hh] & 0x000F000Fu, xb[hh] & 0x000F000Fu,
+                        xa[hh] & 0x00F000F0u, xb[hh] & 0x00F000F0u, qf[s0][0], qf[s0][1]);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          xa[hh] >>= 8;
+          xb[hh] >>= 8;
+          mma_f16_16816(acc[hh][G], xa[hh] & 0x000F000Fu, xb[hh] & 0x000F000Fu,
+                        xa[hh] & 0x00F000F0u, xb[hh] & 0x00F000F0u, qf[s0 + 1][0], qf[s0 + 1][1]);
+        }
       }
     }
-    // scores in log2 units: element e -> token (e < 2 ? g : g + 8), column 2t + (e & 1)
-    float sk[2][NGK], bk[2][NGK];
-    load_scales<NGK>(stg + LY::OFF_KS, g, sk[0], SBF16);
-    load_scales<NGK>(stg + LY::OFF_KS, g + 8, sk[1], SBF16);
-    load_scales<NGK>(stg + LY::OFF_KB, g, bk[0], SBF16);
-    load_scales<NGK>(stg + LY::OFF_KB, g + 8, bk[1], SBF16);
-    float s2[4];
+    // scores in log2 units: s2[hh][e] -> token hh*16 + g + 8*(e>>1), column 2t + (e&1)
+    float s2[2][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int tr = e >> 1, c = e & 1;
-      float x = 0.0f, y = 0.0f;
-#pragma unroll
-      for (int G = 0; G < NGK; ++G) {
-        x = fmaf(sk[tr][G], acc[G][e], x);
-        y = fmaf(bk[tr][G], qb[c][G], y);
-      }
-      s2[e] = fmaf(x, fac[c], y);
-    }
-    // ---- masking ----
-    const bool need_mask = !ok || t0 + kTile > n || t0 < st ||
-                           (p.causal && t0 + kTile - 1 > pos_min) ||
-                           (p.window > 0 && t0 <= pos_max - p.window) || dense_mask;
-    if (need_mask) {
+    for (int hh = 0; hh < 2; ++hh) {
+      float sk[2][NGK], bk[2][NGK];
+      load_scales<NGK>(stg + LY::OFF_KS, hh * 16 + g, sk[0], SBF16);
+      load_scales<NGK>(stg + LY::OFF_KS, hh * 16 + g + 8, sk[1], SBF16);
+      load_scales<NGK>(stg + LY::OFF_KB, hh * 16 + g, bk[0], SBF16);
+      load_scales<NGK>(stg + LY::OFF_KB, hh * 16 + g + 8, bk[1], SBF16);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int tok = t0 + g + 8 * (e >> 1);
-        const int c = e & 1;
-        bool keep = ok && tok < n && tok >= st;
-        if (p.causal && tok > pos_c[c]) keep = false;
-        if (p.window > 0 && tok <= pos_c[c] - p.window) keep = false;
-        float v = keep ? s2[e] : -INFINITY;
-        if (keep && dense_mask) {
-          const float mv = load_mask(p, b, hq_c[c], l_c[c], tok);
-          if (p.mask_kind == AM_MASK_BOOL) {
-            if (mv == 0.0f) v = kMaskedFinite;
-          } else {
-            v = fmaf(mv, 1.4426950408889634f, v);
-          }
+        const int tr = e >> 1, c = e & 1;
+        float x = 0.0f, y = 0.0f;
+#pragma unroll
+        for (int G = 0; G < NGK; ++G) {
+          x = fmaf(sk[tr][G], acc[hh][G][e], x);
+          y = fmaf(bk[tr][G], qb[c][G], y);
         }
-        s2[e] = v;
+        s2[hh][e] = fmaf(x, fac[c], y);
       }
     }
-    // ---- online softmax (per column) ----
-    float mt[2] = {fmaxf(s2[0], s2[2]), fmaxf(s2[1], s2[3])};
+    // ---- masking (only stages that touch a boundary) ----
+    const bool masked_stage = !ok || dense_mask || t0 < mask_lo || t0 + kStage > mask_hi;
+    if (masked_stage) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int tok = t0 + hh * 16 + g + 8 * (e >> 1);
+          const int c = e & 1;
+          bool keep = ok && tok < n && tok >= st;
+          if (p.causal && tok > pos_c[c]) keep = false;
+          if (p.window > 0 && tok <= pos_c[c] - p.window) keep = false;
+          float v = keep ? s2[hh][e] : -INFINITY;
+          if (keep && dense_mask) {
+            const float mv = load_mask(p, b, hq_c[c], l_c[c], tok);
+            if (p.mask_kind == AM_MASK_BOOL) {
+              if (mv == 0.0f) v = kMaskedFinite;
+            } else {
+              v = fmaf(mv, 1.4426950408889634f, v);
+            }
+          }
+          s2[hh][e] = v;
+        }
+      }
+    }
+    // ---- online softmax (per column, over the 32 tokens of the stage) ----
+    float mt[2] = {fmaxf(fmaxf(s2[0][0], s2[0][2]), fmaxf(s2[1][0], s2[1][2])),
+                   fmaxf(fmaxf(s2[0][1], s2[0][3]), fmaxf(s2[1][1], s2[1][3]))};
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       mt[c] = fmaxf(mt[c], __shfl_xor_sync(0xffffffffu, mt[c], 4));
@@ -376,44 +425,70 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     }
     const float ms0 = m_run[0] == -INFINITY ? 0.0f : m_run[0];
     const float ms1 = m_run[1] == -INFINITY ? 0.0f : m_run[1];
-    float pr[4];
-    pr[0] = ex2(s2[0] - ms0);
-    pr[1] = ex2(s2[1] - ms1);
-    pr[2] = ex2(s2[2] - ms0);
-    pr[3] = ex2(s2[3] - ms1);
-    l_run[0] += pr[0] + pr[2];
-    l_run[1] += pr[1] + pr[3];
 
-    // ---- O^T += V^T . (P * scale_v) ----
-    float sv[2][NGV], bv[2][NGV];
-    load_scales<NGV>(stg + LY::OFF_VS, g, sv[0], SBF16);
-    load_scales<NGV>(stg + LY::OFF_VS, g + 8, sv[1], SBF16);
-    load_scales<NGV>(stg + LY::OFF_VB, g, bv[0], SBF16);
-    load_scales<NGV>(stg + LY::OFF_VB, g + 8, bv[1], SBF16);
-    const uint8_t* vbase = stg + LY::OFF_V;
+    // ---- O^T += V^T . (P * scale_v), one k16 step per half ----
 #pragma unroll
-    for (int G = 0; G < NGV; ++G) {
-      vbias[0][G] = fmaf(pr[0], bv[0][G], fmaf(pr[2], bv[1][G], vbias[0][G]));
-      vbias[1][G] = fmaf(pr[1], bv[0][G], fmaf(pr[3], bv[1][G], vbias[1][G]));
-      const uint32_t blo = movmatrix_trans(pack_half2(pr[0] * sv[0][G], pr[1] * sv[0][G]));
-      const uint32_t bhi = movmatrix_trans(pack_half2(pr[2] * sv[1][G], pr[3] * sv[1][G]));
-      const int woff = (8 * G + g) * 4;
-      const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * SV + woff);
-      const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * SV + woff);
-      const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * SV + woff);
-      const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * SV + woff);
+    for (int hh = 0; hh < 2; ++hh) {
+      float pr[4];
+      pr[0] = ex2(s2[hh][0] - ms0);
+      pr[1] = ex2(s2[hh][1] - ms1);
+      pr[2] = ex2(s2[hh][2] - ms0);
+      pr[3] = ex2(s2[hh][3] - ms1);
+      l_run[0] += pr[0] + pr[2];
+      l_run[1] += pr[1] + pr[3];
+      float sv[2][NGV], bv[2][NGV];
+      load_scales<NGV>(stg + LY::OFF_VS, hh * 16 + g, sv[0], SBF16);
+      load_scales<NGV>(stg + LY::OFF_VS, hh * 16 + g + 8, sv[1], SBF16);
+      load_scales<NGV>(stg + LY::OFF_VB, hh * 16 + g, bv[0], SBF16);
+      load_scales<NGV>(stg + LY::OFF_VB, hh * 16 + g + 8, bv[1], SBF16);
+      if (masked_stage) {
+        // rows of excluded keys may hold stale shared memory (not loaded, or beyond the
+        // written length): zero their scale and bias so p = 0 cannot meet a NaN
 #pragma unroll
-      for (int beta = 0; beta < 4; ++beta) {
-        const uint32_t sel = beta | ((4 + beta) << 8);
-        const uint32_t r01 = __byte_perm(v0, v1, sel);
-        const uint32_t r23 = __byte_perm(v2, v3, sel);
-        mma_f16_16816(o[4 * G + beta], r01 & 0x000F000Fu, r01 & 0x00F000F0u, r23 & 0x000F000Fu,
-                      r23 & 0x00F000F0u, blo, bhi);
+        for (int tr = 0; tr < 2; ++tr) {
+          const bool live = pr[2 * tr] > 0.0f || pr[2 * tr + 1] > 0.0f;
+#pragma unroll
+          for (int G = 0; G < NGV; ++G) {
+            sv[tr][G] = live ? sv[tr][G] : 0.0f;
+            bv[tr][G] = live ? bv[tr][G] : 0.0f;
+          }
+        }
+      }
+      const uint8_t* vbase = stg + LY::OFF_V + hh * 16 * VROW;
+#pragma unroll
+      for (int G = 0; G < NGV; ++G) {
+        vbias[0][G] = fmaf(pr[0], bv[0][G], fmaf(pr[2], bv[1][G], vbias[0][G]));
+        vbias[1][G] = fmaf(pr[1], bv[0][G], fmaf(pr[3], bv[1][G], vbias[1][G]));
+        const uint32_t blo = movmatrix_trans(pack_half2(pr[0] * sv[0][G], pr[1] * sv[0][G]));
+        const uint32_t bhi = movmatrix_trans(pack_half2(pr[2] * sv[1][G], pr[3] * sv[1][G]));
+        const int woff = (8 * G + g) * 4;
+        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * VROW + woff);
+        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * VROW + woff);
+        const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * VROW + woff);
+        const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * VROW + woff);
+#pragma unroll
+        for (int beta = 0; beta < 4; ++beta) {
+          const uint32_t sel = beta | ((4 + beta) << 8);
+          const uint32_t r01 = __byte_perm(v0, v1, sel);
+          const uint32_t r23 = __byte_perm(v2, v3, sel);
+          mma_f16_16816(o[4 * G + beta], r01 & 0x000F000Fu, r01 & 0x00F000F0u, r23 & 0x000F000Fu,
+                        r23 & 0x00F000F0u, blo, bhi);
+        }
       }
     }
+    __syncwarp();
   }
-  cp_async_wait<0>();
-  __syncwarp();
+  if (aborted) {
+    if (lane == 0) {
+      flag_status(p.status, AM_STATUS_TIMEOUT);
+      // give copies already in flight a bounded chance to land before the smem is reused
+      for (int k = consumed; k < min(my_stages, consumed + NS); ++k)
+        mbar_wait_bounded(smem_u32(&bars[k % NS]), (k / NS) & 1, 100000000ull);
+    }
+    __syncwarp();
+    m_run[0] = m_run[1] = -INFINITY;
+    l_run[0] = l_run[1] = 0.0f;
+  }
 
   // ------------------------------------------------------------------ warp reduction
 #pragma unroll
@@ -552,7 +627,7 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int* chunk
 template <int DK, int DV, bool SBF16, bool PAGED>
 static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_groups,
                                    cudaStream_t stream) {
-  constexpr int NS = DK >= 256 ? 3 : 4;
+  constexpr int NS = DK >= 256 ? 2 : 3;
   using LY = DecodeLayout<DK, DV, NS>;
   auto kfn = decode_kernel<DK, DV, SBF16, PAGED, NS>;
   static bool attr_done = false;  // per instantiation; idempotent if raced

@@ -157,7 +157,7 @@ def _capacity_of(t: torch.Tensor) -> int | None:
     cap = s1 // W
     if cap < N or (B > 1 and s0 != H * s1):
         return None
-    if t.data_ptr() % (16 if t.dtype == torch.int32 else 4):
+    if t.data_ptr() % 16:  # the decode kernel moves codes and scales with 16-byte bulk copies
         return None
     # the kernels stream whole 16-row tiles: rows up to ceil16(N) of every plane must exist
     end = t.storage_offset() + (B - 1) * s0 + (H - 1) * s1 + ((N + 15) // 16 * 16) * W

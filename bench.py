@@ -217,10 +217,12 @@ def run_ours(args, rank, world, local_rank):
             for _ in range(layers)] for _ in range(args.steps)]
     torch.cuda.synchronize(dev)
     barrier()
+    torch.cuda.nvtx.range_push("timed")
     t0.record(stream)
     for s in range(args.steps):
         step(evs[s])
     t1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     barrier()
     clk = clocks.stop()
@@ -375,10 +377,12 @@ def run_single_workload(args, am, dev, rank, world):
     evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
             for _ in range(inst)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
     t0.record(stream)
     for s in range(args.steps):
         step(evs[s])
     t1.record(stream)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     clk = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps / reps
