@@ -2,19 +2,21 @@
 //
 // One CTA = 128 query rows of one KV head of one sequence.  Rows are (token, GQA head)
 // pairs, token-major: 128 / n_rep query tokens times the n_rep heads that share the KV
-// head, so each dequantized K/V tile feeds all of them.  Per 128-token KV tile:
-//   1. the 128 threads dequantize the Q4 K and V rows (one token each) into fp16
-//      operand tiles in shared memory (128-byte swizzle; K K-major, V MN-major);
-//   2. one thread issues S = Q . K^T as D/16 tcgen05.mma (M=128, N=128, K=16, fp32
-//      accumulators in TMEM columns [0,128)) and commits to an mbarrier;
-//   3. thread r reads TMEM lane r (its row of S) with tcgen05.ld, applies scale and mask,
-//      updates the running max / sum and writes P (fp16) into the K tile's buffer;
-//   4. one thread issues O_tile = P . V (8 MMAs, TMEM columns [128, 128+D)); each thread
-//      then adds its TMEM row of O_tile to its fp32 register accumulator.
-// Operands are fp16 for every query dtype: bf16 queries are rescaled per row by a power
-// of two so the conversion is exact, and the factor is removed from S in fp32.
-// Every mbarrier wait is bounded (2 s of %globaltimer); on timeout the kernel flags
-// AM_STATUS_TIMEOUT, stops issuing work, frees its TMEM and returns.
+// head, so each dequantized K/V tile feeds all of them.  256 threads, warp-specialised:
+//   * producer warps 4-7 dequantize the Q4 K and V rows of 128-key tile j (one token per
+//     thread) into fp16 operand tiles in shared memory (128-byte swizzle; K K-major,
+//     V MN-major; two buffers), then one producer thread issues S_j = Q . K_j^T
+//     (tcgen05.mma kind::f16, M=128, N=128, K=16 steps) into TMEM S[j%2] and, once the
+//     softmax warps have written P_{j-1}, O_{j-1} = P_{j-1} . V_{j-1} into TMEM O[(j-1)%2];
+//   * softmax warps 0-3 own TMEM lanes 0-127 (one query row per thread): tcgen05.ld of
+//     their S row, fp32 online softmax, P (fp16, K-major) into shared memory, and the
+//     previous tile's O row folded into fp32 registers with the running-max correction.
+// mbarriers (MMA commits and 128-thread arrivals) chain the stages so the dequantisation
+// of tile j+1, the MMAs of tile j and the softmax of tile j overlap.  TMEM: S x2 + O x2
+// (512 columns, one CTA per SM).  Operands are fp16 for every query dtype: bf16 queries
+// are rescaled per row by a power of two so the conversion is exact.  Every mbarrier
+// wait is bounded (2 s of %globaltimer); on timeout the kernel flags AM_STATUS_TIMEOUT,
+// stops issuing work, frees its TMEM and returns.
 //
 // Reference semantics: the compiled quantized SDPA (mlx_fused_attention.py:69-139) as
 // used by chunked prefill (batch_engine.py:339-456): the chunk's own K/V are already in
@@ -67,27 +69,6 @@ __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
 
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        "selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (globaltimer() - t0 > 2000000000ull) return false;
-  }
-}
-
 #define AM_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), \
                  "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
 
@@ -112,39 +93,60 @@ __device__ __forceinline__ uint32_t swz(uint32_t off) { return off ^ (((off >> 7
 
 template <int D>
 struct PrefillLayout {
-  static constexpr int TILE_BYTES = 128 * D * 2;                       // 128 rows x D fp16
-  static constexpr int P_BYTES = 128 * 128 * 2;                        // 128 rows x 128 keys
-  static constexpr int KP_BYTES = TILE_BYTES > P_BYTES ? TILE_BYTES : P_BYTES;
+  static constexpr int TILE = 128 * 128 * 2;  // 128 rows x up to 128 fp16 (Q, K, V tiles)
+  static constexpr int P_BYTES = 128 * 128 * 2;  // P: 128 rows x 128 keys fp16
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + TILE_BYTES;  // K tile, reused for P
-  static constexpr int OFF_V = OFF_K + KP_BYTES;
-  static constexpr int OFF_BAR = OFF_V + TILE_BYTES;
-  static constexpr int SMEM = OFF_BAR + 64 + 1024;  // + slack for 1024-byte alignment
-  static constexpr uint32_t TMEM_COLS = 256;
+  static constexpr int OFF_K = OFF_Q + TILE;   // two K buffers
+  static constexpr int OFF_V = OFF_K + 2 * TILE;  // two V buffers
+  static constexpr int OFF_P = OFF_V + 2 * TILE;
+  static constexpr int OFF_QF = OFF_P + P_BYTES;  // per-row query factor (128 floats)
+  static constexpr int OFF_BAR = OFF_QF + 128 * 4;
+  static constexpr int SMEM = OFF_BAR + 128 + 1024;  // barriers + slack for 1024-byte alignment
+  static constexpr uint32_t TMEM_COLS = 512;     // S x2 (256) + O x2 (2 x D)
+  static_assert(D <= 128, "tiles sized for D <= 128");
 };
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) { return pack_half2(a, b); }
+// o_acc = o_acc * scale_old + (this thread's TMEM row of an O tile at taddr)
+template <int D>
+__device__ __forceinline__ void fold_o(float (&o_acc)[D], uint32_t taddr, float scale_old) {
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    float v[32];
+    tc::tmem_ld32(taddr + c * 32, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) o_acc[c * 32 + j] = fmaf(o_acc[c * 32 + j], scale_old, v[j]);
+  }
+}
 
-template <int D, bool SBF16, bool PAGED>
-__global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
+// mbarrier slots (8 bytes each) inside OFF_BAR
+enum { B_SFULL = 0, B_SFREE = 2, B_PFULL = 4, B_OFULL = 5, B_KVFREE = 7, B_COUNT = 9 };
+
+__device__ __forceinline__ void named_bar_producers() {
+  asm volatile("bar.sync 1, 128;\n" ::: "memory");
+}
+
+template <int D, bool SBF16, bool PAGED, bool DENSE>
+__global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
   using LY = PrefillLayout<D>;
   constexpr int NG = D / 64;
   constexpr int KSTEPS = D / 16;
 
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte-align the operand region (swizzle atoms).
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
   const uint32_t s_base = raw_addr + pad;
-  const uint32_t sQ = s_base + LY::OFF_Q, sK = s_base + LY::OFF_K, sV = s_base + LY::OFF_V;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::OFF_BAR + 8);
-  int* abort_flag = reinterpret_cast<int*>(smem + LY::OFF_BAR + 16);
-  const uint32_t bar_addr = smem_u32(bar);
+  const uint32_t sQ = s_base + LY::OFF_Q, sK = s_base + LY::OFF_K, sV = s_base + LY::OFF_V,
+                 sP = s_base + LY::OFF_P;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::OFF_BAR + B_COUNT * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::OFF_BAR + B_COUNT * 8 + 4);
+  float* sqf = reinterpret_cast<float*>(smem + LY::OFF_QF);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  const bool producer = warp >= 4;
   const int b = blockIdx.z, h = blockIdx.y;
   const int n_rep = p.n_rep;
   const int tok_per_cta = 128 / n_rep;
@@ -153,27 +155,27 @@ __global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
 
   const int n = p.kv_len[b];
   const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
-  const bool dense_mask = p.mask_kind != AM_MASK_NONE;
   const int pos_min = n - p.q_len + l0, pos_max = n - p.q_len + l_last;
   int lo = 0, hi = n;
-  if (!dense_mask) {
+  if (!DENSE) {
     lo = max(st, 0);
     if (p.window > 0) lo = max(lo, pos_min - p.window + 1);
   }
   if (p.causal) hi = min(hi, pos_max + 1);
+  const int n_tiles = hi > lo ? (hi - lo + 127) / 128 : 0;
 
-  // ---- this thread's query row
-  const int r = tid;
-  const int rl = r / n_rep;
-  const bool row_ok = r < tok_per_cta * n_rep && l0 + rl < p.q_len;
-  const int l = l0 + (row_ok ? rl : 0);
-  const int hq = h * n_rep + r % n_rep;
-  const int pos = n - p.q_len + l;
-
-  // ---- setup: barrier, TMEM, Q tile
+  // ---- setup
   if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar_addr), "r"(1));
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    mbar_init(bar(B_SFULL), 1);
+    mbar_init(bar(B_SFULL + 1), 1);
+    mbar_init(bar(B_SFREE), 128);
+    mbar_init(bar(B_SFREE + 1), 128);
+    mbar_init(bar(B_PFULL), 128);
+    mbar_init(bar(B_OFULL), 1);
+    mbar_init(bar(B_OFULL + 1), 1);
+    mbar_init(bar(B_KVFREE), 1);
+    mbar_init(bar(B_KVFREE + 1), 1);
+    fence_mbar_init();
     *abort_flag = 0;
   }
   if (warp == 0) {
@@ -182,12 +184,17 @@ __global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
                  "r"(LY::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
   }
-  // Q row -> fp16 with a power-of-two prescale (exact for fp16 and bf16 inputs).
-  float q_fac;
-  {
+  if (producer) {
+    // query row r = tid - 128 -> fp16 with a power-of-two prescale (exact for fp16 / bf16)
+    const int r = tid - 128;
+    const int rl = r / n_rep;
+    const bool row_ok = r < tok_per_cta * n_rep && l0 + rl < p.q_len;
+    const int l = l0 + (row_ok ? rl : 0);
+    const int hq = h * n_rep + r % n_rep;
     const uint16_t* qrow = p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl;
     float amax = 0.0f;
     if (row_ok) {
+#pragma unroll 1
       for (int c = 0; c < D / 8; ++c) {
         const uint4 raw = *reinterpret_cast<const uint4*>(qrow + c * 8);
         const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -204,7 +211,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
       frexpf(amax, &e);
       pw = ldexpf(1.0f, 15 - e);
     }
-    q_fac = p.scale_log2 / pw;
+    sqf[r] = p.scale_log2 / pw;
+#pragma unroll 1
     for (int c = 0; c < D / 8; ++c) {
       uint4 outv = make_uint4(0, 0, 0, 0);
       if (row_ok) {
@@ -213,7 +221,7 @@ __global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
         uint32_t o4[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          o4[i] = pack_h2(h2f_rt(u[i] & 0xffffu, p.q_bf16) * pw, h2f_rt(u[i] >> 16, p.q_bf16) * pw);
+          o4[i] = pack_half2(h2f_rt(u[i] & 0xffffu, p.q_bf16) * pw, h2f_rt(u[i] >> 16, p.q_bf16) * pw);
         outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
       }
       const uint32_t off = (c / 8) * (128 * 128) + r * 128 + (c % 8) * 16;
@@ -225,24 +233,22 @@ __global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tmem_s = tmem;        // S: columns [0, 128)
-  const uint32_t tmem_o = tmem + 128;  // O tile: columns [128, 128 + D)
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-
-  float o_acc[D];
-#pragma unroll
-  for (int i = 0; i < D; ++i) o_acc[i] = 0.0f;
-  float m_run = -INFINITY, l_run = 0.0f;
-  uint32_t phase = 0;
-  bool aborted = false;
-
   constexpr uint32_t ID_S = tc::idesc(128, 128, false);
   constexpr uint32_t ID_O = tc::idesc(128, D, true);
 
-  for (int t0 = lo; t0 < hi && !aborted; t0 += 128) {
-    // ---- 1. dequantize K and V rows (token t0 + tid)
-    {
-      const int tok = t0 + tid;
+  if (producer) {
+    // ================================================================ producer warps
+    const int r = tid - 128;  // token row of each K/V tile this thread dequantizes
+    for (int j = 0; j < n_tiles; ++j) {
+      const int buf = j & 1;
+      if (j >= 2 && !*abort_flag) {
+        if (!mbar_wait_bounded(bar(B_KVFREE + buf), ((j - 2) >> 1) & 1)) *abort_flag = 1;
+      }
+      // every producer thread reads the flag after the same barrier, so all of them leave
+      // the loop together (no thread may be left waiting in bar.sync 1)
+      named_bar_producers();
+      if (*abort_flag) break;
+      const int tok = lo + j * 128 + r;
       bool valid = tok < n && tok >= 0;
       int64_t row = 0;
       if (valid) {
@@ -261,6 +267,8 @@ __global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
       }
       const uint32_t* kc = p.kc + row * (D / 8);
       const uint32_t* vc = p.vc + row * (D / 8);
+      uint8_t* kdst = smem + LY::OFF_K + buf * LY::TILE;
+      uint8_t* vdst = smem + LY::OFF_V + buf * LY::TILE;
 #pragma unroll
       for (int G = 0; G < NG; ++G) {
         float ks = 0.f, kb = 0.f, vs = 0.f, vb = 0.f;
@@ -271,7 +279,7 @@ __global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
           vb = h2f<SBF16>(p.vb[row * NG + G]);
         }
 #pragma unroll
-        for (int w4 = 0; w4 < 2; ++w4) {  // 8 words per group, loaded 4 at a time
+        for (int w4 = 0; w4 < 2; ++w4) {
           uint4 kw = make_uint4(0, 0, 0, 0), vw = make_uint4(0, 0, 0, 0);
           if (valid) {
             kw = *reinterpret_cast<const uint4*>(kc + G * 8 + w4 * 4);
@@ -281,167 +289,235 @@ __global__ void __launch_bounds__(128) prefill_kernel(const DecodeParams p) {
           const uint32_t vv[4] = {vw.x, vw.y, vw.z, vw.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int wi = G * 8 + w4 * 4 + i;  // word index = 8-element chunk along D
+            const int wi = G * 8 + w4 * 4 + i;
             uint32_t ko[4], vo[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float k0 = valid ? fmaf(static_cast<float>((kk[i] >> (8 * e)) & 0xfu), ks, kb) : 0.f;
-              const float k1 = valid ? fmaf(static_cast<float>((kk[i] >> (8 * e + 4)) & 0xfu), ks, kb) : 0.f;
-              const float v0 = valid ? fmaf(static_cast<float>((vv[i] >> (8 * e)) & 0xfu), vs, vb) : 0.f;
-              const float v1 = valid ? fmaf(static_cast<float>((vv[i] >> (8 * e + 4)) & 0xfu), vs, vb) : 0.f;
-              ko[e] = pack_h2(k0, k1);
-              vo[e] = pack_h2(v0, v1);
+              ko[e] = pack_half2(fmaf(static_cast<float>((kk[i] >> (8 * e)) & 0xfu), ks, kb),
+                              fmaf(static_cast<float>((kk[i] >> (8 * e + 4)) & 0xfu), ks, kb));
+              vo[e] = pack_half2(fmaf(static_cast<float>((vv[i] >> (8 * e)) & 0xfu), vs, vb),
+                              fmaf(static_cast<float>((vv[i] >> (8 * e + 4)) & 0xfu), vs, vb));
             }
-            // K: K-major [token][dim], 64-dim column blocks of 128 rows x 128 B.
-            const uint32_t koff = (wi / 8) * (128 * 128) + tid * 128 + (wi % 8) * 16;
-            *reinterpret_cast<uint4*>(smem + LY::OFF_K + tc::swz(koff)) =
-                make_uint4(ko[0], ko[1], ko[2], ko[3]);
-            // V: MN-major [token][dim]: 64-dim blocks (LBO = 16 KB) of 8-token atoms (SBO = 1 KB).
-            const uint32_t voff = (wi / 8) * (128 * 128) + (tid / 8) * 1024 + (tid % 8) * 128 + (wi % 8) * 16;
-            *reinterpret_cast<uint4*>(smem + LY::OFF_V + tc::swz(voff)) =
-                make_uint4(vo[0], vo[1], vo[2], vo[3]);
+            const uint32_t koff = (wi / 8) * (128 * 128) + r * 128 + (wi % 8) * 16;
+            *reinterpret_cast<uint4*>(kdst + tc::swz(koff)) = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+            const uint32_t voff = (wi / 8) * (128 * 128) + (r / 8) * 1024 + (r % 8) * 128 + (wi % 8) * 16;
+            *reinterpret_cast<uint4*>(vdst + tc::swz(voff)) = make_uint4(vo[0], vo[1], vo[2], vo[3]);
           }
         }
       }
-    }
-    tc::fence_proxy_async();
-    tc::fence_before();
-    __syncthreads();
-    // ---- 2. S = Q . K^T
-    if (tid == 0) {
-      tc::fence_after();
+      tc::fence_proxy_async();
+      named_bar_producers();
+      if (r == 0) {
+        tc::fence_after();
+        bool ok = true;
+        if (j >= 2) ok = mbar_wait_bounded(bar(B_SFREE + buf), ((j - 2) >> 1) & 1);
+        if (ok) {
+          const uint32_t kb_addr = sK + buf * LY::TILE;
 #pragma unroll
-      for (int ks = 0; ks < KSTEPS; ++ks) {
-        const uint32_t koff = (ks / 4) * (128 * 128) + (ks % 4) * 32;
-        tc::mma(tmem_s, tc::sdesc(sQ + koff, 16, 1024), tc::sdesc(sK + koff, 16, 1024), ID_S,
-                ks > 0 ? 1u : 0u);
+          for (int ks = 0; ks < KSTEPS; ++ks) {
+            const uint32_t off = (ks / 4) * (128 * 128) + (ks % 4) * 32;
+            tc::mma(tmem + buf * 128, tc::sdesc(sQ + off, 16, 1024), tc::sdesc(kb_addr + off, 16, 1024),
+                    ID_S, ks > 0 ? 1u : 0u);
+          }
+          tc::commit(bar(B_SFULL + buf));
+          if (j >= 1) {
+            ok = mbar_wait_bounded(bar(B_PFULL), (j - 1) & 1);
+            if (ok) {
+              tc::fence_after();
+              const int pb = (j - 1) & 1;
+              const uint32_t vb_addr = sV + pb * LY::TILE;
+#pragma unroll
+              for (int ks = 0; ks < 8; ++ks) {
+                const uint32_t poff = (ks / 4) * (128 * 128) + (ks % 4) * 32;
+                tc::mma(tmem + 256 + pb * D, tc::sdesc(sP + poff, 16, 1024),
+                        tc::sdesc(vb_addr + ks * 2048, 128 * 128, 1024), ID_O, ks > 0 ? 1u : 0u);
+              }
+              tc::commit(bar(B_OFULL + pb));
+              tc::commit(bar(B_KVFREE + pb));
+            }
+          }
+        }
+        if (!ok) *abort_flag = 1;
       }
-      tc::commit(bar_addr);
     }
-    bool ok = tc::mbar_wait(bar_addr, phase);
-    phase ^= 1u;
-    if (!__syncthreads_and(ok)) {
-      aborted = true;
-      break;
+    // last P . V
+    if (tid == 128 && n_tiles > 0 && !*abort_flag) {
+      const int j = n_tiles;
+      if (mbar_wait_bounded(bar(B_PFULL), (j - 1) & 1)) {
+        tc::fence_after();
+        const int pb = (j - 1) & 1;
+        const uint32_t vb_addr = sV + pb * LY::TILE;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t poff = (ks / 4) * (128 * 128) + (ks % 4) * 32;
+          tc::mma(tmem + 256 + pb * D, tc::sdesc(sP + poff, 16, 1024),
+                  tc::sdesc(vb_addr + ks * 2048, 128 * 128, 1024), ID_O, ks > 0 ? 1u : 0u);
+        }
+        tc::commit(bar(B_OFULL + pb));
+        tc::commit(bar(B_KVFREE + pb));
+      } else {
+        *abort_flag = 1;
+      }
     }
-    tc::fence_after();
+  } else {
+    // ================================================================ softmax warps
+    const int r = tid;  // query row == TMEM lane
+    const int rl = r / n_rep;
+    const bool row_ok = r < tok_per_cta * n_rep && l0 + rl < p.q_len;
+    const int l = l0 + (row_ok ? rl : 0);
+    const int hq = h * n_rep + r % n_rep;
+    const int pos = n - p.q_len + l;
+    const int klo = max(st, p.window > 0 ? pos - p.window + 1 : 0);
+    const int khi = p.causal ? min(n, pos + 1) : n;
+    const int tlo = max(st, p.window > 0 ? pos_max - p.window + 1 : 0);  // CTA-wide safe range
+    const int thi = p.causal ? min(n, pos_min + 1) : n;
+    const float q_fac = sqf[r];
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
 
-    // ---- 3. softmax on this thread's row of S
-    const bool need_mask = dense_mask || t0 < st || t0 + 127 >= n ||
-                           (p.causal && t0 + 127 > pos_min) ||
-                           (p.window > 0 && t0 <= pos_max - p.window);
-    auto masked_val = [&](float s, int j) -> float {
-      const int tok = t0 + j;
-      bool keep = row_ok && tok < n && tok >= st;
-      if (p.causal && tok > pos) keep = false;
-      if (p.window > 0 && tok <= pos - p.window) keep = false;
-      if (!keep) return -INFINITY;
-      if (dense_mask) {
+    float o_acc[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o_acc[i] = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
+
+    auto masked = [&](float s, int tok) -> float {
+      if (!(row_ok && tok >= klo && tok < khi)) return -INFINITY;
+      if constexpr (DENSE) {
         const int64_t idx = (int64_t)b * p.msb + (int64_t)hq * p.msh + (int64_t)l * p.msl +
                             (int64_t)tok * p.msn;
         if (p.mask_kind == AM_MASK_BOOL) {
           if (static_cast<const uint8_t*>(p.mask)[idx] == 0) return -1.0e30f;
         } else {
-          float mv = p.mask_dtype == AM_DTYPE_F32
-                         ? static_cast<const float*>(p.mask)[idx]
-                         : h2f_rt(static_cast<const uint16_t*>(p.mask)[idx],
-                                  p.mask_dtype == AM_DTYPE_BF16);
+          const float mv = p.mask_dtype == AM_DTYPE_F32
+                               ? static_cast<const float*>(p.mask)[idx]
+                               : h2f_rt(static_cast<const uint16_t*>(p.mask)[idx],
+                                        p.mask_dtype == AM_DTYPE_BF16);
           s = fmaf(mv, 1.4426950408889634f, s);
         }
       }
       return s;
     };
-    float tile_max = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tc::tmem_ld32(tmem_s + lane_base + c * 32, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float s = v[j] * q_fac;
-        if (need_mask) s = masked_val(s, c * 32 + j);
-        tile_max = fmaxf(tile_max, s);
+
+    for (int i = 0; i < n_tiles; ++i) {
+      const int buf = i & 1;
+      const int t0 = lo + i * 128;
+      // warp-uniform decisions: the tcgen05.ld below is a warp-collective instruction
+      bool ok = !*abort_flag && mbar_wait_bounded(bar(B_SFULL + buf), (i >> 1) & 1);
+      if (!__all_sync(0xffffffffu, ok)) {
+        *abort_flag = 1;
+        break;
       }
-    }
-    const float m_new = fmaxf(m_run, tile_max);
-    if (m_new > m_run) {
-      const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
+      tc::fence_after();
+      const bool need_mask =
+          __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + 128 > thi);  // warp-uniform
+      const uint32_t s_addr = tmem + buf * 128 + lane_base;
+      float tile_max = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tc::tmem_ld32(s_addr + c * 32, v);
+        if (need_mask) {
 #pragma unroll
-      for (int i = 0; i < D; ++i) o_acc[i] *= alpha;
+          for (int j2 = 0; j2 < 32; ++j2) tile_max = fmaxf(tile_max, masked(v[j2] * q_fac, t0 + c * 32 + j2));
+        } else {
+#pragma unroll
+          for (int j2 = 0; j2 < 32; ++j2) tile_max = fmaxf(tile_max, v[j2] * q_fac);
+        }
+      }
+      const float m_new = fmaxf(m_run, tile_max);
+      const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
+      if (i >= 1) {
+        // O of the previous tile is relative to the previous max: fold it in now
+        ok = !*abort_flag && mbar_wait_bounded(bar(B_OFULL + ((i - 1) & 1)), ((i - 1) >> 1) & 1);
+        if (!__all_sync(0xffffffffu, ok)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc::fence_after();
+        fold_o<D>(o_acc, tmem + 256 + ((i - 1) & 1) * D + lane_base, alpha_prev);
+      }
       l_run *= alpha;
       m_run = m_new;
-    }
-    const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
+      alpha_prev = alpha;
+      const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
+      // P row r (fp16, K-major over keys), written once the previous P . V has read P
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tc::tmem_ld32(s_addr + c * 32, v);
+        uint32_t pk[16];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tc::tmem_ld32(tmem_s + lane_base + c * 32, v);
-      uint32_t pk[16];
-#pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        float s0 = v[j] * q_fac, s1 = v[j + 1] * q_fac;
-        if (need_mask) {
-          s0 = masked_val(s0, c * 32 + j);
-          s1 = masked_val(s1, c * 32 + j + 1);
+        for (int j2 = 0; j2 < 32; j2 += 2) {
+          float s0 = v[j2] * q_fac, s1 = v[j2 + 1] * q_fac;
+          if (need_mask) {
+            s0 = masked(s0, t0 + c * 32 + j2);
+            s1 = masked(s1, t0 + c * 32 + j2 + 1);
+          }
+          const float p0 = ex2(s0 - m_safe), p1 = ex2(s1 - m_safe);
+          l_run += p0 + p1;
+          pk[j2 / 2] = pack_half2(p0, p1);
         }
-        const float p0 = ex2(s0 - m_safe), p1 = ex2(s1 - m_safe);
-        l_run += p0 + p1;
-        pk[j / 2] = pack_h2(p0, p1);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int key0 = c * 32 + q4 * 8;
+          const uint32_t off = (key0 / 64) * (128 * 128) + r * 128 + ((key0 % 64) / 8) * 16;
+          *reinterpret_cast<uint4*>(smem + LY::OFF_P + tc::swz(off)) =
+              make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
+        }
       }
-      // P row r, keys c*32 .. c*32+31: K-major over keys, 64-key column blocks.
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const int key0 = c * 32 + q4 * 8;
-        const uint32_t off = (key0 / 64) * (128 * 128) + r * 128 + ((key0 % 64) / 8) * 16;
-        *reinterpret_cast<uint4*>(smem + LY::OFF_K + tc::swz(off)) =
-            make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
+      tc::fence_proxy_async();
+      tc::fence_before();
+      mbar_arrive(bar(B_SFREE + buf));
+      mbar_arrive(bar(B_PFULL));
+    }
+    if (n_tiles > 0 && __all_sync(0xffffffffu, !*abort_flag)) {
+      const int i = n_tiles;
+      const bool ok = mbar_wait_bounded(bar(B_OFULL + ((i - 1) & 1)), ((i - 1) >> 1) & 1);
+      if (__all_sync(0xffffffffu, ok)) {
+        tc::fence_after();
+        fold_o<D>(o_acc, tmem + 256 + ((i - 1) & 1) * D + lane_base, alpha_prev);
+      } else {
+        *abort_flag = 1;
       }
     }
-    tc::fence_proxy_async();
-    tc::fence_before();
-    __syncthreads();
-    // ---- 4. O_tile = P . V
-    if (tid == 0) {
-      tc::fence_after();
+    // ---- epilogue: this thread's output row
+    if (row_ok && !*abort_flag) {
+      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl;
+      if (p.out_dtype == AM_DTYPE_F32) {
+        float* o = static_cast<float*>(p.out) + ob;
+        if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t poff = (ks / 4) * (128 * 128) + (ks % 4) * 32;
-        tc::mma(tmem_o, tc::sdesc(sK + poff, 16, 1024), tc::sdesc(sV + ks * 2048, 128 * 128, 1024),
-                ID_O, ks > 0 ? 1u : 0u);
+          for (int d = 0; d < D; d += 4)
+            *reinterpret_cast<float4*>(o + d) =
+                make_float4(o_acc[d] * inv, o_acc[d + 1] * inv, o_acc[d + 2] * inv, o_acc[d + 3] * inv);
+        } else {
+#pragma unroll
+          for (int d = 0; d < D; ++d) o[d] = o_acc[d] * inv;
+        }
+      } else {
+        const bool bf = p.out_dtype == AM_DTYPE_BF16;
+        uint16_t* o = static_cast<uint16_t*>(p.out) + ob;
+        if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+          for (int d = 0; d < D; d += 8) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float a = o_acc[d + 2 * e] * inv, c2 = o_acc[d + 2 * e + 1] * inv;
+              w[e] = bf ? (static_cast<uint32_t>(f2h<true>(a)) | (static_cast<uint32_t>(f2h<true>(c2)) << 16))
+                        : pack_half2(a, c2);
+            }
+            *reinterpret_cast<uint4*>(o + d) = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        } else {
+#pragma unroll
+          for (int d = 0; d < D; ++d) o[d] = bf ? f2h<true>(o_acc[d] * inv) : f2h<false>(o_acc[d] * inv);
+        }
       }
-      tc::commit(bar_addr);
     }
-    ok = tc::mbar_wait(bar_addr, phase);
-    phase ^= 1u;
-    if (!__syncthreads_and(ok)) {
-      aborted = true;
-      break;
-    }
-    tc::fence_after();
-#pragma unroll
-    for (int c = 0; c < D / 32; ++c) {
-      float v[32];
-      tc::tmem_ld32(tmem_o + lane_base + c * 32, v);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o_acc[c * 32 + j] += v[j];
-    }
-    tc::fence_before();
-    __syncthreads();  // TMEM S / O and the K, V, P buffers are free for the next tile
   }
 
-  if (aborted) {
-    if (tid == 0) flag_status(p.status, AM_STATUS_TIMEOUT);
-    // Give in-flight MMAs a bounded chance to drain before the TMEM is released.
-    tc::mbar_wait(bar_addr, phase);
-  }
-
-  // ---- epilogue
-  if (row_ok && !aborted) {
-    const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-    const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl;
-#pragma unroll
-    for (int d = 0; d < D; ++d) store_out(p.out, ob + d, o_acc[d] * inv, p.out_dtype);
-  }
+  if (*abort_flag && tid == 0) flag_status(p.status, AM_STATUS_TIMEOUT);
   tc::fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -455,10 +531,10 @@ bool prefill_supported(int k_dim, int v_dim) {
   return k_dim == v_dim && (k_dim == 64 || k_dim == 128);
 }
 
-template <int D, bool SBF16, bool PAGED>
+template <int D, bool SBF16, bool PAGED, bool DENSE>
 static cudaError_t launch_prefill_t(const DecodeParams& p, int batch, cudaStream_t stream) {
   using LY = PrefillLayout<D>;
-  auto kfn = prefill_kernel<D, SBF16, PAGED>;
+  auto kfn = prefill_kernel<D, SBF16, PAGED, DENSE>;
   static bool attr_done = false;
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::SMEM);
@@ -467,24 +543,30 @@ static cudaError_t launch_prefill_t(const DecodeParams& p, int batch, cudaStream
   }
   const int tok_per_cta = 128 / p.n_rep;
   dim3 grid((p.q_len + tok_per_cta - 1) / tok_per_cta, p.hkv, batch);
-  kfn<<<grid, 128, LY::SMEM, stream>>>(p);
+  kfn<<<grid, 256, LY::SMEM, stream>>>(p);
   return cudaGetLastError();
+}
+
+template <int D, bool SBF16, bool PAGED>
+static cudaError_t launch_prefill_m(const DecodeParams& p, int batch, cudaStream_t stream) {
+  return p.mask_kind != AM_MASK_NONE ? launch_prefill_t<D, SBF16, PAGED, true>(p, batch, stream)
+                                     : launch_prefill_t<D, SBF16, PAGED, false>(p, batch, stream);
 }
 
 cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16,
                            cudaStream_t stream) {
   if (p.n_rep < 1 || p.n_rep > 128) return cudaErrorNotSupported;
   if (p.k_dim == 128 && p.v_dim == 128) {
-    if (paged) return scale_bf16 ? launch_prefill_t<128, true, true>(p, batch, stream)
-                                 : launch_prefill_t<128, false, true>(p, batch, stream);
-    return scale_bf16 ? launch_prefill_t<128, true, false>(p, batch, stream)
-                      : launch_prefill_t<128, false, false>(p, batch, stream);
+    if (paged) return scale_bf16 ? launch_prefill_m<128, true, true>(p, batch, stream)
+                                 : launch_prefill_m<128, false, true>(p, batch, stream);
+    return scale_bf16 ? launch_prefill_m<128, true, false>(p, batch, stream)
+                      : launch_prefill_m<128, false, false>(p, batch, stream);
   }
   if (p.k_dim == 64 && p.v_dim == 64) {
-    if (paged) return scale_bf16 ? launch_prefill_t<64, true, true>(p, batch, stream)
-                                 : launch_prefill_t<64, false, true>(p, batch, stream);
-    return scale_bf16 ? launch_prefill_t<64, true, false>(p, batch, stream)
-                      : launch_prefill_t<64, false, false>(p, batch, stream);
+    if (paged) return scale_bf16 ? launch_prefill_m<64, true, true>(p, batch, stream)
+                                 : launch_prefill_m<64, false, true>(p, batch, stream);
+    return scale_bf16 ? launch_prefill_m<64, true, false>(p, batch, stream)
+                      : launch_prefill_m<64, false, false>(p, batch, stream);
   }
   return cudaErrorNotSupported;
 }

@@ -359,39 +359,41 @@ def run_single_workload(args, am, dev, rank, world):
     is_global = [(l % GEMMA["global_every"]) == GEMMA["global_every"] - 1 for l in range(layers)]
     stream = torch.cuda.current_stream(dev)
 
-    def step(ev=None):
+    def step():
         for i in range(inst):
             wl = 0 if (w != "gemma" or is_global[i % layers]) else window
-            if ev is not None:
-                ev[i][0].record(stream)
             am.kernels.attention(views[i], q[i], dk ** -0.5, kv_len, N, causal=(L > 1),
                                  window=wl, out=out[i], mode="prefill" if L > 1 else "decode")
-            if ev is not None:
-                ev[i][1].record(stream)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
+    # The whole step (every layer / instance) is captured in one CUDA graph, as a serving
+    # loop would run it, so the time is device time rather than Python launch overhead.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize(dev)
     clocks = ClockSampler(dev.index)
     clocks.start()
-    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
-            for _ in range(inst)] for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed")
     t0.record(stream)
-    for s in range(args.steps):
-        step(evs[s])
+    for _ in range(args.steps):
+        graph.replay()
     t1.record(stream)
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize(dev)
     clk = clocks.stop()
-    ms = t0.elapsed_time(t1) / args.steps / reps
+    step_ms = t0.elapsed_time(t1) / args.steps
+    ms = step_ms / reps
     if world > 1:
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
-    launch_ms = float(np.mean([evs[s][i][0].elapsed_time(evs[s][i][1])
-                               for s in range(args.steps) for i in range(inst)]))
+    launch_ms = step_ms / inst  # graph nodes run back to back: mean time per attention call
     hbm, tf_burst, tf_sus, kind = peaks()
     per_tok = q4_bytes_per_token(hkv, dk, dv)
     if L == 1:
@@ -424,7 +426,8 @@ def run_single_workload(args, am, dev, rank, world):
             "config": {"workload": w, "batch": B, "layers": layers, "context": N, "q_len": L,
                        "n_q_heads": hq, "n_kv_heads": hkv, "k_dim": dk, "v_dim": dv,
                        "window": window, "parallelism": f"replicas x{world}",
-                       "l2": f"{reps} rotating instances" if reps > 1 else "inputs larger than L2"},
+                       "l2": f"{reps} rotating instances" if reps > 1 else "inputs larger than L2",
+                       "timing": "whole step in one CUDA graph; per-call time = step / calls"},
             "roofline": roof, "gpu_launches": args.steps * inst * (1 if L > 1 else 2),
             "clocks": clk}))
 
