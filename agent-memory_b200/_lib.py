@@ -125,6 +125,8 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     global _lib
     if _lib is not None and path is None:
         return _lib
+    if path is None and os.environ.get("AM_Q4_LIB"):
+        path = os.environ["AM_Q4_LIB"]  # an alternative build of the same library
     p = Path(path) if path is not None else LIB_PATH
     if not p.exists():
         raise Q4KernelUnavailable(
@@ -164,8 +166,7 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     ver = lib.am_abi_version()
     if ver != ABI_VERSION:
         raise Q4KernelUnavailable(f"{p} has ABI version {ver}, expected {ABI_VERSION}")
-    if path is None:
-        _lib = lib
+    _lib = lib
     return lib
 
 

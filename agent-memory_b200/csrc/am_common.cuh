@@ -209,6 +209,7 @@ struct DecodeParams {
   int32_t q_len;
   int32_t n_rep;
   int32_t rows_per_head;  // n_rep * q_len
+  int32_t heads_per_cta;  // KV heads packed into one CTA's 8 MMA columns (decode)
   int32_t q_bf16;
   const uint16_t* q;
   int64_t qsb, qsh, qsl;

@@ -34,30 +34,33 @@
 namespace am {
 
 constexpr int kWarps = 4;
-constexpr int kStage = 32;                 // tokens per pipeline stage (two 16-token MMA tiles)
 constexpr int kMaxChunk = 2048;            // tokens per CTA chunk (decode_plan never exceeds it)
 constexpr int kMaxBlk = kMaxChunk / 32 + 2;  // block ids a chunk can touch (block_tokens >= 32)
 constexpr float kMaskedFinite = -1.0e30f;  // boolean-mask fill (finite: keeps uniform rows)
 
-template <int DK, int DV, int NS>
+template <int DK, int DV, int NS, int HP, int TS>
 struct DecodeLayout {
   static constexpr int NGK = DK / 64, NGV = DV / 64;
   static constexpr int KW = DK / 8, VW = DV / 8;
   static constexpr int KROW = DK / 2, VROW = DV / 2;  // bytes of codes per token row
-  // one stage: codes and scales of kStage rows, exactly as laid out in global memory
-  static constexpr int OFF_V = kStage * KROW;
-  static constexpr int OFF_KS = OFF_V + kStage * VROW;
-  static constexpr int OFF_KB = OFF_KS + kStage * NGK * 2;
-  static constexpr int OFF_VS = OFF_KB + kStage * NGK * 2;
-  static constexpr int OFF_VB = OFF_VS + kStage * NGV * 2;
-  static constexpr int STAGE = (OFF_VB + kStage * NGV * 2 + 127) / 128 * 128;
+  // one head's share of a stage: codes and scales of TS rows as laid out in HBM
+  static constexpr int H_OFF_V = TS * KROW;
+  static constexpr int H_OFF_KS = H_OFF_V + TS * VROW;
+  static constexpr int H_OFF_KB = H_OFF_KS + TS * NGK * 2;
+  static constexpr int H_OFF_VS = H_OFF_KB + TS * NGK * 2;
+  static constexpr int H_OFF_VB = H_OFF_VS + TS * NGV * 2;
+  static constexpr int HB = (H_OFF_VB + TS * NGV * 2 + 15) / 16 * 16;
+  static constexpr int STAGE = (HP * HB + 127) / 128 * 128;
   static constexpr int RING = NS * STAGE;
   static constexpr int OFF_BAR = kWarps * RING;
   static constexpr int OFF_OK = OFF_BAR + kWarps * NS * 8;
-  static constexpr int OFF_Q = (OFF_OK + kWarps * NS * 4 + 15) / 16 * 16;
-  static constexpr int OFF_QS = OFF_Q + 8 * DK * 4;
-  static constexpr int OFF_BLK = OFF_QS + 2 * 8 * NGK * 4;
+  static constexpr int OFF_BLK = OFF_OK + kWarps * NS * 4;
   static constexpr int SMEM = OFF_BLK + kMaxBlk * 4;
+  // The queries are staged (as their 16-bit inputs, plus per-group sums and maxima) in the
+  // last stage of warp 0's ring, which no copy touches before the main loop starts.
+  static constexpr int OFF_Q = (NS - 1) * STAGE;
+  static constexpr int OFF_QS = OFF_Q + 8 * DK * 2;
+  static_assert(8 * DK * 2 + 2 * 8 * NGK * 4 <= STAGE, "query staging must fit in one stage");
   static_assert(8 * (DV + 2) * 4 <= RING, "warp result must fit in its ring");
 };
 
@@ -86,12 +89,40 @@ __device__ __forceinline__ float load_mask(const DecodeParams& p, int b, int hq,
   return h2f_rt(static_cast<const uint16_t*>(p.mask)[idx], p.mask_dtype == AM_DTYPE_BF16);
 }
 
-template <int DK, int DV, bool SBF16, bool PAGED, int NS>
+// Column c (0..7) of the CTA's MMA N dimension -> (head offset within the CTA's head group,
+// row within that head).  With HP > 1 the rows of HP KV heads share the 8 columns.
+struct ColMap {
+  int hp, rr;
+  bool valid;
+};
+
+__device__ __forceinline__ ColMap col_map(int c, int hp_n, int rph, int rg) {
+  ColMap m;
+  if (hp_n > 1) {
+    m.hp = c / rph;
+    m.rr = c % rph;
+    m.valid = c < hp_n * rph;
+    if (!m.valid) {
+      m.hp = hp_n - 1;
+      m.rr = rph - 1;
+    }
+  } else {
+    m.hp = 0;
+    m.rr = rg * 8 + c;
+    m.valid = m.rr < rph;
+    if (!m.valid) m.rr = rph - 1;
+  }
+  return m;
+}
+
+template <int DK, int DV, bool SBF16, bool PAGED, int NS, int HP, int TS>
 __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
-  using LY = DecodeLayout<DK, DV, NS>;
+  using LY = DecodeLayout<DK, DV, NS, HP, TS>;
+  constexpr int NH = TS / 16;  // 16-token MMA tiles per stage
   constexpr int NGK = LY::NGK, NGV = LY::NGV;
   constexpr int KW = LY::KW, VW = LY::VW;
   constexpr int KROW = LY::KROW, VROW = LY::VROW;
+  constexpr int HB = LY::HB;
   constexpr int KSTEPS = DK / 16;
   constexpr int MT = DV / 16;
 
@@ -101,10 +132,11 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int b = blockIdx.z;
-  const int row_groups = gridDim.y / p.hkv;
-  const int h = blockIdx.y / row_groups;
+  const int row_groups = gridDim.y / (p.hkv / HP);
+  const int h0 = (blockIdx.y / row_groups) * HP;
   const int rg = blockIdx.y % row_groups;
   const int chunk = blockIdx.x;
+  const int rph = p.rows_per_head;
 
   const int n = p.kv_len[b];
   const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
@@ -116,7 +148,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   if (chunk >= n_chunks_b) return;
   const int c_lo = lo + chunk * p.chunk;
   const int c_hi = min(c_lo + p.chunk, hi);
-  const int n_stages = c_hi > c_lo ? (c_hi - c_lo + kStage - 1) / kStage : 0;
+  const int n_stages = c_hi > c_lo ? (c_hi - c_lo + TS - 1) / TS : 0;
   const int my_stages = n_stages > warp ? (n_stages - warp + kWarps - 1) / kWarps : 0;
 
   uint8_t* ring = smem + warp * LY::RING;
@@ -146,23 +178,25 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   }
   __syncthreads();
 
-  // Lane 0 of each warp fills its ring: one stage = kStage rows of K/V codes and scales,
-  // six 1-D bulk copies completing on the stage's mbarrier.
+  // Lane 0 of each warp fills its ring: a stage = TS rows of K/V codes and scales of
+  // each of the HP heads, six 1-D bulk copies per head completing on the stage's mbarrier.
   auto issue = [&](int k) {
     if (k >= my_stages) return;
     const int s = k % NS;
-    const int t0 = c_lo + (warp + kWarps * k) * kStage;
-    int64_t row0;
+    const int t0 = c_lo + (warp + kWarps * k) * TS;
+    int64_t row0, head_stride;
     int nrows;
     bool ok = true;
     if constexpr (PAGED) {
       const int32_t v = sblk[(t0 >> p.bt_shift) - blk0];
       ok = v >= 0;
-      row0 = ((((int64_t)(ok ? v : 0)) * p.hkv + h) << p.bt_shift) + (t0 & (p.block_tokens - 1));
-      nrows = kStage;
+      row0 = ((((int64_t)(ok ? v : 0)) * p.hkv + h0) << p.bt_shift) + (t0 & (p.block_tokens - 1));
+      head_stride = p.block_tokens;
+      nrows = TS;
     } else {
-      row0 = ((int64_t)b * p.hkv + h) * p.capacity + t0;
-      nrows = min((int64_t)kStage, p.capacity - t0) >= kStage ? kStage : 16;
+      row0 = ((int64_t)b * p.hkv + h0) * p.capacity + t0;
+      head_stride = p.capacity;
+      nrows = p.capacity - t0 >= TS ? TS : 16;
     }
     tile_ok[s] = ok ? 1 : 0;
     const uint32_t bar = smem_u32(&bars[s]);
@@ -171,14 +205,18 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       return;
     }
     const uint32_t bytes = nrows * (KROW + VROW + 4 * NGK + 4 * NGV);
-    mbar_arrive_expect_tx(bar, bytes);
-    uint8_t* stg = ring + s * LY::STAGE;
-    bulk_g2s(stg, p.kc + row0 * KW, nrows * KROW, bar);
-    bulk_g2s(stg + LY::OFF_V, p.vc + row0 * VW, nrows * VROW, bar);
-    bulk_g2s(stg + LY::OFF_KS, p.ks + row0 * NGK, nrows * NGK * 2, bar);
-    bulk_g2s(stg + LY::OFF_KB, p.kb + row0 * NGK, nrows * NGK * 2, bar);
-    bulk_g2s(stg + LY::OFF_VS, p.vs + row0 * NGV, nrows * NGV * 2, bar);
-    bulk_g2s(stg + LY::OFF_VB, p.vb + row0 * NGV, nrows * NGV * 2, bar);
+    mbar_arrive_expect_tx(bar, HP * bytes);
+#pragma unroll
+    for (int hp = 0; hp < HP; ++hp) {
+      const int64_t r0 = row0 + hp * head_stride;
+      uint8_t* stg = ring + s * LY::STAGE + hp * HB;
+      bulk_g2s(stg, p.kc + r0 * KW, nrows * KROW, bar);
+      bulk_g2s(stg + LY::H_OFF_V, p.vc + r0 * VW, nrows * VROW, bar);
+      bulk_g2s(stg + LY::H_OFF_KS, p.ks + r0 * NGK, nrows * NGK * 2, bar);
+      bulk_g2s(stg + LY::H_OFF_KB, p.kb + r0 * NGK, nrows * NGK * 2, bar);
+      bulk_g2s(stg + LY::H_OFF_VS, p.vs + r0 * NGV, nrows * NGV * 2, bar);
+      bulk_g2s(stg + LY::H_OFF_VB, p.vb + r0 * NGV, nrows * NGV * 2, bar);
+    }
   };
   if (lane == 0) {
 #pragma unroll
@@ -186,36 +224,28 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   }
 
   // ------------------------------------------------------------------ stage queries
-  float* qs = reinterpret_cast<float*>(smem + LY::OFF_Q);    // [8][DK]
-  float* qsum_s = reinterpret_cast<float*>(smem + LY::OFF_QS);  // [8][NGK]
-  float* qmax_s = qsum_s + 8 * NGK;                            // [8][NGK]
+  const bool qbf = p.q_bf16 != 0;
+  uint16_t* qs = reinterpret_cast<uint16_t*>(smem + LY::OFF_Q);  // [8 columns][DK] raw inputs
+  float* qsum_s = reinterpret_cast<float*>(smem + LY::OFF_QS);    // [8][NGK]
+  float* qmax_s = qsum_s + 8 * NGK;                               // [8][NGK]
   for (int i = tid; i < 8 * (DK / 8); i += 128) {
-    const int r = i / (DK / 8), c8 = i % (DK / 8);
-    const int rr = rg * 8 + r;
-    float v[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = 0.0f;
-    if (rr < p.rows_per_head) {
-      const int l = rr / p.n_rep;
-      const int hq = h * p.n_rep + rr % p.n_rep;
+    const int c = i / (DK / 8), c8 = i % (DK / 8);
+    const ColMap cm = col_map(c, HP, rph, rg);
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (cm.valid) {
+      const int l = cm.rr / p.n_rep;
+      const int hq = (h0 + cm.hp) * p.n_rep + cm.rr % p.n_rep;
       const uint16_t* src = p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl + c8 * 8;
-      const uint4 raw = *reinterpret_cast<const uint4*>(src);
-      const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        v[2 * e] = h2f_rt(static_cast<uint16_t>(u[e] & 0xffffu), p.q_bf16 != 0);
-        v[2 * e + 1] = h2f_rt(static_cast<uint16_t>(u[e] >> 16), p.q_bf16 != 0);
-      }
+      raw = *reinterpret_cast<const uint4*>(src);
     }
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qs[r * DK + c8 * 8 + e] = v[e];
+    *reinterpret_cast<uint4*>(qs + c * DK + c8 * 8) = raw;
   }
   __syncthreads();
   if (tid < 8 * NGK) {
     const int r = tid / NGK, G = tid % NGK;
     float sm = 0.0f, mx = 0.0f;
     for (int d = 0; d < 64; ++d) {
-      const float v = qs[r * DK + G * 64 + d];
+      const float v = h2f_rt(qs[r * DK + G * 64 + d], qbf);
       sm += v;
       mx = fmaxf(mx, fabsf(v));
     }
@@ -224,24 +254,27 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   }
   __syncthreads();
 
-  // Per-row power-of-two prescale so fp16 MMA operands keep full precision (bf16 queries).
-  auto row_pow2 = [&](int r) -> float {
+  // Per-column power-of-two prescale so fp16 MMA operands keep full precision (bf16 queries).
+  auto col_pow2 = [&](int c) -> float {
     float m = 0.0f;
 #pragma unroll
-    for (int G = 0; G < NGK; ++G) m = fmaxf(m, qmax_s[r * NGK + G]);
+    for (int G = 0; G < NGK; ++G) m = fmaxf(m, qmax_s[c * NGK + G]);
     if (!(m > 0.0f) || !isfinite(m)) return 1.0f;
     int e;
     frexpf(m, &e);  // m in [2^(e-1), 2^e)
     return ldexpf(1.0f, 15 - e);
   };
 
-  // B fragments of Q for S = K . Q^T (row g = CTA query row g).  k-step s = 4G + 2j + e
-  // covers words 8G + 2t + j of this thread's column t; nibbles (2e, 2e+4) feed k-slots
-  // 2t, 2t+1 and nibbles (2e+1, 2e+5) feed 2t+8, 2t+9 (pre-divided by 16).
-  uint32_t qf[KSTEPS][2];
+  // B fragments of Q for S = K . Q^T, one set per packed head: this thread's column g keeps
+  // its query only in the set of its own head (zeros elsewhere), so the MMAs of head hp fill
+  // exactly head hp's columns of the shared accumulator.  k-step s = 4G + 2j + e covers
+  // words 8G + 2t + j of column t's slots; nibbles (2e, 2e+4) feed k-slots 2t, 2t+1 and
+  // nibbles (2e+1, 2e+5) feed 2t+8, 2t+9 (pre-divided by 16).
+  uint32_t qf[HP][KSTEPS][2];
   {
-    const float pw = row_pow2(g);
-    const float* qr = qs + g * DK;
+    const ColMap cm = col_map(g, HP, rph, rg);
+    const float pw = col_pow2(g);
+    const uint16_t* qr = qs + g * DK;
 #pragma unroll
     for (int G = 0; G < NGK; ++G) {
 #pragma unroll
@@ -250,38 +283,48 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
         for (int e = 0; e < 2; ++e) {
           const int s = 4 * G + 2 * j + e;
           const int w = 8 * G + 2 * t + j;
-          const float* q8 = qr + 8 * w + 2 * e;
-          qf[s][0] = pack_half2(q8[0] * pw, q8[4] * pw);
-          qf[s][1] = pack_half2(q8[1] * pw * 0.0625f, q8[5] * pw * 0.0625f);
+          const uint16_t* q8 = qr + 8 * w + 2 * e;
+          const uint32_t b0 = pack_half2(h2f_rt(q8[0], qbf) * pw, h2f_rt(q8[4], qbf) * pw);
+          const uint32_t b1 = pack_half2(h2f_rt(q8[1], qbf) * pw * 0.0625f,
+                                         h2f_rt(q8[5], qbf) * pw * 0.0625f);
+#pragma unroll
+          for (int hp = 0; hp < HP; ++hp) {
+            qf[hp][s][0] = hp == cm.hp ? b0 : 0u;
+            qf[hp][s][1] = hp == cm.hp ? b1 : 0u;
+          }
         }
       }
     }
   }
-  // Per-column (query row 2t, 2t+1) constants.
+  // Per-column (2t, 2t+1) constants.
   float fac[2], qb[2][NGK];
-  int pos_c[2], l_c[2], hq_c[2];
+  int pos_c[2], l_c[2], hq_c[2], hb_c[2];
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
-    const int r = 2 * t + c;
-    const float pw = row_pow2(r);
+    const int col = 2 * t + c;
+    const ColMap cm = col_map(col, HP, rph, rg);
+    const float pw = col_pow2(col);
     fac[c] = 16777216.0f / pw * p.scale_log2;  // 2^24 undoes the subnormal code encoding
 #pragma unroll
-    for (int G = 0; G < NGK; ++G) qb[c][G] = qsum_s[r * NGK + G] * p.scale_log2;
-    const int rr = rg * 8 + r;
-    const int rrc = rr < p.rows_per_head ? rr : p.rows_per_head - 1;
-    l_c[c] = rrc / p.n_rep;
-    hq_c[c] = h * p.n_rep + rrc % p.n_rep;
+    for (int G = 0; G < NGK; ++G) qb[c][G] = qsum_s[col * NGK + G] * p.scale_log2;
+    l_c[c] = cm.rr / p.n_rep;
+    hq_c[c] = (h0 + cm.hp) * p.n_rep + cm.rr % p.n_rep;
     pos_c[c] = n - p.q_len + l_c[c];
+    hb_c[c] = cm.hp * HB;
   }
+  const int my_hp_g = col_map(g, HP, rph, rg).hp;  // head of this thread's B column after movmatrix
+  const bool pair_same = HP == 1 || (rph % 2) == 0;  // columns 2t and 2t+1 belong to one head
   // Stages entirely inside [mask_lo, mask_hi) need no per-element masking.
   int mask_lo, mask_hi;
   {
-    const int r1 = min(rg * 8 + 7, p.rows_per_head - 1);
-    const int pos_min = n - p.q_len + (rg * 8) / p.n_rep;
-    const int pos_max = n - p.q_len + r1 / p.n_rep;
+    const int rows_here = HP > 1 ? rph : min(8, rph - rg * 8);
+    const int rr0 = HP > 1 ? 0 : rg * 8;
+    const int pos_min = n - p.q_len + rr0 / p.n_rep;
+    const int pos_max = n - p.q_len + (rr0 + rows_here - 1) / p.n_rep;
     mask_lo = max(st, p.window > 0 ? pos_max - p.window + 1 : 0);
     mask_hi = p.causal ? min(n, pos_min + 1) : n;
   }
+  __syncthreads();  // every warp is done with the staged queries before warp 0 refills that stage
 
   // ------------------------------------------------------------------ streaming loop
   float o[MT][4];
@@ -308,71 +351,105 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     }
     consumed = k + 1;
     const uint8_t* stg = ring + s * LY::STAGE;
-    const int t0 = c_lo + (warp + kWarps * k) * kStage;
+    const int t0 = c_lo + (warp + kWarps * k) * TS;
     const bool ok = tile_ok[s] != 0;
 
-    // ---- S = K . Q^T for the two 16-token halves (independent accumulator chains) ----
-    float acc[2][NGK][4];
+    // ---- S = K . Q^T for the two 16-token halves, all packed heads into one accumulator ----
+    // one accumulator set per packed head keeps each MMA dependency chain 4 deep; head hp's
+    // MMAs only fill head hp's columns, so the sets are summed afterwards
+    float acch[HP][NH][NGK][4];
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh)
+    for (int hp = 0; hp < HP; ++hp)
 #pragma unroll
-      for (int G = 0; G < NGK; ++G) acc[hh][G][0] = acc[hh][G][1] = acc[hh][G][2] = acc[hh][G][3] = 0.0f;
+      for (int hh = 0; hh < NH; ++hh)
 #pragma unroll
-    for (int G = 0; G < NGK; ++G) {
-      uint2 wa[2], wb[2];
+        for (int G = 0; G < NGK; ++G)
+          acch[hp][hh][G][0] = acch[hp][hh][G][1] = acch[hp][hh][G][2] = acch[hp][hh][G][3] = 0.0f;
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        wa[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g) * KROW + G * 32 + t * 8);
-        wb[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g + 8) * KROW + G * 32 + t * 8);
-      }
+    for (int hp = 0; hp < HP; ++hp) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        uint32_t xa[2], xb[2];
+      for (int G = 0; G < NGK; ++G) {
+        uint2 wa[NH], wb[NH];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          xa[hh] = j ? wa[hh].y : wa[hh].x;
-          xb[hh] = j ? wb[hh].y : wb[hh].x;
+        for (int hh = 0; hh < NH; ++hh) {
+          wa[hh] = *reinterpret_cast<const uint2*>(stg + hp * HB + (hh * 16 + g) * KROW + G * 32 + t * 8);
+          wb[hh] = *reinterpret_cast<const uint2*>(stg + hp * HB + (hh * 16 + g + 8) * KROW + G * 32 + t * 8);
         }
-        const int s0 = 4 * G + 2 * j;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh)
-          mma_f16_16816(acc[hh][G], xa[hh] & 0x000F000Fu, xb[hh] & 0x000F000Fu,
-                        xa[hh] & 0x00F000F0u, xb[hh] & 0x00F000F0u, qf[s0][0], qf[s0][1]);
+        for (int j = 0; j < 2; ++j) {
+          uint32_t xa[NH], xb[NH];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          xa[hh] >>= 8;
-          xb[hh] >>= 8;
-          mma_f16_16816(acc[hh][G], xa[hh] & 0x000F000Fu, xb[hh] & 0x000F000Fu,
-                        xa[hh] & 0x00F000F0u, xb[hh] & 0x00F000F0u, qf[s0 + 1][0], qf[s0 + 1][1]);
+          for (int hh = 0; hh < NH; ++hh) {
+            xa[hh] = j ? wa[hh].y : wa[hh].x;
+            xb[hh] = j ? wb[hh].y : wb[hh].x;
+          }
+          const int s0 = 4 * G + 2 * j;
+#pragma unroll
+          for (int hh = 0; hh < NH; ++hh)
+            mma_f16_16816(acch[hp][hh][G], xa[hh] & 0x000F000Fu, xb[hh] & 0x000F000Fu,
+                          xa[hh] & 0x00F000F0u, xb[hh] & 0x00F000F0u, qf[hp][s0][0], qf[hp][s0][1]);
+#pragma unroll
+          for (int hh = 0; hh < NH; ++hh) {
+            xa[hh] >>= 8;
+            xb[hh] >>= 8;
+            mma_f16_16816(acch[hp][hh][G], xa[hh] & 0x000F000Fu, xb[hh] & 0x000F000Fu,
+                          xa[hh] & 0x00F000F0u, xb[hh] & 0x00F000F0u, qf[hp][s0 + 1][0],
+                          qf[hp][s0 + 1][1]);
+          }
         }
       }
     }
-    // scores in log2 units: s2[hh][e] -> token hh*16 + g + 8*(e>>1), column 2t + (e&1)
-    float s2[2][4];
+    float acc[NH][NGK][4];
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float sk[2][NGK], bk[2][NGK];
-      load_scales<NGK>(stg + LY::OFF_KS, hh * 16 + g, sk[0], SBF16);
-      load_scales<NGK>(stg + LY::OFF_KS, hh * 16 + g + 8, sk[1], SBF16);
-      load_scales<NGK>(stg + LY::OFF_KB, hh * 16 + g, bk[0], SBF16);
-      load_scales<NGK>(stg + LY::OFF_KB, hh * 16 + g + 8, bk[1], SBF16);
+    for (int hh = 0; hh < NH; ++hh)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int tr = e >> 1, c = e & 1;
-        float x = 0.0f, y = 0.0f;
+      for (int G = 0; G < NGK; ++G)
 #pragma unroll
-        for (int G = 0; G < NGK; ++G) {
-          x = fmaf(sk[tr][G], acc[hh][G][e], x);
-          y = fmaf(bk[tr][G], qb[c][G], y);
+        for (int e = 0; e < 4; ++e) {
+          float a = acch[0][hh][G][e];
+#pragma unroll
+          for (int hp = 1; hp < HP; ++hp) a += acch[hp][hh][G][e];
+          acc[hh][G][e] = a;
         }
-        s2[hh][e] = fmaf(x, fac[c], y);
+    // scores in log2 units: s2[hh][e] -> token hh*16 + g + 8*(e>>1), column 2t + (e&1); the
+    // group scale and bias come from the head of the element's column (one head for both
+    // columns of a thread unless heads hold a single query row each)
+    float s2[NH][4];
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+#pragma unroll
+      for (int tr = 0; tr < 2; ++tr) {
+        float sk[2][NGK], bk[2][NGK];
+        load_scales<NGK>(stg + hb_c[0] + LY::H_OFF_KS, hh * 16 + g + 8 * tr, sk[0], SBF16);
+        load_scales<NGK>(stg + hb_c[0] + LY::H_OFF_KB, hh * 16 + g + 8 * tr, bk[0], SBF16);
+        if (pair_same) {
+#pragma unroll
+          for (int G = 0; G < NGK; ++G) {
+            sk[1][G] = sk[0][G];
+            bk[1][G] = bk[0][G];
+          }
+        } else {
+          load_scales<NGK>(stg + hb_c[1] + LY::H_OFF_KS, hh * 16 + g + 8 * tr, sk[1], SBF16);
+          load_scales<NGK>(stg + hb_c[1] + LY::H_OFF_KB, hh * 16 + g + 8 * tr, bk[1], SBF16);
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int e = 2 * tr + c;
+          float x = 0.0f, y = 0.0f;
+#pragma unroll
+          for (int G = 0; G < NGK; ++G) {
+            x = fmaf(sk[c][G], acc[hh][G][e], x);
+            y = fmaf(bk[c][G], qb[c][G], y);
+          }
+          s2[hh][e] = fmaf(x, fac[c], y);
+        }
       }
     }
     // ---- masking (only stages that touch a boundary) ----
-    const bool masked_stage = !ok || dense_mask || t0 < mask_lo || t0 + kStage > mask_hi;
+    const bool masked_stage = !ok || dense_mask || t0 < mask_lo || t0 + TS > mask_hi;
     if (masked_stage) {
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
+      for (int hh = 0; hh < NH; ++hh) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int tok = t0 + hh * 16 + g + 8 * (e >> 1);
@@ -394,8 +471,12 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       }
     }
     // ---- online softmax (per column, over the 32 tokens of the stage) ----
-    float mt[2] = {fmaxf(fmaxf(s2[0][0], s2[0][2]), fmaxf(s2[1][0], s2[1][2])),
-                   fmaxf(fmaxf(s2[0][1], s2[0][3]), fmaxf(s2[1][1], s2[1][3]))};
+    float mt[2] = {fmaxf(s2[0][0], s2[0][2]), fmaxf(s2[0][1], s2[0][3])};
+#pragma unroll
+    for (int hh = 1; hh < NH; ++hh) {
+      mt[0] = fmaxf(mt[0], fmaxf(s2[hh][0], s2[hh][2]));
+      mt[1] = fmaxf(mt[1], fmaxf(s2[hh][1], s2[hh][3]));
+    }
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       mt[c] = fmaxf(mt[c], __shfl_xor_sync(0xffffffffu, mt[c], 4));
@@ -426,9 +507,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     const float ms0 = m_run[0] == -INFINITY ? 0.0f : m_run[0];
     const float ms1 = m_run[1] == -INFINITY ? 0.0f : m_run[1];
 
-    // ---- O^T += V^T . (P * scale_v), one k16 step per half ----
+    // ---- O^T += V^T . (P * scale_v): per half, one B operand per packed head ----
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
+    for (int hh = 0; hh < NH; ++hh) {
       float pr[4];
       pr[0] = ex2(s2[hh][0] - ms0);
       pr[1] = ex2(s2[hh][1] - ms1);
@@ -436,43 +517,62 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       pr[3] = ex2(s2[hh][3] - ms1);
       l_run[0] += pr[0] + pr[2];
       l_run[1] += pr[1] + pr[3];
-      float sv[2][NGV], bv[2][NGV];
-      load_scales<NGV>(stg + LY::OFF_VS, hh * 16 + g, sv[0], SBF16);
-      load_scales<NGV>(stg + LY::OFF_VS, hh * 16 + g + 8, sv[1], SBF16);
-      load_scales<NGV>(stg + LY::OFF_VB, hh * 16 + g, bv[0], SBF16);
-      load_scales<NGV>(stg + LY::OFF_VB, hh * 16 + g + 8, bv[1], SBF16);
+      // sv[tr][c][G] / bv: scale / bias of the element's token row (g + 8 tr) and column head
+      float sv[2][2][NGV], bv[2][2][NGV];
+#pragma unroll
+      for (int tr = 0; tr < 2; ++tr) {
+        load_scales<NGV>(stg + hb_c[0] + LY::H_OFF_VS, hh * 16 + g + 8 * tr, sv[tr][0], SBF16);
+        load_scales<NGV>(stg + hb_c[0] + LY::H_OFF_VB, hh * 16 + g + 8 * tr, bv[tr][0], SBF16);
+        if (pair_same) {
+#pragma unroll
+          for (int G = 0; G < NGV; ++G) {
+            sv[tr][1][G] = sv[tr][0][G];
+            bv[tr][1][G] = bv[tr][0][G];
+          }
+        } else {
+          load_scales<NGV>(stg + hb_c[1] + LY::H_OFF_VS, hh * 16 + g + 8 * tr, sv[tr][1], SBF16);
+          load_scales<NGV>(stg + hb_c[1] + LY::H_OFF_VB, hh * 16 + g + 8 * tr, bv[tr][1], SBF16);
+        }
+      }
       if (masked_stage) {
         // rows of excluded keys may hold stale shared memory (not loaded, or beyond the
         // written length): zero their scale and bias so p = 0 cannot meet a NaN
 #pragma unroll
-        for (int tr = 0; tr < 2; ++tr) {
-          const bool live = pr[2 * tr] > 0.0f || pr[2 * tr + 1] > 0.0f;
+        for (int tr = 0; tr < 2; ++tr)
 #pragma unroll
-          for (int G = 0; G < NGV; ++G) {
-            sv[tr][G] = live ? sv[tr][G] : 0.0f;
-            bv[tr][G] = live ? bv[tr][G] : 0.0f;
+          for (int c = 0; c < 2; ++c) {
+            const bool live = pr[2 * tr + c] > 0.0f;
+#pragma unroll
+            for (int G = 0; G < NGV; ++G) {
+              sv[tr][c][G] = live ? sv[tr][c][G] : 0.0f;
+              bv[tr][c][G] = live ? bv[tr][c][G] : 0.0f;
+            }
           }
-        }
       }
-      const uint8_t* vbase = stg + LY::OFF_V + hh * 16 * VROW;
 #pragma unroll
       for (int G = 0; G < NGV; ++G) {
-        vbias[0][G] = fmaf(pr[0], bv[0][G], fmaf(pr[2], bv[1][G], vbias[0][G]));
-        vbias[1][G] = fmaf(pr[1], bv[0][G], fmaf(pr[3], bv[1][G], vbias[1][G]));
-        const uint32_t blo = movmatrix_trans(pack_half2(pr[0] * sv[0][G], pr[1] * sv[0][G]));
-        const uint32_t bhi = movmatrix_trans(pack_half2(pr[2] * sv[1][G], pr[3] * sv[1][G]));
-        const int woff = (8 * G + g) * 4;
-        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * VROW + woff);
-        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * VROW + woff);
-        const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * VROW + woff);
-        const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * VROW + woff);
+        vbias[0][G] = fmaf(pr[0], bv[0][0][G], fmaf(pr[2], bv[1][0][G], vbias[0][G]));
+        vbias[1][G] = fmaf(pr[1], bv[0][1][G], fmaf(pr[3], bv[1][1][G], vbias[1][G]));
+        const uint32_t blo = movmatrix_trans(pack_half2(pr[0] * sv[0][0][G], pr[1] * sv[0][1][G]));
+        const uint32_t bhi = movmatrix_trans(pack_half2(pr[2] * sv[1][0][G], pr[3] * sv[1][1][G]));
 #pragma unroll
-        for (int beta = 0; beta < 4; ++beta) {
-          const uint32_t sel = beta | ((4 + beta) << 8);
-          const uint32_t r01 = __byte_perm(v0, v1, sel);
-          const uint32_t r23 = __byte_perm(v2, v3, sel);
-          mma_f16_16816(o[4 * G + beta], r01 & 0x000F000Fu, r01 & 0x00F000F0u, r23 & 0x000F000Fu,
-                        r23 & 0x00F000F0u, blo, bhi);
+        for (int hp = 0; hp < HP; ++hp) {
+          const uint32_t bl = (HP == 1 || hp == my_hp_g) ? blo : 0u;
+          const uint32_t bh = (HP == 1 || hp == my_hp_g) ? bhi : 0u;
+          const uint8_t* vbase = stg + hp * HB + LY::H_OFF_V + hh * 16 * VROW;
+          const int woff = (8 * G + g) * 4;
+          const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * VROW + woff);
+          const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * VROW + woff);
+          const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * VROW + woff);
+          const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * VROW + woff);
+#pragma unroll
+          for (int beta = 0; beta < 4; ++beta) {
+            const uint32_t sel = beta | ((4 + beta) << 8);
+            const uint32_t r01 = __byte_perm(v0, v1, sel);
+            const uint32_t r23 = __byte_perm(v2, v3, sel);
+            mma_f16_16816(o[4 * G + beta], r01 & 0x000F000Fu, r01 & 0x00F000F0u, r23 & 0x000F000Fu,
+                          r23 & 0x00F000F0u, bl, bh);
+          }
         }
       }
     }
@@ -523,23 +623,23 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   // ------------------------------------------------------------------ CTA combine
   const int rows_total = p.hq * p.q_len;
   for (int i = tid; i < 8 * DV; i += 128) {
-    const int r = i / DV, d = i % DV;
-    const int rr = rg * 8 + r;
-    if (rr >= p.rows_per_head) continue;
+    const int c = i / DV, d = i % DV;
+    const ColMap cm = col_map(c, HP, rph, rg);
+    if (!cm.valid) continue;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, reinterpret_cast<const float*>(smem + w * LY::RING)[r]);
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, reinterpret_cast<const float*>(smem + w * LY::RING)[c]);
     float L = 0.0f, O = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
       const float* wr = reinterpret_cast<const float*>(smem + w * LY::RING);
-      const float mw = wr[r];
+      const float mw = wr[c];
       const float sc = (mw == -INFINITY) ? 0.0f : ex2(mw - M);
-      L = fmaf(wr[8 + r], sc, L);
-      O = fmaf(wr[16 + r * DV + d], sc, O);
+      L = fmaf(wr[8 + c], sc, L);
+      O = fmaf(wr[16 + c * DV + d], sc, O);
     }
-    const int l = rr / p.n_rep;
-    const int hq = h * p.n_rep + rr % p.n_rep;
+    const int l = cm.rr / p.n_rep;
+    const int hq = (h0 + cm.hp) * p.n_rep + cm.rr % p.n_rep;
     if (n_chunks_b == 1) {
       const float val = L > 0.0f ? O / L : 0.0f;
       store_out(p.out, (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + d, val,
@@ -624,19 +724,22 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int* chunk
   if (*n_chunks < 1) *n_chunks = 1;
 }
 
-template <int DK, int DV, bool SBF16, bool PAGED>
+template <int DK, int DV, bool SBF16, bool PAGED, int HP>
 static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_groups,
                                    cudaStream_t stream) {
-  constexpr int NS = DK >= 256 ? 2 : 3;
-  using LY = DecodeLayout<DK, DV, NS>;
-  auto kfn = decode_kernel<DK, DV, SBF16, PAGED, NS>;
+  // 32-token stages for one head; 16-token stages when several heads share the CTA, so a
+  // stage stays ~5 KB and three stages per warp fit three CTAs per SM
+  constexpr int TS = HP > 1 ? 16 : 32;
+  constexpr int NS = DecodeLayout<DK, DV, 3, HP, TS>::STAGE <= 6144 ? 3 : 2;
+  using LY = DecodeLayout<DK, DV, NS, HP, TS>;
+  auto kfn = decode_kernel<DK, DV, SBF16, PAGED, NS, HP, TS>;
   static bool attr_done = false;  // per instantiation; idempotent if raced
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::SMEM);
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  dim3 grid(p.max_chunks, p.hkv * row_groups, batch);
+  dim3 grid(p.max_chunks, (p.hkv / HP) * row_groups, batch);
   kfn<<<grid, 128, LY::SMEM, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -649,25 +752,46 @@ static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_gro
   return e;
 }
 
-template <int DK, int DV>
-static cudaError_t launch_decode_dims(const DecodeParams& p, int batch, int row_groups, bool paged,
-                                      bool sbf16, cudaStream_t stream) {
+template <int DK, int DV, int HP>
+static cudaError_t launch_decode_hp(const DecodeParams& p, int batch, int row_groups, bool paged,
+                                    bool sbf16, cudaStream_t stream) {
   if (paged) {
-    return sbf16 ? launch_decode_t<DK, DV, true, true>(p, batch, row_groups, stream)
-                 : launch_decode_t<DK, DV, false, true>(p, batch, row_groups, stream);
+    return sbf16 ? launch_decode_t<DK, DV, true, true, HP>(p, batch, row_groups, stream)
+                 : launch_decode_t<DK, DV, false, true, HP>(p, batch, row_groups, stream);
   }
-  return sbf16 ? launch_decode_t<DK, DV, true, false>(p, batch, row_groups, stream)
-               : launch_decode_t<DK, DV, false, false>(p, batch, row_groups, stream);
+  return sbf16 ? launch_decode_t<DK, DV, true, false, HP>(p, batch, row_groups, stream)
+               : launch_decode_t<DK, DV, false, false, HP>(p, batch, row_groups, stream);
+}
+
+#ifndef AM_DECODE_MAX_HP
+#define AM_DECODE_MAX_HP 1
+#endif
+
+int decode_max_heads_per_cta(int k_dim, int v_dim) {
+  int cap = 1;
+  if (k_dim == 64 && v_dim == 64) cap = 4;
+  if (k_dim == 128 && v_dim == 128) cap = 2;
+  if (k_dim == 192 && v_dim == 128) cap = 2;
+  return cap < AM_DECODE_MAX_HP ? cap : AM_DECODE_MAX_HP;
 }
 
 cudaError_t launch_decode(const DecodeParams& p, int batch, int row_groups, bool paged,
                           bool scale_bf16, cudaStream_t stream) {
   const int dk = p.k_dim, dv = p.v_dim;
-  if (dk == 64 && dv == 64) return launch_decode_dims<64, 64>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 128 && dv == 128) return launch_decode_dims<128, 128>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 128 && dv == 64) return launch_decode_dims<128, 64>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 192 && dv == 128) return launch_decode_dims<192, 128>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 256 && dv == 256) return launch_decode_dims<256, 256>(p, batch, row_groups, paged, scale_bf16, stream);
+#if AM_DECODE_MAX_HP > 1
+  // Packing several KV heads per CTA (built with -DAM_DECODE_MAX_HP=2/4) measured slower on
+  // B200 than one head per CTA, so the default build only instantiates heads_per_cta = 1.
+  const int hp = p.heads_per_cta;
+  if (dk == 64 && dv == 64 && hp == 4) return launch_decode_hp<64, 64, 4>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 64 && dv == 64 && hp == 2) return launch_decode_hp<64, 64, 2>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 128 && dv == 128 && hp == 2) return launch_decode_hp<128, 128, 2>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 192 && dv == 128 && hp == 2) return launch_decode_hp<192, 128, 2>(p, batch, row_groups, paged, scale_bf16, stream);
+#endif
+  if (dk == 64 && dv == 64) return launch_decode_hp<64, 64, 1>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 128 && dv == 128) return launch_decode_hp<128, 128, 1>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 128 && dv == 64) return launch_decode_hp<128, 64, 1>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 192 && dv == 128) return launch_decode_hp<192, 128, 1>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 256 && dv == 256) return launch_decode_hp<256, 256, 1>(p, batch, row_groups, paged, scale_bf16, stream);
   return cudaErrorNotSupported;
 }
 

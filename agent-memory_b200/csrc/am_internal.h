@@ -21,6 +21,7 @@ cudaError_t launch_append(const AppendParams& p, bool bf16, cudaStream_t stream)
 
 // Decode: returns cudaErrorNotSupported (without launching) for head dims without a kernel.
 bool decode_supported(int k_dim, int v_dim);
+int decode_max_heads_per_cta(int k_dim, int v_dim);
 cudaError_t launch_decode(const DecodeParams& p, int batch, int row_groups, bool paged,
                           bool scale_bf16, cudaStream_t stream);
 

@@ -107,10 +107,22 @@ def test_decode_fully_masked_row_is_uniform(cuda, orc):
     assert_close(got.float().cpu().numpy(), want, what="fully masked")
 
 
+@pytest.mark.parametrize("geom", [(16, 8, 256), (32, 8, 128), (8, 8, 64), (16, 16, 192)],
+                         ids=["gemma256", "llama128_2heads_per_cta", "mha64_4heads_per_cta", "mla192"])
 @pytest.mark.parametrize("window", [0, 64, 1024])
-def test_decode_left_padding_and_window(cuda, orc, window):
-    """Structured mask from BatchQuantizedKVCache.make_mask: left padding + sliding window."""
-    B, Hq, Hkv, N, D = 3, 16, 8, 1500, 256
+def test_decode_left_padding_and_window(cuda, orc, window, geom):
+    """Structured mask from BatchQuantizedKVCache.make_mask: left padding + sliding window,
+    for one KV head per CTA and for several KV heads packed into one CTA."""
+    Hq, Hkv, D = geom
+    B, N = 3, 1500
+    if D == 192:
+        q, kq, vq = make_case(B, Hq, Hkv, N, 192, 128, cuda=cuda, seed=window + 7)
+        lp = torch.tensor([0, 37, 700], dtype=torch.int64)
+        mask = pkg.CausalMask(1, N - 1, window if window else None, lp)
+        got = pkg.quantized_scaled_dot_product_attention(q.to(cuda), kq, vq, 192 ** -0.5, mask)
+        want = oracle(orc, q, kq, vq, 192 ** -0.5, causal=True, window=window, kv_start=lp.numpy())
+        assert_close(got.float().cpu().numpy(), want, what=f"mla left pad window={window}")
+        return
     q, kq, vq = make_case(B, Hq, Hkv, N, D, D, cuda=cuda, seed=window + 1)
     lp = torch.tensor([0, 37, 700], dtype=torch.int64)
     mask = pkg.CausalMask(1, N - 1, window if window else None, lp)
