@@ -312,7 +312,8 @@ size_t am_q4_attention_workspace_bytes(const am_q4_cache* cache, const am_attn_a
   decode_geometry(cache, args, &row_groups, &chunk, &n_chunks);
   if (n_chunks <= 1) return 0;
   const size_t rows_total = static_cast<size_t>(args->n_q_heads) * args->q_len;
-  return static_cast<size_t>(args->batch) * rows_total * n_chunks * (cache->v_dim + 2) * sizeof(float);
+  return static_cast<size_t>(args->batch) * rows_total * n_chunks * (cache->v_dim + kPartialHead) *
+         sizeof(float);
 }
 
 int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspace,

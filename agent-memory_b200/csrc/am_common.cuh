@@ -163,6 +163,19 @@ __device__ __forceinline__ void flag_status(int32_t* status, int bits) {
   if (status != nullptr) atomicOr(status, bits);
 }
 
+// Programmatic dependent launch.  griddep_wait() returns once every grid this one depends
+// on has completed and its writes are visible (immediately when the grid was launched
+// without the programmatic-serialization attribute); griddep_launch_dependents() lets the
+// next grid in the stream start its prologue early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+// Split-KV partial record of one query row and chunk: m, l, two pad words (so O starts
+// 16-byte aligned), then O[DV].
+constexpr int kPartialHead = 4;
+
 // ---------------------------------------------------------------- launch parameters
 
 // Quantize-on-append / plain quantize.  Rows are (b, h, l) triples of the source tensors.

@@ -128,6 +128,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
 
   extern __shared__ __align__(128) uint8_t smem[];
 
+  griddep_launch_dependents();
+  griddep_wait();  // everything this kernel reads or writes is ordered after the previous grid
+
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -646,8 +649,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
                 p.out_dtype);
     } else {
       float* slot = p.ws + (((int64_t)b * rows_total + (int64_t)hq * p.q_len + l) * p.max_chunks +
-                            chunk) * (DV + 2);
-      slot[2 + d] = O;
+                            chunk) * (DV + kPartialHead);
+      slot[kPartialHead + d] = O;
       if (d == 0) {
         slot[0] = M;
         slot[1] = L;
@@ -656,9 +659,17 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   }
 }
 
-// Merge the per-chunk partials of sequences split into more than one chunk.
+// Merge the per-chunk partials of sequences split into more than one chunk.  One warp per
+// query row: lanes hold the chunk maxima, the softmax weights are broadcast with shuffles
+// and every lane accumulates 16-byte column slices, so all partial loads of a row are
+// independent and in flight together.
 template <int DV>
 __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
+  constexpr int PF = DV + kPartialHead;  // floats per partial record
+  constexpr int V4 = DV / 4;             // float4 column slices per row
+  constexpr int PER = (V4 + 31) / 32;    // slices per lane
+  griddep_launch_dependents();
+  griddep_wait();  // the decode grid's partials are complete and visible past this point
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows_total = p.hq * p.q_len;
   const int row = blockIdx.x * 4 + warp;
@@ -671,28 +682,66 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
   const int span = max(0, hi - lo);
   const int nc = max(1, (span + p.chunk - 1) / p.chunk);
   if (nc <= 1) return;
-  const float* base = p.ws + ((int64_t)b * rows_total + row) * p.max_chunks * (DV + 2);
-  float M = -INFINITY;
-  for (int c = lane; c < nc; c += 32) M = fmaxf(M, base[(int64_t)c * (DV + 2)]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float L = 0.0f;
+  const float* base = p.ws + ((int64_t)b * rows_total + row) * p.max_chunks * PF;
+
+  // (max, sum) over this lane's chunks, online, then across the warp
+  float m = -INFINITY, l = 0.0f, m_first = -INFINITY;
   for (int c = lane; c < nc; c += 32) {
-    const float mc = base[(int64_t)c * (DV + 2)];
-    if (mc != -INFINITY) L = fmaf(base[(int64_t)c * (DV + 2) + 1], ex2(mc - M), L);
+    const float mc = base[(int64_t)c * PF], lc = base[(int64_t)c * PF + 1];
+    if (c == lane) m_first = mc;
+    if (mc == -INFINITY) continue;
+    const float mn = fmaxf(m, mc);
+    l = (m == -INFINITY ? 0.0f : l * ex2(m - mn)) + lc * ex2(mc - mn);
+    m = mn;
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-  const int hq = row / p.q_len, l = row % p.q_len;
-  for (int d = lane; d < DV; d += 32) {
-    float O = 0.0f;
-    for (int c = 0; c < nc; ++c) {
-      const float mc = base[(int64_t)c * (DV + 2)];
-      if (mc != -INFINITY) O = fmaf(base[(int64_t)c * (DV + 2) + 2 + d], ex2(mc - M), O);
+  for (int off = 16; off > 0; off >>= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m, off);
+    const float lo_ = __shfl_xor_sync(0xffffffffu, l, off);
+    const float mn = fmaxf(m, mo);
+    if (mn != -INFINITY) {
+      l = (m == -INFINITY ? 0.0f : l * ex2(m - mn)) + (mo == -INFINITY ? 0.0f : lo_ * ex2(mo - mn));
+      m = mn;
     }
-    const float val = L > 0.0f ? O / L : 0.0f;
-    store_out(p.out, (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + d, val,
-              p.out_dtype);
+  }
+  const float M = m, inv_l = l > 0.0f ? 1.0f / l : 0.0f;
+
+  float4 acc[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) acc[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int c0 = 0; c0 < nc; c0 += 32) {
+    const int c = c0 + lane;
+    const float mc = c0 == 0 ? m_first : (c < nc ? base[(int64_t)c * PF] : -INFINITY);
+    const float w = (c < nc && mc != -INFINITY) ? ex2(mc - M) : 0.0f;
+    const int cnt = min(32, nc - c0);
+#pragma unroll 8
+    for (int j = 0; j < cnt; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, w, j);
+      const float4* src = reinterpret_cast<const float4*>(base + (int64_t)(c0 + j) * PF + kPartialHead);
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int v = lane + 32 * k;
+        if (V4 % 32 == 0 || v < V4) {
+          const float4 x = src[v];
+          acc[k].x = fmaf(x.x, wj, acc[k].x);
+          acc[k].y = fmaf(x.y, wj, acc[k].y);
+          acc[k].z = fmaf(x.z, wj, acc[k].z);
+          acc[k].w = fmaf(x.w, wj, acc[k].w);
+        }
+      }
+    }
+  }
+  const int hq = row / p.q_len, lq = row % p.q_len;
+  const int64_t o0 = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)lq * p.osl;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int v = lane + 32 * k;
+    if (V4 % 32 == 0 || v < V4) {
+      store_out(p.out, o0 + 4 * v + 0, acc[k].x * inv_l, p.out_dtype);
+      store_out(p.out, o0 + 4 * v + 1, acc[k].y * inv_l, p.out_dtype);
+      store_out(p.out, o0 + 4 * v + 2, acc[k].z * inv_l, p.out_dtype);
+      store_out(p.out, o0 + 4 * v + 3, acc[k].w * inv_l, p.out_dtype);
+    }
   }
 }
 
@@ -724,6 +773,44 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int* chunk
   if (*n_chunks < 1) *n_chunks = 1;
 }
 
+// Launch with programmatic stream serialization: the grid may become resident while the
+// previous kernel in the stream finishes (it waits in griddep_wait() before touching
+// memory).  Streams or drivers that refuse the attribute get a plain launch.
+template <typename... Args>
+static cudaError_t launch_pdl(void (*kfn)(Args...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, const DecodeParams& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, p);
+  if (e == cudaErrorNotSupported || e == cudaErrorInvalidValue) {
+    (void)cudaGetLastError();
+    kfn<<<grid, block, smem, stream>>>(p);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+// cudaFuncSetAttribute is per device: remember, per kernel instantiation, the devices done.
+template <typename F>
+static cudaError_t set_smem_once(F kfn, int bytes, unsigned long long* done_mask) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit != 0 && (__atomic_load_n(done_mask, __ATOMIC_ACQUIRE) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit != 0) __atomic_fetch_or(done_mask, bit, __ATOMIC_RELEASE);
+  return e;
+}
+
 template <int DK, int DV, bool SBF16, bool PAGED, int HP>
 static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_groups,
                                    cudaStream_t stream) {
@@ -733,21 +820,15 @@ static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_gro
   constexpr int NS = DecodeLayout<DK, DV, 3, HP, TS>::STAGE <= 6144 ? 3 : 2;
   using LY = DecodeLayout<DK, DV, NS, HP, TS>;
   auto kfn = decode_kernel<DK, DV, SBF16, PAGED, NS, HP, TS>;
-  static bool attr_done = false;  // per instantiation; idempotent if raced
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, LY::SMEM);
-    if (e != cudaSuccess) return e;
-    attr_done = true;
-  }
+  static unsigned long long smem_done = 0;
+  cudaError_t e = set_smem_once(kfn, LY::SMEM, &smem_done);
+  if (e != cudaSuccess) return e;
   dim3 grid(p.max_chunks, (p.hkv / HP) * row_groups, batch);
-  kfn<<<grid, 128, LY::SMEM, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  e = launch_pdl(kfn, grid, dim3(128), LY::SMEM, stream, p);
   if (e != cudaSuccess) return e;
   if (p.max_chunks > 1) {
     const int rows_total = p.hq * p.q_len;
-    dim3 g2((rows_total + 3) / 4, batch);
-    combine_kernel<DV><<<g2, 128, 0, stream>>>(p);
-    e = cudaGetLastError();
+    e = launch_pdl(combine_kernel<DV>, dim3((rows_total + 3) / 4, batch), dim3(128), 0, stream, p);
   }
   return e;
 }
