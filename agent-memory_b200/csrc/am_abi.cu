@@ -130,29 +130,21 @@ static int check_args(const am_q4_cache* c, const am_attn_args* a, const char* f
   return AM_OK;
 }
 
-// Rows of one KV head = n_rep * q_len query rows.  When they fill at most half of the 8 MMA
-// columns, several KV heads share a CTA (heads_per_cta, a power of two dividing n_kv_heads).
-static int decode_heads_per_cta(const am_q4_cache* c, const am_attn_args* a) {
-  const int n_rep = a->n_q_heads / c->n_kv_heads;
-  const int rows = n_rep * a->q_len;
-  int hp = 1;
-  const int cap = decode_max_heads_per_cta(c->k_dim, c->v_dim);
-  while (hp * 2 <= cap && hp * 2 * rows <= 8 && c->n_kv_heads % (hp * 2) == 0) hp *= 2;
-  return hp;
-}
-
+// Decode grid geometry: row groups of up to 8 query rows (n_rep * q_len rows per KV head)
+// and the KV split.  The span of a windowed call is the window plus the query rows, plus
+// up to one stage of keys from rounding the first key down to a stage boundary.
 static int decode_geometry(const am_q4_cache* c, const am_attn_args* a, int* row_groups,
                            int* chunk, int* n_chunks) {
   const int n_rep = a->n_q_heads / c->n_kv_heads;
   const int rows = n_rep * a->q_len;
-  const int hp = decode_heads_per_cta(c, a);
-  *row_groups = hp > 1 ? 1 : (rows + 7) / 8;
+  *row_groups = (rows + 7) / 8;
   int span = a->max_kv_len;
   if (a->mask_kind == AM_MASK_NONE && a->window > 0) {
-    const long long w = (long long)a->window + a->q_len - 1;
+    const long long w = (long long)a->window + a->q_len - 1 + decode_stage_tokens(c->k_dim, c->v_dim) - 1;
     if (w < span) span = static_cast<int>(w);
   }
-  decode_plan(a->batch, c->n_kv_heads / hp, *row_groups, span, chunk, n_chunks);
+  decode_plan(a->batch, c->n_kv_heads, *row_groups, span, decode_ctas_per_sm(c->k_dim, c->v_dim),
+              chunk, n_chunks);
   return rows;
 }
 
@@ -327,10 +319,11 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
     set_error("am_q4_decode: no kernel for k_dim=%d v_dim=%d", cache->k_dim, cache->v_dim);
     return AM_ERR_UNSUPPORTED;
   }
+  const int stage = decode_stage_tokens(cache->k_dim, cache->v_dim);
   if (cache->layout == AM_LAYOUT_PAGED &&
-      (cache->block_tokens < 32 || (cache->block_tokens & (cache->block_tokens - 1)))) {
-    set_error("am_q4_decode: paged decode needs block_tokens to be a power of two >= 32 (got %d)",
-              cache->block_tokens);
+      (cache->block_tokens < stage || (cache->block_tokens & (cache->block_tokens - 1)))) {
+    set_error("am_q4_decode: paged decode needs block_tokens to be a power of two >= %d (got %d)",
+              stage, cache->block_tokens);
     return AM_ERR_UNSUPPORTED;
   }
   if (!aligned(cache->k_scales, 16) || !aligned(cache->k_biases, 16) ||
@@ -355,7 +348,7 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
   fill_params(p, cache, a);
   p.chunk = chunk;
   p.max_chunks = n_chunks;
-  p.heads_per_cta = decode_heads_per_cta(cache, a);
+  p.stage_tokens = decode_stage_tokens(cache->k_dim, cache->v_dim);
   p.ws = static_cast<float*>(workspace);
   return cuda_status(launch_decode(p, a->batch, row_groups, cache->layout == AM_LAYOUT_PAGED,
                                    cache->scale_dtype == AM_DTYPE_BF16,

@@ -138,22 +138,25 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Wait for phase `parity` of an mbarrier; gives up after `limit_ns` (returns false).
+// Wait for phase `parity` of an mbarrier; gives up after `limit_ns` (returns false).  Each
+// try_wait may suspend the warp for up to 0.5 ms (woken early when the phase completes), so
+// a waiting warp yields its issue slots instead of spinning.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   uint64_t limit_ns = 2000000000ull) {
+  constexpr uint32_t kSuspendNs = 500000;
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     uint32_t done;
     asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
         "selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(kSuspendNs)
         : "memory");
     if (done) return true;
     if (it == 0) {
       t0 = globaltimer_ns();
-    } else if ((it & 63) == 0 && globaltimer_ns() - t0 > limit_ns) {
+    } else if (globaltimer_ns() - t0 > limit_ns) {
       return false;
     }
   }
@@ -222,7 +225,7 @@ struct DecodeParams {
   int32_t q_len;
   int32_t n_rep;
   int32_t rows_per_head;  // n_rep * q_len
-  int32_t heads_per_cta;  // KV heads packed into one CTA's 8 MMA columns (decode)
+  int32_t stage_tokens;   // decode pipeline stage (tokens); visible ranges align to it
   int32_t q_bf16;
   const uint16_t* q;
   int64_t qsb, qsh, qsl;
@@ -241,13 +244,14 @@ struct DecodeParams {
   int32_t* status;
   int32_t chunk;       // tokens per split (multiple of 64)
   int32_t max_chunks;  // grid.x
-  float* ws;           // partials [batch][hq*q_len][max_chunks][v_dim + 2]
+  float* ws;           // partials [batch][hq*q_len][max_chunks][kPartialHead + v_dim]
 };
 
 // Visible key range of a sequence for the structured mask: keys outside [lo, hi) are
-// excluded for every query row.  lo is rounded down to a multiple of 32 (stage size).
+// excluded for every query row.  lo is rounded down to a multiple of `align` (the decode
+// stage size, a power of two).
 __device__ __forceinline__ void visible_range(int n, int st, int q_len, int window, bool dense_mask,
-                                              int& lo, int& hi) {
+                                              int align, int& lo, int& hi) {
   hi = n;
   if (dense_mask) {
     lo = 0;
@@ -256,7 +260,7 @@ __device__ __forceinline__ void visible_range(int n, int st, int q_len, int wind
     if (window > 0) lo = max(lo, n - q_len - window + 1);
     lo = max(lo, 0);
   }
-  lo &= ~31;  // 32-token pipeline stages start on 32-token boundaries
+  lo &= ~(align - 1);  // pipeline stages start on stage boundaries
 }
 
 }  // namespace am

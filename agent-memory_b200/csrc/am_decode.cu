@@ -38,46 +38,50 @@ constexpr int kMaxChunk = 2048;            // tokens per CTA chunk (decode_plan 
 constexpr int kMaxBlk = kMaxChunk / 32 + 2;  // block ids a chunk can touch (block_tokens >= 32)
 constexpr float kMaskedFinite = -1.0e30f;  // boolean-mask fill (finite: keeps uniform rows)
 
-template <int DK, int DV, int NS, int HP, int TS>
+template <int DK, int DV, int NS, int TS>
 struct DecodeLayout {
   static constexpr int NGK = DK / 64, NGV = DV / 64;
   static constexpr int KW = DK / 8, VW = DV / 8;
   static constexpr int KROW = DK / 2, VROW = DV / 2;  // bytes of codes per token row
-  // one head's share of a stage: codes and scales of TS rows as laid out in HBM
-  static constexpr int H_OFF_V = TS * KROW;
-  static constexpr int H_OFF_KS = H_OFF_V + TS * VROW;
-  static constexpr int H_OFF_KB = H_OFF_KS + TS * NGK * 2;
-  static constexpr int H_OFF_VS = H_OFF_KB + TS * NGK * 2;
-  static constexpr int H_OFF_VB = H_OFF_VS + TS * NGV * 2;
-  static constexpr int HB = (H_OFF_VB + TS * NGV * 2 + 15) / 16 * 16;
-  static constexpr int STAGE = (HP * HB + 127) / 128 * 128;
+  // a stage: codes and scales of TS rows, each section as laid out in HBM
+  static constexpr int OFF_V = TS * KROW;
+  static constexpr int OFF_KS = OFF_V + TS * VROW;
+  static constexpr int OFF_KB = OFF_KS + TS * NGK * 2;
+  static constexpr int OFF_VS = OFF_KB + TS * NGK * 2;
+  static constexpr int OFF_VB = OFF_VS + TS * NGV * 2;
+  static constexpr int STAGE = (OFF_VB + TS * NGV * 2 + 127) / 128 * 128;
   static constexpr int RING = NS * STAGE;
   static constexpr int OFF_BAR = kWarps * RING;
   static constexpr int OFF_OK = OFF_BAR + kWarps * NS * 8;
   static constexpr int OFF_BLK = OFF_OK + kWarps * NS * 4;
-  static constexpr int SMEM = OFF_BLK + kMaxBlk * 4;
-  // The queries are staged (as their 16-bit inputs, plus per-group sums and maxima) in the
-  // last stage of warp 0's ring, which no copy touches before the main loop starts.
+  // per-column table: int32 [8][4] (hq, l, pos, valid), float [8] prescale, int64 [8]
+  // output offset, int64 [8] partial offset, int32 [4] (mask_lo, mask_hi)
+  static constexpr int OFF_COL = (OFF_BLK + kMaxBlk * 4 + 15) / 16 * 16;
+  static constexpr int SMEM = OFF_COL + 8 * 16 + 8 * 4 + 8 * 8 * 2 + 16;
+  // The queries are staged (as fp32 when they fit, else as their 16-bit inputs, plus
+  // per-group sums and maxima) in the last stage of warp 0's ring, which no copy touches
+  // before the main loop starts.
+  static constexpr bool Q32 = 8 * DK * 4 + 2 * 8 * NGK * 4 <= STAGE;
   static constexpr int OFF_Q = (NS - 1) * STAGE;
-  static constexpr int OFF_QS = OFF_Q + 8 * DK * 2;
+  static constexpr int OFF_QS = OFF_Q + 8 * DK * (Q32 ? 4 : 2);
   static_assert(8 * DK * 2 + 2 * 8 * NGK * 4 <= STAGE, "query staging must fit in one stage");
-  static_assert(8 * (DV + 2) * 4 <= RING, "warp result must fit in its ring");
+  static_assert((16 + 8 * (DV + 1)) * 4 <= RING, "warp result must fit in its ring");
+  static_assert((kWarps * 8 + 24) * 4 <= kMaxBlk * 4, "CTA merge factors must fit in the block-id area");
 };
 
-template <int NG>
-__device__ __forceinline__ void load_scales(const uint8_t* base, int tok, float (&out)[NG],
-                                            bool bf16) {
+template <int NG, bool BF16>
+__device__ __forceinline__ void load_scales(const uint8_t* base, int tok, float (&out)[NG]) {
   const uint16_t* p = reinterpret_cast<const uint16_t*>(base) + tok * NG;
   if constexpr (NG % 2 == 0) {
 #pragma unroll
     for (int i = 0; i < NG; i += 2) {
       const uint32_t u = *reinterpret_cast<const uint32_t*>(p + i);
-      out[i] = h2f_rt(static_cast<uint16_t>(u & 0xffffu), bf16);
-      out[i + 1] = h2f_rt(static_cast<uint16_t>(u >> 16), bf16);
+      out[i] = h2f<BF16>(static_cast<uint16_t>(u & 0xffffu));
+      out[i + 1] = h2f<BF16>(static_cast<uint16_t>(u >> 16));
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < NG; ++i) out[i] = h2f_rt(p[i], bf16);
+    for (int i = 0; i < NG; ++i) out[i] = h2f<BF16>(p[i]);
   }
 }
 
@@ -89,40 +93,16 @@ __device__ __forceinline__ float load_mask(const DecodeParams& p, int b, int hq,
   return h2f_rt(static_cast<const uint16_t*>(p.mask)[idx], p.mask_dtype == AM_DTYPE_BF16);
 }
 
-// Column c (0..7) of the CTA's MMA N dimension -> (head offset within the CTA's head group,
-// row within that head).  With HP > 1 the rows of HP KV heads share the 8 columns.
-struct ColMap {
-  int hp, rr;
-  bool valid;
-};
+// Lazy softmax rescaling: the running max is only raised when a stage's max exceeds it by
+// more than 2^3 (log2 units), so P <= 8 and P * scale_v stays well inside fp16.
+constexpr float kRescaleSlack = 3.0f;
 
-__device__ __forceinline__ ColMap col_map(int c, int hp_n, int rph, int rg) {
-  ColMap m;
-  if (hp_n > 1) {
-    m.hp = c / rph;
-    m.rr = c % rph;
-    m.valid = c < hp_n * rph;
-    if (!m.valid) {
-      m.hp = hp_n - 1;
-      m.rr = rph - 1;
-    }
-  } else {
-    m.hp = 0;
-    m.rr = rg * 8 + c;
-    m.valid = m.rr < rph;
-    if (!m.valid) m.rr = rph - 1;
-  }
-  return m;
-}
-
-template <int DK, int DV, bool SBF16, bool PAGED, int NS, int HP, int TS>
+template <int DK, int DV, bool SBF16, bool PAGED, int NS, int TS>
 __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
-  using LY = DecodeLayout<DK, DV, NS, HP, TS>;
+  using LY = DecodeLayout<DK, DV, NS, TS>;
   constexpr int NH = TS / 16;  // 16-token MMA tiles per stage
   constexpr int NGK = LY::NGK, NGV = LY::NGV;
-  constexpr int KW = LY::KW, VW = LY::VW;
   constexpr int KROW = LY::KROW, VROW = LY::VROW;
-  constexpr int HB = LY::HB;
   constexpr int KSTEPS = DK / 16;
   constexpr int MT = DV / 16;
 
@@ -135,8 +115,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int b = blockIdx.z;
-  const int row_groups = gridDim.y / (p.hkv / HP);
-  const int h0 = (blockIdx.y / row_groups) * HP;
+  const int row_groups = gridDim.y / p.hkv;
+  const int h0 = blockIdx.y / row_groups;
   const int rg = blockIdx.y % row_groups;
   const int chunk = blockIdx.x;
   const int rph = p.rows_per_head;
@@ -145,9 +125,12 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
   const bool dense_mask = p.mask_kind != AM_MASK_NONE;
   int lo, hi;
-  visible_range(n, st, p.q_len, p.window, dense_mask, lo, hi);
+  visible_range(n, st, p.q_len, p.window, dense_mask, TS, lo, hi);
   const int span = max(0, hi - lo);
-  const int n_chunks_b = max(1, (span + p.chunk - 1) / p.chunk);
+  const int n_chunks_need = max(1, (span + p.chunk - 1) / p.chunk);
+  if (n_chunks_need > p.max_chunks && chunk == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    flag_status(p.status, AM_STATUS_BAD_POSITION);  // kv_len beyond the planned max_kv_len
+  const int n_chunks_b = min(n_chunks_need, p.max_chunks);
   if (chunk >= n_chunks_b) return;
   const int c_lo = lo + chunk * p.chunk;
   const int c_hi = min(c_lo + p.chunk, hi);
@@ -158,6 +141,11 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR) + warp * NS;
   int32_t* tile_ok = reinterpret_cast<int32_t*>(smem + LY::OFF_OK) + warp * NS;
   int32_t* sblk = reinterpret_cast<int32_t*>(smem + LY::OFF_BLK);
+  int32_t* col_i = reinterpret_cast<int32_t*>(smem + LY::OFF_COL);           // [8][4]
+  float* col_pw = reinterpret_cast<float*>(smem + LY::OFF_COL + 128);         // [8]
+  int64_t* col_oo = reinterpret_cast<int64_t*>(smem + LY::OFF_COL + 160);     // [8]
+  int64_t* col_wo = reinterpret_cast<int64_t*>(smem + LY::OFF_COL + 224);     // [8]
+  int32_t* col_mask = reinterpret_cast<int32_t*>(smem + LY::OFF_COL + 288);   // [2]
 
   // ------------------------------------------------------------------ barriers, block ids
   if (lane == 0) {
@@ -181,25 +169,25 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   }
   __syncthreads();
 
-  // Lane 0 of each warp fills its ring: a stage = TS rows of K/V codes and scales of
-  // each of the HP heads, six 1-D bulk copies per head completing on the stage's mbarrier.
+  // Lane 0 of each warp fills its ring: a stage = TS rows of K/V codes and scales, six
+  // 1-D bulk copies completing on the stage's mbarrier.  A stage never crosses a paged
+  // block (block_tokens is a power of two >= TS and stages start on TS boundaries).
+  const int64_t head_rows = PAGED ? 0 : ((int64_t)b * p.hkv + h0) * p.capacity;
   auto issue = [&](int k) {
     if (k >= my_stages) return;
     const int s = k % NS;
     const int t0 = c_lo + (warp + kWarps * k) * TS;
-    int64_t row0, head_stride;
+    int64_t row0;
     int nrows;
     bool ok = true;
     if constexpr (PAGED) {
       const int32_t v = sblk[(t0 >> p.bt_shift) - blk0];
       ok = v >= 0;
       row0 = ((((int64_t)(ok ? v : 0)) * p.hkv + h0) << p.bt_shift) + (t0 & (p.block_tokens - 1));
-      head_stride = p.block_tokens;
       nrows = TS;
     } else {
-      row0 = ((int64_t)b * p.hkv + h0) * p.capacity + t0;
-      head_stride = p.capacity;
-      nrows = p.capacity - t0 >= TS ? TS : 16;
+      row0 = head_rows + t0;
+      nrows = min(TS, static_cast<int>(p.capacity - t0));  // capacity and t0 are multiples of 16
     }
     tile_ok[s] = ok ? 1 : 0;
     const uint32_t bar = smem_u32(&bars[s]);
@@ -207,19 +195,14 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       mbar_arrive(bar);
       return;
     }
-    const uint32_t bytes = nrows * (KROW + VROW + 4 * NGK + 4 * NGV);
-    mbar_arrive_expect_tx(bar, HP * bytes);
-#pragma unroll
-    for (int hp = 0; hp < HP; ++hp) {
-      const int64_t r0 = row0 + hp * head_stride;
-      uint8_t* stg = ring + s * LY::STAGE + hp * HB;
-      bulk_g2s(stg, p.kc + r0 * KW, nrows * KROW, bar);
-      bulk_g2s(stg + LY::H_OFF_V, p.vc + r0 * VW, nrows * VROW, bar);
-      bulk_g2s(stg + LY::H_OFF_KS, p.ks + r0 * NGK, nrows * NGK * 2, bar);
-      bulk_g2s(stg + LY::H_OFF_KB, p.kb + r0 * NGK, nrows * NGK * 2, bar);
-      bulk_g2s(stg + LY::H_OFF_VS, p.vs + r0 * NGV, nrows * NGV * 2, bar);
-      bulk_g2s(stg + LY::H_OFF_VB, p.vb + r0 * NGV, nrows * NGV * 2, bar);
-    }
+    mbar_arrive_expect_tx(bar, nrows * (KROW + VROW + 4 * NGK + 4 * NGV));
+    uint8_t* stg = ring + s * LY::STAGE;
+    bulk_g2s(stg, p.kc + row0 * LY::KW, nrows * KROW, bar);
+    bulk_g2s(stg + LY::OFF_V, p.vc + row0 * LY::VW, nrows * VROW, bar);
+    bulk_g2s(stg + LY::OFF_KS, p.ks + row0 * NGK, nrows * NGK * 2, bar);
+    bulk_g2s(stg + LY::OFF_KB, p.kb + row0 * NGK, nrows * NGK * 2, bar);
+    bulk_g2s(stg + LY::OFF_VS, p.vs + row0 * NGV, nrows * NGV * 2, bar);
+    bulk_g2s(stg + LY::OFF_VB, p.vb + row0 * NGV, nrows * NGV * 2, bar);
   };
   if (lane == 0) {
 #pragma unroll
@@ -227,57 +210,116 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   }
 
   // ------------------------------------------------------------------ stage queries
+  // Column c of the MMA N dimension is query row rg*8 + c of this KV head (row r = l*n_rep
+  // + head offset); columns past the head's rows repeat its last row and are never written.
   const bool qbf = p.q_bf16 != 0;
-  uint16_t* qs = reinterpret_cast<uint16_t*>(smem + LY::OFF_Q);  // [8 columns][DK] raw inputs
-  float* qsum_s = reinterpret_cast<float*>(smem + LY::OFF_QS);    // [8][NGK]
-  float* qmax_s = qsum_s + 8 * NGK;                               // [8][NGK]
+  float* qs32 = reinterpret_cast<float*>(smem + LY::OFF_Q);         // [8][DK] fp32, or
+  uint16_t* qs16 = reinterpret_cast<uint16_t*>(smem + LY::OFF_Q);   // [8][DK] 16-bit inputs
+  auto qget = [&](int c, int d) -> float {
+    if constexpr (LY::Q32) {
+      return qs32[c * DK + d];
+    } else {
+      return h2f_rt(qs16[c * DK + d], qbf);
+    }
+  };
+  float* qsum_s = reinterpret_cast<float*>(smem + LY::OFF_QS);   // [8][NGK]
+  float* qmax_s = qsum_s + 8 * NGK;                              // [8][NGK]
+  if (tid < 8) {
+    const int c = tid;
+    int rr = rg * 8 + c;
+    const int valid = rr < rph;
+    if (!valid) rr = rph - 1;
+    const int l = rr / p.n_rep;
+    const int hq = h0 * p.n_rep + rr % p.n_rep;
+    col_i[c * 4 + 0] = hq;
+    col_i[c * 4 + 1] = l;
+    col_i[c * 4 + 2] = n - p.q_len + l;
+    col_i[c * 4 + 3] = valid;
+    col_oo[c] = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl;
+    col_wo[c] = (((int64_t)b * p.hq * p.q_len + (int64_t)hq * p.q_len + l) * p.max_chunks + chunk) *
+                (DV + kPartialHead);
+    if (c == 0) {
+      // keys inside [mask_lo, mask_hi) are visible to every row of the CTA
+      const int rows_here = min(8, rph - rg * 8);
+      const int pos_min = n - p.q_len + (rg * 8) / p.n_rep;
+      const int pos_max = n - p.q_len + (rg * 8 + rows_here - 1) / p.n_rep;
+      col_mask[0] = max(st, p.window > 0 ? pos_max - p.window + 1 : 0);
+      col_mask[1] = p.causal ? min(n, pos_min + 1) : n;
+    }
+  }
   for (int i = tid; i < 8 * (DK / 8); i += 128) {
     const int c = i / (DK / 8), c8 = i % (DK / 8);
-    const ColMap cm = col_map(c, HP, rph, rg);
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (cm.valid) {
-      const int l = cm.rr / p.n_rep;
-      const int hq = (h0 + cm.hp) * p.n_rep + cm.rr % p.n_rep;
-      const uint16_t* src = p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl + c8 * 8;
-      raw = *reinterpret_cast<const uint4*>(src);
+    int rr = rg * 8 + c;
+    if (rr >= rph) rr = rph - 1;
+    const int l = rr / p.n_rep;
+    const int hq = h0 * p.n_rep + rr % p.n_rep;
+    const uint4 raw = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh +
+                                                      (int64_t)l * p.qsl + c8 * 8);
+    if constexpr (LY::Q32) {
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      float4 lo4, hi4;
+      float* f = &lo4.x;
+      float* h = &hi4.x;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        f[2 * j] = h2f_rt(static_cast<uint16_t>(w[j] & 0xffffu), qbf);
+        f[2 * j + 1] = h2f_rt(static_cast<uint16_t>(w[j] >> 16), qbf);
+        h[2 * j] = h2f_rt(static_cast<uint16_t>(w[2 + j] & 0xffffu), qbf);
+        h[2 * j + 1] = h2f_rt(static_cast<uint16_t>(w[2 + j] >> 16), qbf);
+      }
+      *reinterpret_cast<float4*>(qs32 + c * DK + c8 * 8) = lo4;
+      *reinterpret_cast<float4*>(qs32 + c * DK + c8 * 8 + 4) = hi4;
+    } else {
+      *reinterpret_cast<uint4*>(qs16 + c * DK + c8 * 8) = raw;
     }
-    *reinterpret_cast<uint4*>(qs + c * DK + c8 * 8) = raw;
   }
   __syncthreads();
-  if (tid < 8 * NGK) {
-    const int r = tid / NGK, G = tid % NGK;
-    float sm = 0.0f, mx = 0.0f;
-    for (int d = 0; d < 64; ++d) {
-      const float v = h2f_rt(qs[r * DK + G * 64 + d], qbf);
-      sm += v;
-      mx = fmaxf(mx, fabsf(v));
+  {
+    // per (column, 64-dim group) sum and max |q|: 4 threads per pair, 16 dims each
+    constexpr int NQ = 8 * NGK * 4;
+    static_assert(NQ % 32 == 0 && NQ <= 128, "query statistics use whole warps");
+    if (tid < NQ) {
+      const int r = tid / (NGK * 4), G = (tid / 4) % NGK, part = tid % 4;
+      float sm = 0.0f, mx = 0.0f;
+#pragma unroll
+      for (int d = 0; d < 16; ++d) {
+        const float v = qget(r, G * 64 + part * 16 + d);
+        sm += v;
+        mx = fmaxf(mx, fabsf(v));
+      }
+#pragma unroll
+      for (int off = 1; off < 4; off <<= 1) {
+        sm += __shfl_xor_sync(0xffffffffu, sm, off);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      }
+      if (part == 0) {
+        qsum_s[r * NGK + G] = sm;
+        qmax_s[r * NGK + G] = mx;
+      }
     }
-    qsum_s[tid] = sm;
-    qmax_s[tid] = mx;
   }
   __syncthreads();
-
-  // Per-column power-of-two prescale so fp16 MMA operands keep full precision (bf16 queries).
-  auto col_pow2 = [&](int c) -> float {
+  if (tid < 8) {
+    // power-of-two prescale per column so fp16 MMA operands keep full precision
     float m = 0.0f;
 #pragma unroll
-    for (int G = 0; G < NGK; ++G) m = fmaxf(m, qmax_s[c * NGK + G]);
-    if (!(m > 0.0f) || !isfinite(m)) return 1.0f;
-    int e;
-    frexpf(m, &e);  // m in [2^(e-1), 2^e)
-    return ldexpf(1.0f, 15 - e);
-  };
+    for (int G = 0; G < NGK; ++G) m = fmaxf(m, qmax_s[tid * NGK + G]);
+    float pw = 1.0f;
+    if (m > 0.0f && isfinite(m)) {
+      int e;
+      frexpf(m, &e);  // m in [2^(e-1), 2^e)
+      pw = ldexpf(1.0f, 15 - e);
+    }
+    col_pw[tid] = pw;
+  }
+  __syncthreads();
 
-  // B fragments of Q for S = K . Q^T, one set per packed head: this thread's column g keeps
-  // its query only in the set of its own head (zeros elsewhere), so the MMAs of head hp fill
-  // exactly head hp's columns of the shared accumulator.  k-step s = 4G + 2j + e covers
-  // words 8G + 2t + j of column t's slots; nibbles (2e, 2e+4) feed k-slots 2t, 2t+1 and
-  // nibbles (2e+1, 2e+5) feed 2t+8, 2t+9 (pre-divided by 16).
-  uint32_t qf[HP][KSTEPS][2];
+  // B fragments of Q for S = K . Q^T.  k-step s = 4G + 2j + e covers words 8G + 2t + j of
+  // column g's slots; nibbles (2e, 2e+4) feed k-slots 2t, 2t+1 and nibbles (2e+1, 2e+5)
+  // feed 2t+8, 2t+9 (pre-divided by 16).
+  uint32_t qf[KSTEPS][2];
   {
-    const ColMap cm = col_map(g, HP, rph, rg);
-    const float pw = col_pow2(g);
-    const uint16_t* qr = qs + g * DK;
+    const float pw = col_pw[g];
 #pragma unroll
     for (int G = 0; G < NGK; ++G) {
 #pragma unroll
@@ -285,48 +327,28 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int s = 4 * G + 2 * j + e;
-          const int w = 8 * G + 2 * t + j;
-          const uint16_t* q8 = qr + 8 * w + 2 * e;
-          const uint32_t b0 = pack_half2(h2f_rt(q8[0], qbf) * pw, h2f_rt(q8[4], qbf) * pw);
-          const uint32_t b1 = pack_half2(h2f_rt(q8[1], qbf) * pw * 0.0625f,
-                                         h2f_rt(q8[5], qbf) * pw * 0.0625f);
-#pragma unroll
-          for (int hp = 0; hp < HP; ++hp) {
-            qf[hp][s][0] = hp == cm.hp ? b0 : 0u;
-            qf[hp][s][1] = hp == cm.hp ? b1 : 0u;
-          }
+          const int d8 = 8 * (8 * G + 2 * t + j) + 2 * e;
+          qf[s][0] = pack_half2(qget(g, d8) * pw, qget(g, d8 + 4) * pw);
+          qf[s][1] = pack_half2(qget(g, d8 + 1) * pw * 0.0625f, qget(g, d8 + 5) * pw * 0.0625f);
         }
       }
     }
   }
   // Per-column (2t, 2t+1) constants.
   float fac[2], qb[2][NGK];
-  int pos_c[2], l_c[2], hq_c[2], hb_c[2];
+  int pos_c[2], l_c[2], hq_c[2];
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const int col = 2 * t + c;
-    const ColMap cm = col_map(col, HP, rph, rg);
-    const float pw = col_pow2(col);
-    fac[c] = 16777216.0f / pw * p.scale_log2;  // 2^24 undoes the subnormal code encoding
+    fac[c] = 16777216.0f / col_pw[col] * p.scale_log2;  // 2^24 undoes the subnormal code encoding
 #pragma unroll
     for (int G = 0; G < NGK; ++G) qb[c][G] = qsum_s[col * NGK + G] * p.scale_log2;
-    l_c[c] = cm.rr / p.n_rep;
-    hq_c[c] = (h0 + cm.hp) * p.n_rep + cm.rr % p.n_rep;
-    pos_c[c] = n - p.q_len + l_c[c];
-    hb_c[c] = cm.hp * HB;
+    hq_c[c] = col_i[col * 4 + 0];
+    l_c[c] = col_i[col * 4 + 1];
+    pos_c[c] = col_i[col * 4 + 2];
   }
-  const int my_hp_g = col_map(g, HP, rph, rg).hp;  // head of this thread's B column after movmatrix
-  const bool pair_same = HP == 1 || (rph % 2) == 0;  // columns 2t and 2t+1 belong to one head
   // Stages entirely inside [mask_lo, mask_hi) need no per-element masking.
-  int mask_lo, mask_hi;
-  {
-    const int rows_here = HP > 1 ? rph : min(8, rph - rg * 8);
-    const int rr0 = HP > 1 ? 0 : rg * 8;
-    const int pos_min = n - p.q_len + rr0 / p.n_rep;
-    const int pos_max = n - p.q_len + (rr0 + rows_here - 1) / p.n_rep;
-    mask_lo = max(st, p.window > 0 ? pos_max - p.window + 1 : 0);
-    mask_hi = p.causal ? min(n, pos_min + 1) : n;
-  }
+  const int mask_lo = col_mask[0], mask_hi = col_mask[1];
   __syncthreads();  // every warp is done with the staged queries before warp 0 refills that stage
 
   // ------------------------------------------------------------------ streaming loop
@@ -357,92 +379,56 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     const int t0 = c_lo + (warp + kWarps * k) * TS;
     const bool ok = tile_ok[s] != 0;
 
-    // ---- S = K . Q^T for the two 16-token halves, all packed heads into one accumulator ----
-    // one accumulator set per packed head keeps each MMA dependency chain 4 deep; head hp's
-    // MMAs only fill head hp's columns, so the sets are summed afterwards
-    float acch[HP][NH][NGK][4];
-#pragma unroll
-    for (int hp = 0; hp < HP; ++hp)
-#pragma unroll
-      for (int hh = 0; hh < NH; ++hh)
-#pragma unroll
-        for (int G = 0; G < NGK; ++G)
-          acch[hp][hh][G][0] = acch[hp][hh][G][1] = acch[hp][hh][G][2] = acch[hp][hh][G][3] = 0.0f;
-#pragma unroll
-    for (int hp = 0; hp < HP; ++hp) {
-#pragma unroll
-      for (int G = 0; G < NGK; ++G) {
-        uint2 wa[NH], wb[NH];
-#pragma unroll
-        for (int hh = 0; hh < NH; ++hh) {
-          wa[hh] = *reinterpret_cast<const uint2*>(stg + hp * HB + (hh * 16 + g) * KROW + G * 32 + t * 8);
-          wb[hh] = *reinterpret_cast<const uint2*>(stg + hp * HB + (hh * 16 + g + 8) * KROW + G * 32 + t * 8);
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          uint32_t xa[NH], xb[NH];
-#pragma unroll
-          for (int hh = 0; hh < NH; ++hh) {
-            xa[hh] = j ? wa[hh].y : wa[hh].x;
-            xb[hh] = j ? wb[hh].y : wb[hh].x;
-          }
-          const int s0 = 4 * G + 2 * j;
-#pragma unroll
-          for (int hh = 0; hh < NH; ++hh)
-            mma_f16_16816(acch[hp][hh][G], xa[hh] & 0x000F000Fu, xb[hh] & 0x000F000Fu,
-                          xa[hh] & 0x00F000F0u, xb[hh] & 0x00F000F0u, qf[hp][s0][0], qf[hp][s0][1]);
-#pragma unroll
-          for (int hh = 0; hh < NH; ++hh) {
-            xa[hh] >>= 8;
-            xb[hh] >>= 8;
-            mma_f16_16816(acch[hp][hh][G], xa[hh] & 0x000F000Fu, xb[hh] & 0x000F000Fu,
-                          xa[hh] & 0x00F000F0u, xb[hh] & 0x00F000F0u, qf[hp][s0 + 1][0],
-                          qf[hp][s0 + 1][1]);
-          }
-        }
-      }
-    }
+    // ---- S = K . Q^T, one accumulator set per 16-token tile and 64-dim group ----
     float acc[NH][NGK][4];
 #pragma unroll
     for (int hh = 0; hh < NH; ++hh)
 #pragma unroll
-      for (int G = 0; G < NGK; ++G)
+      for (int G = 0; G < NGK; ++G) acc[hh][G][0] = acc[hh][G][1] = acc[hh][G][2] = acc[hh][G][3] = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float a = acch[0][hh][G][e];
+    for (int G = 0; G < NGK; ++G) {
+      uint2 wa[NH], wb[NH];
 #pragma unroll
-          for (int hp = 1; hp < HP; ++hp) a += acch[hp][hh][G][e];
-          acc[hh][G][e] = a;
+      for (int hh = 0; hh < NH; ++hh) {
+        wa[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g) * KROW + G * 32 + t * 8);
+        wb[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g + 8) * KROW + G * 32 + t * 8);
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int s0 = 4 * G + 2 * j;
+#pragma unroll
+        for (int hh = 0; hh < NH; ++hh) {
+          const uint32_t xa = j ? wa[hh].y : wa[hh].x;
+          const uint32_t xb = j ? wb[hh].y : wb[hh].x;
+          mma_f16_16816(acc[hh][G], xa & 0x000F000Fu, xb & 0x000F000Fu, xa & 0x00F000F0u,
+                        xb & 0x00F000F0u, qf[s0][0], qf[s0][1]);
         }
-    // scores in log2 units: s2[hh][e] -> token hh*16 + g + 8*(e>>1), column 2t + (e&1); the
-    // group scale and bias come from the head of the element's column (one head for both
-    // columns of a thread unless heads hold a single query row each)
+#pragma unroll
+        for (int hh = 0; hh < NH; ++hh) {
+          const uint32_t xa = (j ? wa[hh].y : wa[hh].x) >> 8;
+          const uint32_t xb = (j ? wb[hh].y : wb[hh].x) >> 8;
+          mma_f16_16816(acc[hh][G], xa & 0x000F000Fu, xb & 0x000F000Fu, xa & 0x00F000F0u,
+                        xb & 0x00F000F0u, qf[s0 + 1][0], qf[s0 + 1][1]);
+        }
+      }
+    }
+    // scores in log2 units: s2[hh][e] -> token hh*16 + g + 8*(e>>1), column 2t + (e&1)
     float s2[NH][4];
 #pragma unroll
     for (int hh = 0; hh < NH; ++hh) {
 #pragma unroll
       for (int tr = 0; tr < 2; ++tr) {
-        float sk[2][NGK], bk[2][NGK];
-        load_scales<NGK>(stg + hb_c[0] + LY::H_OFF_KS, hh * 16 + g + 8 * tr, sk[0], SBF16);
-        load_scales<NGK>(stg + hb_c[0] + LY::H_OFF_KB, hh * 16 + g + 8 * tr, bk[0], SBF16);
-        if (pair_same) {
-#pragma unroll
-          for (int G = 0; G < NGK; ++G) {
-            sk[1][G] = sk[0][G];
-            bk[1][G] = bk[0][G];
-          }
-        } else {
-          load_scales<NGK>(stg + hb_c[1] + LY::H_OFF_KS, hh * 16 + g + 8 * tr, sk[1], SBF16);
-          load_scales<NGK>(stg + hb_c[1] + LY::H_OFF_KB, hh * 16 + g + 8 * tr, bk[1], SBF16);
-        }
+        float sk[NGK], bk[NGK];
+        load_scales<NGK, SBF16>(stg + LY::OFF_KS, hh * 16 + g + 8 * tr, sk);
+        load_scales<NGK, SBF16>(stg + LY::OFF_KB, hh * 16 + g + 8 * tr, bk);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int e = 2 * tr + c;
           float x = 0.0f, y = 0.0f;
 #pragma unroll
           for (int G = 0; G < NGK; ++G) {
-            x = fmaf(sk[c][G], acc[hh][G][e], x);
-            y = fmaf(bk[c][G], qb[c][G], y);
+            x = fmaf(sk[G], acc[hh][G][e], x);
+            y = fmaf(bk[G], qb[c][G], y);
           }
           s2[hh][e] = fmaf(x, fac[c], y);
         }
@@ -473,7 +459,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
         }
       }
     }
-    // ---- online softmax (per column, over the 32 tokens of the stage) ----
+    // ---- online softmax (per column, over the TS tokens of the stage) ----
     float mt[2] = {fmaxf(s2[0][0], s2[0][2]), fmaxf(s2[0][1], s2[0][3])};
 #pragma unroll
     for (int hh = 1; hh < NH; ++hh) {
@@ -486,8 +472,10 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       mt[c] = fmaxf(mt[c], __shfl_xor_sync(0xffffffffu, mt[c], 8));
       mt[c] = fmaxf(mt[c], __shfl_xor_sync(0xffffffffu, mt[c], 16));
     }
-    const float mn0 = fmaxf(m_run[0], mt[0]), mn1 = fmaxf(m_run[1], mt[1]);
-    if (__any_sync(0xffffffffu, mn0 > m_run[0] || mn1 > m_run[1])) {
+    // (m_run + slack is -inf while nothing is visible yet, so the first finite max always
+    // installs itself)
+    if (__any_sync(0xffffffffu, mt[0] > m_run[0] + kRescaleSlack || mt[1] > m_run[1] + kRescaleSlack)) {
+      const float mn0 = fmaxf(m_run[0], mt[0]), mn1 = fmaxf(m_run[1], mt[1]);
       const float a0 = m_run[0] == -INFINITY ? 0.0f : ex2(m_run[0] - mn0);
       const float a1 = m_run[1] == -INFINITY ? 0.0f : ex2(m_run[1] - mn1);
 #pragma unroll
@@ -510,7 +498,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     const float ms0 = m_run[0] == -INFINITY ? 0.0f : m_run[0];
     const float ms1 = m_run[1] == -INFINITY ? 0.0f : m_run[1];
 
-    // ---- O^T += V^T . (P * scale_v): per half, one B operand per packed head ----
+    // ---- O^T += V^T . (P * scale_v) per 16-token tile ----
 #pragma unroll
     for (int hh = 0; hh < NH; ++hh) {
       float pr[4];
@@ -520,23 +508,23 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       pr[3] = ex2(s2[hh][3] - ms1);
       l_run[0] += pr[0] + pr[2];
       l_run[1] += pr[1] + pr[3];
-      // sv[tr][c][G] / bv: scale / bias of the element's token row (g + 8 tr) and column head
-      float sv[2][2][NGV], bv[2][2][NGV];
+      // scale / bias of the element's token row (g + 8 tr)
+      float sv[2][NGV], bv[2][NGV];
 #pragma unroll
       for (int tr = 0; tr < 2; ++tr) {
-        load_scales<NGV>(stg + hb_c[0] + LY::H_OFF_VS, hh * 16 + g + 8 * tr, sv[tr][0], SBF16);
-        load_scales<NGV>(stg + hb_c[0] + LY::H_OFF_VB, hh * 16 + g + 8 * tr, bv[tr][0], SBF16);
-        if (pair_same) {
+        load_scales<NGV, SBF16>(stg + LY::OFF_VS, hh * 16 + g + 8 * tr, sv[tr]);
+        load_scales<NGV, SBF16>(stg + LY::OFF_VB, hh * 16 + g + 8 * tr, bv[tr]);
+      }
+      float svc[2][2][NGV], bvc[2][2][NGV];  // [tr][column][G]
+#pragma unroll
+      for (int tr = 0; tr < 2; ++tr)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int G = 0; G < NGV; ++G) {
-            sv[tr][1][G] = sv[tr][0][G];
-            bv[tr][1][G] = bv[tr][0][G];
+            svc[tr][c][G] = sv[tr][G];
+            bvc[tr][c][G] = bv[tr][G];
           }
-        } else {
-          load_scales<NGV>(stg + hb_c[1] + LY::H_OFF_VS, hh * 16 + g + 8 * tr, sv[tr][1], SBF16);
-          load_scales<NGV>(stg + hb_c[1] + LY::H_OFF_VB, hh * 16 + g + 8 * tr, bv[tr][1], SBF16);
-        }
-      }
       if (masked_stage) {
         // rows of excluded keys may hold stale shared memory (not loaded, or beyond the
         // written length): zero their scale and bias so p = 0 cannot meet a NaN
@@ -547,35 +535,30 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
             const bool live = pr[2 * tr + c] > 0.0f;
 #pragma unroll
             for (int G = 0; G < NGV; ++G) {
-              sv[tr][c][G] = live ? sv[tr][c][G] : 0.0f;
-              bv[tr][c][G] = live ? bv[tr][c][G] : 0.0f;
+              svc[tr][c][G] = live ? svc[tr][c][G] : 0.0f;
+              bvc[tr][c][G] = live ? bvc[tr][c][G] : 0.0f;
             }
           }
       }
+      const uint8_t* vbase = stg + LY::OFF_V + hh * 16 * VROW;
 #pragma unroll
       for (int G = 0; G < NGV; ++G) {
-        vbias[0][G] = fmaf(pr[0], bv[0][0][G], fmaf(pr[2], bv[1][0][G], vbias[0][G]));
-        vbias[1][G] = fmaf(pr[1], bv[0][1][G], fmaf(pr[3], bv[1][1][G], vbias[1][G]));
-        const uint32_t blo = movmatrix_trans(pack_half2(pr[0] * sv[0][0][G], pr[1] * sv[0][1][G]));
-        const uint32_t bhi = movmatrix_trans(pack_half2(pr[2] * sv[1][0][G], pr[3] * sv[1][1][G]));
+        vbias[0][G] = fmaf(pr[0], bvc[0][0][G], fmaf(pr[2], bvc[1][0][G], vbias[0][G]));
+        vbias[1][G] = fmaf(pr[1], bvc[0][1][G], fmaf(pr[3], bvc[1][1][G], vbias[1][G]));
+        const uint32_t bl = movmatrix_trans(pack_half2(pr[0] * svc[0][0][G], pr[1] * svc[0][1][G]));
+        const uint32_t bh = movmatrix_trans(pack_half2(pr[2] * svc[1][0][G], pr[3] * svc[1][1][G]));
+        const int woff = (8 * G + g) * 4;
+        const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * VROW + woff);
+        const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * VROW + woff);
+        const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * VROW + woff);
+        const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * VROW + woff);
 #pragma unroll
-        for (int hp = 0; hp < HP; ++hp) {
-          const uint32_t bl = (HP == 1 || hp == my_hp_g) ? blo : 0u;
-          const uint32_t bh = (HP == 1 || hp == my_hp_g) ? bhi : 0u;
-          const uint8_t* vbase = stg + hp * HB + LY::H_OFF_V + hh * 16 * VROW;
-          const int woff = (8 * G + g) * 4;
-          const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * VROW + woff);
-          const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * VROW + woff);
-          const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * VROW + woff);
-          const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * VROW + woff);
-#pragma unroll
-          for (int beta = 0; beta < 4; ++beta) {
-            const uint32_t sel = beta | ((4 + beta) << 8);
-            const uint32_t r01 = __byte_perm(v0, v1, sel);
-            const uint32_t r23 = __byte_perm(v2, v3, sel);
-            mma_f16_16816(o[4 * G + beta], r01 & 0x000F000Fu, r01 & 0x00F000F0u, r23 & 0x000F000Fu,
-                          r23 & 0x00F000F0u, bl, bh);
-          }
+        for (int beta = 0; beta < 4; ++beta) {
+          const uint32_t sel = beta | ((4 + beta) << 8);
+          const uint32_t r01 = __byte_perm(v0, v1, sel);
+          const uint32_t r23 = __byte_perm(v2, v3, sel);
+          mma_f16_16816(o[4 * G + beta], r01 & 0x000F000Fu, r01 & 0x00F000F0u, r23 & 0x000F000Fu,
+                        r23 & 0x00F000F0u, bl, bh);
         }
       }
     }
@@ -603,7 +586,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       for (int G = 0; G < NGV; ++G) vbias[c][G] += __shfl_xor_sync(0xffffffffu, vbias[c][G], off);
     }
   }
-  // warp result into this warp's (now idle) ring: m[8], l[8], O[8][DV]
+  // warp result into this warp's (now idle) ring: m[8], l[8], then O[8][DV + 1] (the odd
+  // row stride keeps the fragment-order stores at most 2-way bank conflicted)
+  constexpr int OS = DV + 1;
   float* wres = reinterpret_cast<float*>(ring);
   if (g == 0) {
     wres[2 * t] = m_run[0];
@@ -616,44 +601,51 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   for (int mt_i = 0; mt_i < MT; ++mt_i) {
     const int G = mt_i / 4, beta = mt_i % 4;
     const int d = 64 * G + 8 * g + 2 * beta;
-    wo[(2 * t) * DV + d] = fmaf(o[mt_i][0], 16777216.0f, vbias[0][G]);
-    wo[(2 * t + 1) * DV + d] = fmaf(o[mt_i][1], 16777216.0f, vbias[1][G]);
-    wo[(2 * t) * DV + d + 1] = fmaf(o[mt_i][2], 1048576.0f, vbias[0][G]);
-    wo[(2 * t + 1) * DV + d + 1] = fmaf(o[mt_i][3], 1048576.0f, vbias[1][G]);
+    wo[(2 * t) * OS + d] = fmaf(o[mt_i][0], 16777216.0f, vbias[0][G]);
+    wo[(2 * t + 1) * OS + d] = fmaf(o[mt_i][1], 16777216.0f, vbias[1][G]);
+    wo[(2 * t) * OS + d + 1] = fmaf(o[mt_i][2], 1048576.0f, vbias[0][G]);
+    wo[(2 * t + 1) * OS + d + 1] = fmaf(o[mt_i][3], 1048576.0f, vbias[1][G]);
   }
   __syncthreads();
 
   // ------------------------------------------------------------------ CTA combine
-  const int rows_total = p.hq * p.q_len;
-  for (int i = tid; i < 8 * DV; i += 128) {
-    const int c = i / DV, d = i % DV;
-    const ColMap cm = col_map(c, HP, rph, rg);
-    if (!cm.valid) continue;
+  // Threads 0..7 merge the warps' (m, l) of one column each into per-warp weights, the CTA
+  // max and sum (in the block-id area, free after the loop); then every thread merges
+  // output elements.
+  float* cf = reinterpret_cast<float*>(smem + LY::OFF_BLK);  // [kWarps][8] weights, M[8], L[8], 1/L[8]
+  if (tid < 8) {
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, reinterpret_cast<const float*>(smem + w * LY::RING)[c]);
-    float L = 0.0f, O = 0.0f;
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, reinterpret_cast<const float*>(smem + w * LY::RING)[tid]);
+    float L = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
       const float* wr = reinterpret_cast<const float*>(smem + w * LY::RING);
-      const float mw = wr[c];
+      const float mw = wr[tid];
       const float sc = (mw == -INFINITY) ? 0.0f : ex2(mw - M);
-      L = fmaf(wr[8 + c], sc, L);
-      O = fmaf(wr[16 + c * DV + d], sc, O);
+      cf[w * 8 + tid] = sc;
+      L = fmaf(wr[8 + tid], sc, L);
     }
-    const int l = cm.rr / p.n_rep;
-    const int hq = (h0 + cm.hp) * p.n_rep + cm.rr % p.n_rep;
+    cf[kWarps * 8 + tid] = M;
+    cf[kWarps * 8 + 8 + tid] = L;
+    cf[kWarps * 8 + 16 + tid] = L > 0.0f ? __fdividef(1.0f, L) : 0.0f;
+  }
+  __syncthreads();
+  for (int i = tid; i < 8 * DV; i += 128) {
+    const int c = i / DV, d = i % DV;
+    if (!col_i[c * 4 + 3]) continue;
+    float O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w)
+      O = fmaf(reinterpret_cast<const float*>(smem + w * LY::RING)[16 + c * OS + d], cf[w * 8 + c], O);
     if (n_chunks_b == 1) {
-      const float val = L > 0.0f ? O / L : 0.0f;
-      store_out(p.out, (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + d, val,
-                p.out_dtype);
+      store_out(p.out, col_oo[c] + d, O * cf[kWarps * 8 + 16 + c], p.out_dtype);
     } else {
-      float* slot = p.ws + (((int64_t)b * rows_total + (int64_t)hq * p.q_len + l) * p.max_chunks +
-                            chunk) * (DV + kPartialHead);
+      float* slot = p.ws + col_wo[c];
       slot[kPartialHead + d] = O;
       if (d == 0) {
-        slot[0] = M;
-        slot[1] = L;
+        slot[0] = cf[kWarps * 8 + c];
+        slot[1] = cf[kWarps * 8 + 8 + c];
       }
     }
   }
@@ -678,9 +670,9 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
   const int n = p.kv_len[b];
   const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
   int lo, hi;
-  visible_range(n, st, p.q_len, p.window, p.mask_kind != AM_MASK_NONE, lo, hi);
+  visible_range(n, st, p.q_len, p.window, p.mask_kind != AM_MASK_NONE, p.stage_tokens, lo, hi);
   const int span = max(0, hi - lo);
-  const int nc = max(1, (span + p.chunk - 1) / p.chunk);
+  const int nc = min(max(1, (span + p.chunk - 1) / p.chunk), p.max_chunks);
   if (nc <= 1) return;
   const float* base = p.ws + ((int64_t)b * rows_total + row) * p.max_chunks * PF;
 
@@ -704,7 +696,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
       m = mn;
     }
   }
-  const float M = m, inv_l = l > 0.0f ? 1.0f / l : 0.0f;
+  const float M = m, inv_l = l > 0.0f ? __fdividef(1.0f, l) : 0.0f;
 
   float4 acc[PER];
 #pragma unroll
@@ -753,7 +745,13 @@ bool decode_supported(int k_dim, int v_dim) {
          (k_dim == 256 && v_dim == 256);
 }
 
-void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int* chunk, int* n_chunks) {
+// Split size (tokens per CTA chunk) for a decode call.  With fewer (sequence, KV head, row
+// group) pairs than CTA slots on the device, each pair is split into chunks; the split is
+// chosen by a small cost model: waves of CTAs x (fixed per-CTA cost + chunk tokens), where
+// the fixed cost (prologue, pipeline fill, CTA merge) is worth ~256 streamed tokens.  With
+// at least a full wave of pairs, chunks are as long as allowed (fewer partials to merge).
+void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_per_sm, int* chunk,
+                 int* n_chunks) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
@@ -761,15 +759,30 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int* chunk
     (void)cudaGetLastError();  // clear: this query must not poison a later launch check
   }
   const int64_t pairs = (int64_t)batch * n_kv_heads * row_groups;
-  const int64_t target = (int64_t)sms * 6;
-  const int64_t n_split = pairs >= target ? 1 : (target + pairs - 1) / pairs;
-  const int64_t span16 = (int64_t)span + 15;
-  int64_t c = (span16 + n_split - 1) / n_split;
-  c = (c + 63) / 64 * 64;
-  if (c < 128) c = 128;
-  if (c > 2048) c = 2048;
-  *chunk = static_cast<int>(c);
-  *n_chunks = static_cast<int>(span16 > 0 ? (span16 + c - 1) / c : 1);
+  const int64_t slots = (int64_t)sms * (ctas_per_sm > 0 ? ctas_per_sm : 1);
+  const int64_t sp = span > 0 ? span : 1;
+  auto chunk_for = [&](int64_t n_split) {
+    int64_t c = (sp + n_split - 1) / n_split;
+    c = (c + 63) / 64 * 64;
+    return c < 128 ? (int64_t)128 : (c > kMaxChunk ? (int64_t)kMaxChunk : c);
+  };
+  int64_t best_c = chunk_for(1);
+  if (pairs < slots) {
+    constexpr int64_t kFixed = 256;
+    int64_t best_cost = -1;
+    const int64_t max_split = (4 * slots + pairs - 1) / pairs;
+    for (int64_t n = 1; n <= max_split; ++n) {
+      const int64_t c = chunk_for(n);
+      const int64_t ctas = pairs * ((sp + c - 1) / c);
+      const int64_t cost = ((ctas + slots - 1) / slots) * (kFixed + c);
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        best_c = c;
+      }
+    }
+  }
+  *chunk = static_cast<int>(best_c);
+  *n_chunks = static_cast<int>((sp + best_c - 1) / best_c);
   if (*n_chunks < 1) *n_chunks = 1;
 }
 
@@ -811,19 +824,27 @@ static cudaError_t set_smem_once(F kfn, int bytes, unsigned long long* done_mask
   return e;
 }
 
-template <int DK, int DV, bool SBF16, bool PAGED, int HP>
+// Stage geometry of an instantiation: 64-token stages when a token row of K and V is
+// small (Dk + Dv <= 256), so the per-stage work (copy issue, barrier wait, softmax max)
+// is spread over more tokens; 32-token stages for larger heads.  Three stages per warp
+// when a stage is at most 6 KB, else two.
+template <int DK, int DV>
+struct DecodeCfg {
+  static constexpr int TS = DK + DV <= 256 ? 64 : 32;
+  static constexpr int NS = DecodeLayout<DK, DV, 3, TS>::STAGE <= 6144 ? 3 : 2;
+  using LY = DecodeLayout<DK, DV, NS, TS>;
+};
+
+template <int DK, int DV, bool SBF16, bool PAGED>
 static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_groups,
                                    cudaStream_t stream) {
-  // 32-token stages for one head; 16-token stages when several heads share the CTA, so a
-  // stage stays ~5 KB and three stages per warp fit three CTAs per SM
-  constexpr int TS = HP > 1 ? 16 : 32;
-  constexpr int NS = DecodeLayout<DK, DV, 3, HP, TS>::STAGE <= 6144 ? 3 : 2;
-  using LY = DecodeLayout<DK, DV, NS, HP, TS>;
-  auto kfn = decode_kernel<DK, DV, SBF16, PAGED, NS, HP, TS>;
+  using CF = DecodeCfg<DK, DV>;
+  using LY = typename CF::LY;
+  auto kfn = decode_kernel<DK, DV, SBF16, PAGED, CF::NS, CF::TS>;
   static unsigned long long smem_done = 0;
   cudaError_t e = set_smem_once(kfn, LY::SMEM, &smem_done);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.max_chunks, (p.hkv / HP) * row_groups, batch);
+  dim3 grid(p.max_chunks, p.hkv * row_groups, batch);
   e = launch_pdl(kfn, grid, dim3(128), LY::SMEM, stream, p);
   if (e != cudaSuccess) return e;
   if (p.max_chunks > 1) {
@@ -833,46 +854,65 @@ static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_gro
   return e;
 }
 
-template <int DK, int DV, int HP>
-static cudaError_t launch_decode_hp(const DecodeParams& p, int batch, int row_groups, bool paged,
-                                    bool sbf16, cudaStream_t stream) {
-  if (paged) {
-    return sbf16 ? launch_decode_t<DK, DV, true, true, HP>(p, batch, row_groups, stream)
-                 : launch_decode_t<DK, DV, false, true, HP>(p, batch, row_groups, stream);
+// Resident decode CTAs per SM for a head-dim pair (the paged fp16-scale instantiation
+// stands for all four: same registers and shared memory), cached per device.
+template <int DK, int DV>
+static int ctas_per_sm_t() {
+  using CF = DecodeCfg<DK, DV>;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 1;
   }
-  return sbf16 ? launch_decode_t<DK, DV, true, false, HP>(p, batch, row_groups, stream)
-               : launch_decode_t<DK, DV, false, false, HP>(p, batch, row_groups, stream);
+  if (dev >= 0 && dev < 64) {
+    const int v = __atomic_load_n(&cache[dev], __ATOMIC_ACQUIRE);
+    if (v > 0) return v;
+  }
+  auto kfn = decode_kernel<DK, DV, false, true, CF::NS, CF::TS>;
+  static unsigned long long smem_done = 0;
+  int n = 0;
+  if (set_smem_once(kfn, CF::LY::SMEM, &smem_done) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kfn, 128, CF::LY::SMEM) != cudaSuccess ||
+      n < 1) {
+    (void)cudaGetLastError();
+    return 1;
+  }
+  if (dev >= 0 && dev < 64) __atomic_store_n(&cache[dev], n, __ATOMIC_RELEASE);
+  return n;
 }
 
-#ifndef AM_DECODE_MAX_HP
-#define AM_DECODE_MAX_HP 1
-#endif
+int decode_ctas_per_sm(int k_dim, int v_dim) {
+  if (k_dim == 64 && v_dim == 64) return ctas_per_sm_t<64, 64>();
+  if (k_dim == 128 && v_dim == 128) return ctas_per_sm_t<128, 128>();
+  if (k_dim == 128 && v_dim == 64) return ctas_per_sm_t<128, 64>();
+  if (k_dim == 192 && v_dim == 128) return ctas_per_sm_t<192, 128>();
+  if (k_dim == 256 && v_dim == 256) return ctas_per_sm_t<256, 256>();
+  return 1;
+}
 
-int decode_max_heads_per_cta(int k_dim, int v_dim) {
-  int cap = 1;
-  if (k_dim == 64 && v_dim == 64) cap = 4;
-  if (k_dim == 128 && v_dim == 128) cap = 2;
-  if (k_dim == 192 && v_dim == 128) cap = 2;
-  return cap < AM_DECODE_MAX_HP ? cap : AM_DECODE_MAX_HP;
+int decode_stage_tokens(int k_dim, int v_dim) { return k_dim + v_dim <= 256 ? 64 : 32; }
+
+template <int DK, int DV>
+static cudaError_t launch_decode_d(const DecodeParams& p, int batch, int row_groups, bool paged,
+                                   bool sbf16, cudaStream_t stream) {
+  if (paged) {
+    return sbf16 ? launch_decode_t<DK, DV, true, true>(p, batch, row_groups, stream)
+                 : launch_decode_t<DK, DV, false, true>(p, batch, row_groups, stream);
+  }
+  return sbf16 ? launch_decode_t<DK, DV, true, false>(p, batch, row_groups, stream)
+               : launch_decode_t<DK, DV, false, false>(p, batch, row_groups, stream);
 }
 
 cudaError_t launch_decode(const DecodeParams& p, int batch, int row_groups, bool paged,
                           bool scale_bf16, cudaStream_t stream) {
   const int dk = p.k_dim, dv = p.v_dim;
-#if AM_DECODE_MAX_HP > 1
-  // Packing several KV heads per CTA (built with -DAM_DECODE_MAX_HP=2/4) measured slower on
-  // B200 than one head per CTA, so the default build only instantiates heads_per_cta = 1.
-  const int hp = p.heads_per_cta;
-  if (dk == 64 && dv == 64 && hp == 4) return launch_decode_hp<64, 64, 4>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 64 && dv == 64 && hp == 2) return launch_decode_hp<64, 64, 2>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 128 && dv == 128 && hp == 2) return launch_decode_hp<128, 128, 2>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 192 && dv == 128 && hp == 2) return launch_decode_hp<192, 128, 2>(p, batch, row_groups, paged, scale_bf16, stream);
-#endif
-  if (dk == 64 && dv == 64) return launch_decode_hp<64, 64, 1>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 128 && dv == 128) return launch_decode_hp<128, 128, 1>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 128 && dv == 64) return launch_decode_hp<128, 64, 1>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 192 && dv == 128) return launch_decode_hp<192, 128, 1>(p, batch, row_groups, paged, scale_bf16, stream);
-  if (dk == 256 && dv == 256) return launch_decode_hp<256, 256, 1>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (p.stage_tokens != decode_stage_tokens(dk, dv)) return cudaErrorInvalidValue;
+  if (dk == 64 && dv == 64) return launch_decode_d<64, 64>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 128 && dv == 128) return launch_decode_d<128, 128>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 128 && dv == 64) return launch_decode_d<128, 64>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 192 && dv == 128) return launch_decode_d<192, 128>(p, batch, row_groups, paged, scale_bf16, stream);
+  if (dk == 256 && dv == 256) return launch_decode_d<256, 256>(p, batch, row_groups, paged, scale_bf16, stream);
   return cudaErrorNotSupported;
 }
 

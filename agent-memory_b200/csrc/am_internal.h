@@ -21,7 +21,8 @@ cudaError_t launch_append(const AppendParams& p, bool bf16, cudaStream_t stream)
 
 // Decode: returns cudaErrorNotSupported (without launching) for head dims without a kernel.
 bool decode_supported(int k_dim, int v_dim);
-int decode_max_heads_per_cta(int k_dim, int v_dim);
+// Tokens per decode pipeline stage for a head-dim pair (paged blocks must hold a whole stage).
+int decode_stage_tokens(int k_dim, int v_dim);
 cudaError_t launch_decode(const DecodeParams& p, int batch, int row_groups, bool paged,
                           bool scale_bf16, cudaStream_t stream);
 
@@ -30,6 +31,9 @@ cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool sc
                            cudaStream_t stream);
 
 // Split size (tokens per CTA chunk) and number of chunks for a decode call.
-void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int* chunk, int* n_chunks);
+void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_per_sm, int* chunk,
+                 int* n_chunks);
+// Resident decode CTAs per SM on the current device for a (k_dim, v_dim) pair.
+int decode_ctas_per_sm(int k_dim, int v_dim);
 
 }  // namespace am

@@ -108,11 +108,11 @@ def test_decode_fully_masked_row_is_uniform(cuda, orc):
 
 
 @pytest.mark.parametrize("geom", [(16, 8, 256), (32, 8, 128), (8, 8, 64), (16, 16, 192)],
-                         ids=["gemma256", "llama128_2heads_per_cta", "mha64_4heads_per_cta", "mla192"])
+                         ids=["gemma256", "llama128_gqa4", "mha64", "mla192"])
 @pytest.mark.parametrize("window", [0, 64, 1024])
 def test_decode_left_padding_and_window(cuda, orc, window, geom):
     """Structured mask from BatchQuantizedKVCache.make_mask: left padding + sliding window,
-    for one KV head per CTA and for several KV heads packed into one CTA."""
+    for GQA, MHA and MLA geometries."""
     Hq, Hkv, D = geom
     B, N = 3, 1500
     if D == 192:
@@ -133,6 +133,19 @@ def test_decode_left_padding_and_window(cuda, orc, window, geom):
     dense = mask.to_dense(cuda)
     got2 = pkg.quantized_scaled_dot_product_attention(q.to(cuda), kq, vq, D ** -0.5, dense)
     assert_close(got2.float().cpu().numpy(), want, what="dense form")
+
+
+@pytest.mark.parametrize("n,window", [(1027, 100), (1026, 99), (2047, 113), (700, 129), (4000, 1000)])
+def test_decode_window_stage_alignment(cuda, orc, n, window):
+    """The first visible key is rounded down to a pipeline stage boundary (32 or 64 tokens),
+    which can add up to a stage of keys to a window's span: spans that cross a chunk
+    boundary only after that rounding still attend every key of the window."""
+    q, kq, vq = make_case(1, 4, 1, n, 128, 128, cuda=cuda, seed=n + window)
+    lp = torch.zeros(1, dtype=torch.int64)
+    mask = pkg.CausalMask(1, n - 1, window, lp)
+    got = pkg.quantized_scaled_dot_product_attention(q.to(cuda), kq, vq, 128 ** -0.5, mask)
+    want = oracle(orc, q, kq, vq, 128 ** -0.5, causal=True, window=window, kv_start=lp.numpy())
+    assert_close(got.float().cpu().numpy(), want, what=f"n={n} window={window}")
 
 
 def test_batch_split_consistency(cuda):
