@@ -443,8 +443,8 @@ def cpu_baseline_multi_agent(args, lengths_all, layers, geo, budget_s=12.0, thre
     from oracle import q4_oracle as orc
 
     orc.build()
-    if threads:
-        orc.set_threads(threads)
+    # all host threads this process may use (launchers such as torchrun default OpenMP to 1)
+    orc.set_threads(threads or len(os.sched_getaffinity(0)))
     nthr = orc.num_threads()
     hq, hkv, dk, dv = geo["hq"], geo["hkv"], geo["dk"], geo["dv"]
     rng = np.random.default_rng(1234)
