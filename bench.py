@@ -60,6 +60,11 @@ def parse():
 # ------------------------------------------------------------------------------- helpers
 
 
+# DRAM bytes (read + write) per algorithmic byte of one decode launch, from the ncu capture
+# of the 32-agent x 2-layer case of this workload (traffic grows with the Q4 bytes read).
+DECODE_TRAFFIC_RATIO = 664.7 / 655.4
+
+
 def peaks():
     f = ROOT / "MEASURED_PEAKS.json"
     if f.exists():
@@ -70,7 +75,11 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed region.
+
+    Read-only NVML queries from a background thread every 5 ms, plus one sample when the
+    sampler starts and one when it stops, so short timed regions are covered; falls back to
+    `nvidia-smi -lms 200` when NVML is unavailable.  Nothing here changes a GPU setting."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -80,8 +89,49 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []
+        self._nv = None
+        self._handle = None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _nvml_handle(self):
+        import pynvml as nv
+
+        nv.nvmlInit()
+        try:
+            import torch
+
+            bus = torch.cuda.get_device_properties(self.index).pci_bus_id
+            pci = f"{torch.cuda.get_device_properties(self.index).pci_domain_id:08x}:{bus:02x}:" \
+                  f"{torch.cuda.get_device_properties(self.index).pci_device_id:02x}.0"
+            h = nv.nvmlDeviceGetHandleByPciBusId(pci)
+        except Exception:  # noqa: BLE001 - fall back to the NVML index
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+        return nv, h
+
+    def _sample(self):
+        nv, h = self._nv, self._handle
+        try:
+            self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                 float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)),
+                                 int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))))
+        except Exception:  # noqa: BLE001
+            pass
+
+    def _loop(self):
+        while not self._stop.wait(0.005):
+            self._sample()
 
     def start(self):
+        try:
+            self._nv, self._handle = self._nvml_handle()
+            self._sample()
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+            return
+        except Exception:  # noqa: BLE001 - no NVML: use nvidia-smi
+            self._nv = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
@@ -96,6 +146,22 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self._nv is not None:
+            self._sample()
+            self._stop.set()
+            if self._thread is not None:
+                self._thread.join(timeout=1)
+            nv = self._nv
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            if not self.samples:
+                return None
+            reasons = sorted({k for _, _, r in self.samples for k, bit in bits.items() if r & bit})
+            return {"sm_mhz": float(np.median([s for s, _, _ in self.samples])),
+                    "sm_max_mhz": max(m for _, m, _ in self.samples), "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml"}
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -119,7 +185,7 @@ class ClockSampler:
         if not sms:
             return None
         return {"sm_mhz": float(np.median(sms)), "sm_max_mhz": max(maxs),
-                "reasons": sorted(reasons), "samples": len(sms)}
+                "reasons": sorted(reasons), "samples": len(sms), "source": "nvidia-smi"}
 
 
 def agent_lengths(n_agents, lo, hi, seed):
@@ -311,7 +377,11 @@ def run_ours(args, rank, world, local_rank):
                          "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "bytes_per_launch": int(launch_bytes),
-                         "avg_launch_ms": round(avg_launch_s * 1e3, 4), "traffic": None},
+                         "avg_launch_ms": round(avg_launch_s * 1e3, 4),
+                         "traffic": round(launch_bytes * DECODE_TRAFFIC_RATIO),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                           "decode launch of the 32-agent case (664.7 MB for 655.4 MB "
+                                           "algorithmic), scaled by the bytes this launch processes"},
             "e2e": e2e,
             "gpu_launches": args.steps * layers * 3,
             "clocks": clk,
