@@ -15,10 +15,12 @@ from .cache import BatchQuantizedKVCache, QuantizedKVCache, validate_q4_pipeline
 from .kernels import dequantize, quantize
 from .masks import CausalMask, create_causal_mask
 from .paged import PagedLayerCache, PagedQ4Pool, lpt_partition, shuffled_allocator
+from .paged_cache import DeviceBlockPool, PagedBatchQuantizedKVCache, PagedKV, PagedMask
 
 __all__ = [
     "AgentBlocks", "BLOCK_SIZE_TOKENS", "BatchQuantizedKVCache", "BlockPool", "CausalMask",
-    "KVBlock", "ModelCacheSpec", "PagedLayerCache", "PagedQ4Pool", "PoolExhaustedError",
+    "DeviceBlockPool", "KVBlock", "ModelCacheSpec", "PagedBatchQuantizedKVCache", "PagedKV",
+    "PagedLayerCache", "PagedMask", "PagedQ4Pool", "PoolExhaustedError",
     "Q4KernelError", "Q4KernelUnavailable", "QuantizedKVCache", "apply_fused_attention_patch",
     "create_causal_mask", "dequantize", "lpt_partition", "quantize",
     "quantized_scaled_dot_product_attention", "scaled_dot_product_attention",

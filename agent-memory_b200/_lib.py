@@ -15,7 +15,7 @@ PKG_DIR = Path(__file__).resolve().parent
 LIB_NAME = "libamq4.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Status codes / enums (mirrors include/am_q4.h)
 AM_OK = 0
@@ -27,7 +27,7 @@ AM_ERR_CUDA = -4
 DTYPE_F16, DTYPE_BF16, DTYPE_F32, DTYPE_U8 = 0, 1, 2, 3
 LAYOUT_CONTIGUOUS, LAYOUT_PAGED = 0, 1
 MASK_NONE, MASK_BOOL, MASK_ADDITIVE = 0, 1, 2
-STATUS_BAD_BLOCK, STATUS_BAD_POSITION, STATUS_TIMEOUT = 1, 2, 4
+STATUS_BAD_BLOCK, STATUS_BAD_POSITION, STATUS_TIMEOUT, STATUS_POOL_EXHAUSTED = 1, 2, 4, 8
 
 EXPORTED_SYMBOLS = (
     "am_abi_version",
@@ -40,6 +40,10 @@ EXPORTED_SYMBOLS = (
     "am_q4_prefill",
     "am_q4_attention",
     "am_q4_decode_noalloc",
+    "am_q4_blocks_pack",
+    "am_q4_blocks_unpack",
+    "am_block_reserve",
+    "am_block_release",
 )
 STATIC_DECODE_SCRATCH_BYTES = 16 << 20
 
@@ -102,6 +106,7 @@ class AttnArgs(ctypes.Structure):
         ("mask_stride_l", c_int64),
         ("mask_stride_n", c_int64),
         ("status", c_void_p),
+        ("sinks", c_void_p),
     ]
 
 
@@ -163,6 +168,17 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     lib.am_q4_decode_noalloc.argtypes = [ctypes.POINTER(Q4CacheDesc), ctypes.POINTER(AttnArgs),
                                          c_void_p]
     lib.am_q4_decode_noalloc.restype = c_int32
+    for fn in ("am_q4_blocks_pack", "am_q4_blocks_unpack"):
+        f = getattr(lib, fn)
+        f.argtypes = [ctypes.POINTER(Q4CacheDesc), c_void_p, c_void_p, c_void_p, c_int32, c_void_p,
+                      c_void_p, c_void_p]
+        f.restype = c_int32
+    lib.am_block_reserve.argtypes = [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32,
+                                     c_void_p, c_void_p, c_int32, c_void_p, c_void_p]
+    lib.am_block_reserve.restype = c_int32
+    lib.am_block_release.argtypes = [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32,
+                                     c_void_p, c_void_p, c_void_p]
+    lib.am_block_release.restype = c_int32
     ver = lib.am_abi_version()
     if ver != ABI_VERSION:
         raise Q4KernelUnavailable(f"{p} has ABI version {ver}, expected {ABI_VERSION}")

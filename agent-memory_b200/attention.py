@@ -28,6 +28,7 @@ import torch
 
 from . import kernels
 from .masks import CausalMask
+from .paged_cache import PagedKV, PagedMask
 
 _dispatch_module: Any = None  # module patched by apply_fused_attention_patch
 
@@ -60,10 +61,17 @@ def _as_mask_args(mask, B: int, L: int, N: int, device: torch.device):
 
 
 def quantized_scaled_dot_product_attention(queries: torch.Tensor, q_keys, q_values, scale: float,
-                                           mask=None, group_size: int = 64, bits: int = 4):
-    """Q4 scaled dot-product attention on the GPU (see module docstring)."""
+                                           mask=None, group_size: int = 64, bits: int = 4,
+                                           sinks: torch.Tensor | None = None):
+    """Q4 scaled dot-product attention on the GPU (see module docstring).
+
+    ``sinks`` (optional [Hq] logits, scaled-score units) adds one value-less key per head to
+    the softmax normaliser, as mx.fast.scaled_dot_product_attention(..., sinks=) does on
+    the reference's dequantized fallback (mlx_sink_compat.py:46-69)."""
     kernels._check_params(group_size, bits)
     B, Hq, L, Dk = queries.shape
+    if isinstance(q_keys, PagedKV):
+        return _paged_attention(queries, q_keys.cache, scale, mask, sinks)
     view, N = kernels.contiguous_view(q_keys, q_values)
     if Hq % view.n_kv_heads:
         raise ValueError(f"{Hq} query heads is not a multiple of {view.n_kv_heads} KV heads")
@@ -72,7 +80,29 @@ def quantized_scaled_dot_product_attention(queries: torch.Tensor, q_keys, q_valu
     causal, window, kv_start, dense = _as_mask_args(mask, B, L, N, queries.device)
     kv_len = torch.full((B,), N, dtype=torch.int32, device=queries.device)
     return kernels.attention(view, queries, scale, kv_len, N, kv_start=kv_start, causal=causal,
-                             window=window, mask=dense, out_dtype=queries.dtype)
+                             window=window, mask=dense, out_dtype=queries.dtype, sinks=sinks)
+
+
+def _paged_attention(queries, cache, scale, mask, sinks):
+    """The drop-in op over a PagedBatchQuantizedKVCache (keys/values from its
+    update_and_fetch): each row attends its own [0, len) keys through the block table;
+    query l of row b sits at position len[b] - L + l."""
+    B, Hq, L, _ = queries.shape
+    if B != cache.rows:
+        raise ValueError(f"queries have batch {B}, the paged cache has {cache.rows} rows")
+    causal, window, dense = False, 0, None
+    if isinstance(mask, str):
+        if mask != "causal":
+            raise ValueError(f"unknown mask string {mask!r}")
+        causal = True
+    elif isinstance(mask, (PagedMask, CausalMask)):
+        causal, window = True, int(mask.window_size or 0)
+    elif mask is not None:
+        dense = mask.to(queries.device)
+        while dense.dim() < 4:
+            dense = dense.unsqueeze(0)
+    return kernels.attention(cache.view(), queries, scale, cache.kv_len, cache._idx, causal=causal,
+                             window=window, mask=dense, out_dtype=queries.dtype, sinks=sinks)
 
 
 def scaled_dot_product_attention(queries: torch.Tensor, keys, values, cache, scale: float, mask,
@@ -80,20 +110,24 @@ def scaled_dot_product_attention(queries: torch.Tensor, keys, values, cache, sca
     """Dispatch shim of mlx_sink_compat._patched_sdpa (mlx_sink_compat.py:36-89).
 
     With a quantized cache (an object with ``bits``) and no sinks, routes to the Q4 op that
-    is currently installed on the patched module (dynamic lookup, :70-81).  Attention sinks
-    over a Q4 cache (GPT-OSS) have no kernel here and raise.  Non-quantized caches use
-    PyTorch's SDPA (not part of the Q4 hot path).
+    is currently installed on the patched module (dynamic lookup, :70-81).  With sinks
+    (GPT-OSS), the reference dequantizes the Q4 tuples to fp16 and calls the fast SDPA
+    (:46-69); here the Q4 kernels take the sinks directly, with no fp16 copy of the cache.
+    Non-quantized caches use PyTorch math (not part of the Q4 hot path).
     """
     if hasattr(cache, "bits"):
         if sinks is not None:
-            raise NotImplementedError("attention sinks over a Q4 cache are not implemented")
+            return quantized_scaled_dot_product_attention(
+                queries, keys, values, scale, mask, group_size=cache.group_size, bits=cache.bits,
+                sinks=sinks)
         op = getattr(_dispatch_module, "quantized_scaled_dot_product_attention",
                      quantized_scaled_dot_product_attention)
         return op(queries, keys, values, scale=scale, mask=mask, group_size=cache.group_size,
                   bits=cache.bits)
-    if sinks is not None:
-        raise NotImplementedError("attention sinks are not implemented")
     import torch.nn.functional as F
+
+    if sinks is not None:
+        return _sdpa_with_sinks(queries, keys, values, scale, mask, sinks)
 
     attn_mask = mask
     is_causal = False
@@ -107,6 +141,26 @@ def scaled_dot_product_attention(queries: torch.Tensor, keys, values, cache, sca
         values = values.repeat_interleave(n_rep, dim=1)
     return F.scaled_dot_product_attention(queries, keys, values, attn_mask=attn_mask,
                                           is_causal=is_causal, scale=scale)
+
+
+def _sdpa_with_sinks(queries, keys, values, scale, mask, sinks):
+    """Dense attention with per-head sink logits (fp32 math; the non-Q4 fallback)."""
+    B, Hq, L, _ = queries.shape
+    n_rep = Hq // keys.shape[1]
+    k = keys.repeat_interleave(n_rep, dim=1).float()
+    v = values.repeat_interleave(n_rep, dim=1).float()
+    s = (queries.float() * scale) @ k.transpose(-1, -2)
+    N = s.shape[-1]
+    if isinstance(mask, str):
+        keep = torch.arange(N - L, N, device=s.device)[:, None] >= torch.arange(N, device=s.device)[None]
+        s = s.masked_fill(~keep, float("-inf"))
+    elif isinstance(mask, CausalMask):
+        s = s.masked_fill(~mask.to_dense(s.device), float("-inf"))
+    elif mask is not None:
+        s = s.masked_fill(~mask, float("-inf")) if mask.dtype == torch.bool else s + mask.float()
+    sk = sinks.to(device=s.device, dtype=torch.float32).view(1, Hq, 1, 1).expand(B, Hq, L, 1)
+    p = torch.softmax(torch.cat([s, sk], dim=-1), dim=-1)[..., :N]
+    return (p @ v).to(queries.dtype)
 
 
 def apply_fused_attention_patch(base_module: Any) -> bool:

@@ -17,7 +17,8 @@ CSRC = PKG_DIR / "csrc"
 INCLUDE = REPO / "include"
 OUT = PKG_DIR / "libamq4.so"
 
-SOURCES = ["am_abi.cu", "am_quantize.cu", "am_decode.cu", "am_prefill.cu", "am_noalloc.cu"]
+SOURCES = ["am_abi.cu", "am_quantize.cu", "am_decode.cu", "am_prefill.cu", "am_noalloc.cu",
+           "am_blocks.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

@@ -1,7 +1,9 @@
 // C ABI of libamq4.so: argument validation, dispatch to the kernel launchers, and
 // per-thread error reporting.  The library allocates no device memory and keeps no
 // pointer after a call returns.
+#include <climits>
 #include <cmath>
+#include <cstdint>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -184,6 +186,7 @@ static void fill_params(DecodeParams& p, const am_q4_cache* cache, const am_attn
   p.kv_start = a->kv_start;
   p.causal = a->causal;
   p.window = a->window;
+  p.sinks = a->sinks;
   p.mask_kind = a->mask_kind;
   p.mask_dtype = a->mask_dtype;
   p.mask = a->mask;
@@ -384,6 +387,119 @@ int am_q4_attention(const am_q4_cache* cache, const am_attn_args* a, void* works
     }
   }
   return am_q4_decode(cache, a, workspace, workspace_bytes, stream);
+}
+
+static int blocks_copy(const am_q4_cache* pool, const int32_t* block_ids, const int32_t* tokens,
+                       const int64_t* offsets, int32_t n_blocks, void* buffer, int32_t* status,
+                       void* stream, bool to_buffer, const char* fn) {
+  clear_error();
+  if (pool == nullptr || pool->layout != AM_LAYOUT_PAGED) {
+    set_error("%s: pool must describe a paged cache", fn);
+    return AM_ERR_INVALID;
+  }
+  if (!pool->k_codes || !pool->k_scales || !pool->k_biases || !pool->v_codes || !pool->v_scales ||
+      !pool->v_biases || !valid_half_dtype(pool->scale_dtype) || pool->n_kv_heads <= 0 ||
+      pool->k_dim <= 0 || pool->v_dim <= 0 || pool->k_dim % 64 || pool->v_dim % 64 ||
+      pool->block_tokens <= 0 || pool->capacity <= 0 || pool->capacity > INT32_MAX) {
+    set_error("%s: incomplete pool description", fn);
+    return AM_ERR_INVALID;
+  }
+  if (n_blocks < 0 || (n_blocks > 0 && (!block_ids || !tokens || !offsets || !buffer))) {
+    set_error("%s: n_blocks >= 0 and block_ids, tokens, offsets, buffer required", fn);
+    return AM_ERR_INVALID;
+  }
+  if (n_blocks == 0) return AM_OK;
+  BlockCopyParams p{};
+  p.pool[0] = const_cast<uint32_t*>(pool->k_codes);
+  p.pool[1] = const_cast<void*>(pool->k_scales);
+  p.pool[2] = const_cast<void*>(pool->k_biases);
+  p.pool[3] = const_cast<uint32_t*>(pool->v_codes);
+  p.pool[4] = const_cast<void*>(pool->v_scales);
+  p.pool[5] = const_cast<void*>(pool->v_biases);
+  p.row_bytes[0] = pool->k_dim / 2;
+  p.row_bytes[1] = p.row_bytes[2] = pool->k_dim / 64 * 2;
+  p.row_bytes[3] = pool->v_dim / 2;
+  p.row_bytes[4] = p.row_bytes[5] = pool->v_dim / 64 * 2;
+  p.hkv = pool->n_kv_heads;
+  p.block_tokens = pool->block_tokens;
+  p.num_blocks = static_cast<int32_t>(pool->capacity);
+  p.block_ids = block_ids;
+  p.tokens = tokens;
+  p.offsets = offsets;
+  p.buf = static_cast<uint8_t*>(buffer);
+  p.to_buffer = to_buffer ? 1 : 0;
+  p.status = status;
+  return cuda_status(launch_blocks_copy(p, n_blocks, static_cast<cudaStream_t>(stream)), fn);
+}
+
+int am_q4_blocks_pack(const am_q4_cache* pool, const int32_t* block_ids, const int32_t* tokens,
+                      const int64_t* offsets, int32_t n_blocks, void* buffer, int32_t* status,
+                      void* stream) {
+  return blocks_copy(pool, block_ids, tokens, offsets, n_blocks, buffer, status, stream, true,
+                     "am_q4_blocks_pack");
+}
+
+int am_q4_blocks_unpack(const am_q4_cache* pool, const int32_t* block_ids, const int32_t* tokens,
+                        const int64_t* offsets, int32_t n_blocks, const void* buffer,
+                        int32_t* status, void* stream) {
+  return blocks_copy(pool, block_ids, tokens, offsets, n_blocks, const_cast<void*>(buffer), status,
+                     stream, false, "am_q4_blocks_unpack");
+}
+
+static int block_list_check(int32_t* free_ids, int32_t* free_top, int32_t num_blocks,
+                            int32_t* table, int32_t table_stride, int32_t rows,
+                            const int32_t* counts, const char* fn) {
+  clear_error();
+  if (!free_ids || !free_top || num_blocks <= 0 || rows < 0 || table_stride <= 0 ||
+      (rows > 0 && (!table || !counts))) {
+    set_error("%s: free list, table (stride > 0) and per-row counts required", fn);
+    return AM_ERR_INVALID;
+  }
+  return AM_OK;
+}
+
+int am_block_reserve(int32_t* free_ids, int32_t* free_top, int32_t num_blocks, int32_t* table,
+                     int32_t table_stride, int32_t rows, const int32_t* lengths,
+                     const int32_t* add, int32_t block_tokens, int32_t* status, void* stream) {
+  int rc = block_list_check(free_ids, free_top, num_blocks, table, table_stride, rows, add,
+                            "am_block_reserve");
+  if (rc) return rc;
+  if (rows > 0 && (lengths == nullptr || block_tokens <= 0)) {
+    set_error("am_block_reserve: lengths and block_tokens > 0 required");
+    return AM_ERR_INVALID;
+  }
+  if (rows == 0) return AM_OK;
+  BlockListParams p{};
+  p.free_ids = free_ids;
+  p.free_top = free_top;
+  p.capacity = num_blocks;
+  p.table = table;
+  p.table_stride = table_stride;
+  p.rows = rows;
+  p.lengths = lengths;
+  p.counts = add;
+  p.block_tokens = block_tokens;
+  p.status = status;
+  return cuda_status(launch_block_reserve(p, static_cast<cudaStream_t>(stream)), "am_block_reserve");
+}
+
+int am_block_release(int32_t* free_ids, int32_t* free_top, int32_t num_blocks, int32_t* table,
+                     int32_t table_stride, int32_t rows, const int32_t* keep_blocks,
+                     int32_t* status, void* stream) {
+  int rc = block_list_check(free_ids, free_top, num_blocks, table, table_stride, rows, keep_blocks,
+                            "am_block_release");
+  if (rc) return rc;
+  if (rows == 0) return AM_OK;
+  BlockListParams p{};
+  p.free_ids = free_ids;
+  p.free_top = free_top;
+  p.capacity = num_blocks;
+  p.table = table;
+  p.table_stride = table_stride;
+  p.rows = rows;
+  p.counts = keep_blocks;
+  p.status = status;
+  return cuda_status(launch_block_release(p, static_cast<cudaStream_t>(stream)), "am_block_release");
 }
 
 }  // extern "C"

@@ -175,11 +175,52 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
+// Final softmax normalisation of one query row from its running max m and sum l (log2
+// units), with an optional attention sink s2 (log2 units): returns the factor that turns
+// the unnormalised output O into O * w / den, i.e. w / den, so that
+// out = O * factor.  Without a sink: 1 / l.  With one: the sink joins max and sum.
+__device__ __forceinline__ float softmax_out_factor(float m, float l, bool has_sink, float s2) {
+  if (!has_sink) return l > 0.0f ? __fdividef(1.0f, l) : 0.0f;
+  const float mm = fmaxf(m, s2);
+  const float w = m == -INFINITY ? 0.0f : exp2f(m - mm);
+  const float den = fmaf(l, w, exp2f(s2 - mm));
+  return den > 0.0f ? __fdividef(w, den) : 0.0f;
+}
+
 // Split-KV partial record of one query row and chunk: m, l, two pad words (so O starts
 // 16-byte aligned), then O[DV].
 constexpr int kPartialHead = 4;
 
 // ---------------------------------------------------------------- launch parameters
+
+// Whole-block copies between the pool and a packed buffer (am_blocks.cu).  Sections:
+// 0 K weights, 1 K scales, 2 K biases, 3 V weights, 4 V scales, 5 V biases.
+struct BlockCopyParams {
+  void* pool[6];
+  int64_t row_bytes[6];
+  int32_t hkv, block_tokens, num_blocks;
+  const int32_t* block_ids;
+  const int32_t* tokens;
+  const int64_t* offsets;  // [n_blocks][6] byte offsets into buf
+  uint8_t* buf;
+  int32_t to_buffer;
+  int32_t* status;
+};
+
+// Device free list (am_blocks.cu).  counts = tokens to add (reserve) or blocks to keep
+// (release) per row.
+struct BlockListParams {
+  int32_t* free_ids;
+  int32_t* free_top;
+  int32_t capacity;
+  int32_t* table;
+  int32_t table_stride;
+  int32_t rows;
+  const int32_t* lengths;
+  const int32_t* counts;
+  int32_t block_tokens;
+  int32_t* status;
+};
 
 // Quantize-on-append / plain quantize.  Rows are (b, h, l) triples of the source tensors.
 struct AppendParams {
@@ -245,6 +286,7 @@ struct DecodeParams {
   int32_t chunk;       // tokens per split (multiple of 64)
   int32_t max_chunks;  // grid.x
   float* ws;           // partials [batch][hq*q_len][max_chunks][kPartialHead + v_dim]
+  const float* sinks;  // [hq] sink logits (scaled-score units) or nullptr
 };
 
 // Visible key range of a sequence for the structured mask: keys outside [lo, hi) are

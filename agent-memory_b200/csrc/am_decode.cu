@@ -628,7 +628,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     }
     cf[kWarps * 8 + tid] = M;
     cf[kWarps * 8 + 8 + tid] = L;
-    cf[kWarps * 8 + 16 + tid] = L > 0.0f ? __fdividef(1.0f, L) : 0.0f;
+    const bool sink = p.sinks != nullptr;
+    cf[kWarps * 8 + 16 + tid] =
+        softmax_out_factor(M, L, sink, sink ? p.sinks[col_i[tid * 4 + 0]] * 1.4426950408889634f : 0.0f);
   }
   __syncthreads();
   for (int i = tid; i < 8 * DV; i += 128) {
@@ -696,7 +698,10 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
       m = mn;
     }
   }
-  const float M = m, inv_l = l > 0.0f ? __fdividef(1.0f, l) : 0.0f;
+  const int hq = row / p.q_len, lq = row % p.q_len;
+  const float M = m;
+  const bool sink = p.sinks != nullptr;
+  const float inv_l = softmax_out_factor(m, l, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
 
   float4 acc[PER];
 #pragma unroll
@@ -723,7 +728,6 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
       }
     }
   }
-  const int hq = row / p.q_len, lq = row % p.q_len;
   const int64_t o0 = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)lq * p.osl;
 #pragma unroll
   for (int k = 0; k < PER; ++k) {

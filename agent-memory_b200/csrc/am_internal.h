@@ -11,6 +11,8 @@ namespace am {
 
 struct AppendParams;
 struct DecodeParams;
+struct BlockCopyParams;
+struct BlockListParams;
 
 cudaError_t launch_quantize(const void* x, bool bf16, int64_t rows, int dim, uint32_t* codes,
                             void* scales, void* biases, cudaStream_t stream);
@@ -35,5 +37,9 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_p
                  int* n_chunks);
 // Resident decode CTAs per SM on the current device for a (k_dim, v_dim) pair.
 int decode_ctas_per_sm(int k_dim, int v_dim);
+
+cudaError_t launch_blocks_copy(const BlockCopyParams& p, int n_blocks, cudaStream_t stream);
+cudaError_t launch_block_reserve(const BlockListParams& p, cudaStream_t stream);
+cudaError_t launch_block_release(const BlockListParams& p, cudaStream_t stream);
 
 }  // namespace am

@@ -481,7 +481,9 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
     }
     // ---- epilogue: this thread's output row
     if (row_ok && !*abort_flag) {
-      const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      const bool sink = p.sinks != nullptr;
+      const float inv =
+          softmax_out_factor(m_run, l_run, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
       const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl;
       if (p.out_dtype == AM_DTYPE_F32) {
         float* o = static_cast<float*>(p.out) + ob;

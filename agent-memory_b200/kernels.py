@@ -298,11 +298,12 @@ def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torc
               max_kv_len: int, *, kv_start: torch.Tensor | None = None, causal: bool = False,
               window: int = 0, mask: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
               out: torch.Tensor | None = None, status: torch.Tensor | None = None,
-              mode: str = "auto") -> torch.Tensor:
+              mode: str = "auto", sinks: torch.Tensor | None = None) -> torch.Tensor:
     """Attention of queries [B, Hq, L, Dk] over the cache -> [B, Hq, L, Dv].
 
     kv_len/kv_start: int32 device tensors [B].  mode: "auto" (library dispatch), "decode"
-    (split-KV kernel) or "prefill" (tcgen05 kernel).
+    (split-KV kernel) or "prefill" (tcgen05 kernel).  sinks: optional [Hq] attention-sink
+    logits (scaled-score units).
     """
     dev = _require_cuda(queries, kv_len)
     B, Hq, L, Dk = queries.shape
@@ -339,6 +340,14 @@ def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torc
     a.max_kv_len = int(max_kv_len)
     _mask_args(a, mask, keep)
     a.status = status.data_ptr() if status is not None else None
+    if sinks is not None:
+        sk = torch.as_tensor(sinks).to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+        if sk.numel() != Hq:
+            raise ValueError(f"sinks must hold one logit per query head ({Hq}), got {sk.numel()}")
+        keep.append(sk)
+        a.sinks = sk.data_ptr()
+    else:
+        a.sinks = None
     L_ = _lib.load()
     ws_bytes = L_.am_q4_attention_workspace_bytes(ctypes.byref(view.desc), ctypes.byref(a))
     ws = torch.empty(max(int(ws_bytes), 16), dtype=torch.uint8, device=dev) if ws_bytes else None
@@ -354,3 +363,70 @@ def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torc
         rc = L_.am_q4_attention(ctypes.byref(view.desc), ctypes.byref(a), ws_ptr, ws_bytes, s)
         check("am_q4_attention", rc)
     return out
+
+
+# ----------------------------------------------------------------------------- pool blocks
+
+
+def _pool_desc(k_pool: Sequence[torch.Tensor], v_pool: Sequence[torch.Tensor]) -> CacheView:
+    """CacheView describing a paged pool without a block table (block-level calls)."""
+    dummy = torch.full((1, 1), -1, dtype=torch.int32, device=k_pool[0].device)
+    return paged_view(k_pool, v_pool, dummy)
+
+
+def blocks_copy(k_pool, v_pool, block_ids: torch.Tensor, tokens: torch.Tensor,
+                offsets: torch.Tensor, buffer: torch.Tensor, *, to_buffer: bool,
+                status: torch.Tensor | None = None) -> None:
+    """Copy whole pool blocks to (pack) or from (unpack) a packed uint8 device buffer: block i
+    holds six tensors [1, Hkv, tokens[i], cols] (K weights, K scales, K biases, V weights, V
+    scales, V biases) at byte offsets offsets[i, 0:6]."""
+    view = _pool_desc(k_pool, v_pool)
+    dev = _require_cuda(buffer)
+    if dev != view.device:
+        raise ValueError("buffer and pool must be on the same device")
+    n = int(block_ids.numel())
+    ids = block_ids.to(device=dev, dtype=torch.int32).contiguous()
+    tok = tokens.to(device=dev, dtype=torch.int32).contiguous()
+    off = offsets.to(device=dev, dtype=torch.int64).contiguous()
+    if tok.numel() != n or off.numel() != 6 * n:
+        raise ValueError("tokens must have n entries and offsets n x 6")
+    if buffer.dtype != torch.uint8 or not buffer.is_contiguous():
+        raise ValueError("buffer must be a contiguous uint8 tensor")
+    st = status.data_ptr() if status is not None else None
+    L = _lib.load()
+    fn = L.am_q4_blocks_pack if to_buffer else L.am_q4_blocks_unpack
+    rc = fn(ctypes.byref(view.desc), ids.data_ptr(), tok.data_ptr(), off.data_ptr(), n,
+            buffer.data_ptr(), st, _stream(dev))
+    check("am_q4_blocks_pack" if to_buffer else "am_q4_blocks_unpack", rc)
+
+
+def block_reserve(free_ids: torch.Tensor, free_top: torch.Tensor, table: torch.Tensor,
+                  lengths: torch.Tensor, add: torch.Tensor, block_tokens: int,
+                  status: torch.Tensor | None = None) -> None:
+    """Device free list: give each row of `table` blocks for lengths + add tokens."""
+    dev = _require_cuda(free_ids, free_top, table, lengths, add)
+    for t in (free_ids, free_top, table, lengths, add):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("free list, table, lengths and counts must be contiguous int32")
+    rows, stride = table.shape
+    rc = _lib.load().am_block_reserve(free_ids.data_ptr(), free_top.data_ptr(), free_ids.numel(),
+                                      table.data_ptr(), stride, rows, lengths.data_ptr(),
+                                      add.data_ptr(), int(block_tokens),
+                                      status.data_ptr() if status is not None else None,
+                                      _stream(dev))
+    check("am_block_reserve", rc)
+
+
+def block_release(free_ids: torch.Tensor, free_top: torch.Tensor, table: torch.Tensor,
+                  keep_blocks: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """Device free list: return each row's blocks past keep_blocks[r] to the free stack."""
+    dev = _require_cuda(free_ids, free_top, table, keep_blocks)
+    for t in (free_ids, free_top, table, keep_blocks):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError("free list, table and counts must be contiguous int32")
+    rows, stride = table.shape
+    rc = _lib.load().am_block_release(free_ids.data_ptr(), free_top.data_ptr(), free_ids.numel(),
+                                      table.data_ptr(), stride, rows, keep_blocks.data_ptr(),
+                                      status.data_ptr() if status is not None else None,
+                                      _stream(dev))
+    check("am_block_release", rc)

@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define AM_ABI_VERSION 1
+#define AM_ABI_VERSION 2
 
 enum {
   AM_OK = 0,
@@ -41,7 +41,8 @@ enum { AM_MASK_NONE = 0, AM_MASK_BOOL = 1, AM_MASK_ADDITIVE = 2 };
 enum {
   AM_STATUS_BAD_BLOCK = 1,    /* a block-table entry outside [0, num_blocks) was skipped */
   AM_STATUS_BAD_POSITION = 2, /* a position outside the cache capacity was skipped */
-  AM_STATUS_TIMEOUT = 4       /* a bounded wait inside a kernel gave up */
+  AM_STATUS_TIMEOUT = 4,      /* a bounded wait inside a kernel gave up */
+  AM_STATUS_POOL_EXHAUSTED = 8 /* am_block_reserve: not enough free blocks, nothing taken */
 };
 
 /*
@@ -109,6 +110,10 @@ typedef struct am_attn_args {
   int32_t reserved0;
   int64_t mask_stride_b, mask_stride_h, mask_stride_l, mask_stride_n;
   int32_t* status;            /* device word or NULL: kernels OR AM_STATUS_* bits into it */
+  /* Attention sinks (replaces the fp16 detour of mlx_sink_compat.py:46-69): device fp32
+   * [n_q_heads] logits in scaled-score units, or NULL.  Each joins its head's softmax
+   * normaliser as one extra key that carries no value. */
+  const float* sinks;
 } am_attn_args;
 
 /* Library ABI version (AM_ABI_VERSION). */
@@ -185,6 +190,45 @@ int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* args, void* stre
  */
 int am_q4_attention(const am_q4_cache* cache, const am_attn_args* args, void* workspace,
                     size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- paged pool blocks
+ *
+ * `pool` describes a paged cache (layout AM_LAYOUT_PAGED; capacity = num_blocks; the
+ * block table is not used by these calls).  Device arrays throughout. */
+
+/*
+ * Copy whole blocks between the pool and a packed byte buffer laid out like the
+ * reference's persisted block tensors (replaces the per-block mx arrays written and read
+ * by safetensors_cache_adapter.py:141-199, :284-327): block i contributes six tensors
+ * [1, n_kv_heads, tokens[i], cols] -- K weights (uint32, cols = k_dim/8), K scales,
+ * K biases (scale dtype, cols = k_dim/64), V weights, V scales, V biases -- at byte
+ * offsets offsets[6*i .. 6*i+5] of the buffer.  pack: pool -> buffer; unpack: buffer ->
+ * pool.  Bad block ids or token counts are skipped and flagged AM_STATUS_BAD_BLOCK.
+ */
+int am_q4_blocks_pack(const am_q4_cache* pool, const int32_t* block_ids, const int32_t* tokens,
+                      const int64_t* offsets, int32_t n_blocks, void* buffer, int32_t* status,
+                      void* stream);
+int am_q4_blocks_unpack(const am_q4_cache* pool, const int32_t* block_ids, const int32_t* tokens,
+                        const int64_t* offsets, int32_t n_blocks, const void* buffer,
+                        int32_t* status, void* stream);
+
+/*
+ * The pool's free list on the device (replaces BlockPool.allocate / free,
+ * domain/services.py:111-223, for growth inside a captured step).  free_ids[0, *free_top)
+ * is the stack of free block ids, top last.
+ * am_block_reserve: for every row r, entries [0, ceil((lengths[r] + add[r]) /
+ * block_tokens)) of table row r that are < 0 take the next id from the top, rows in
+ * order, entries in order; all-or-nothing (AM_STATUS_POOL_EXHAUSTED).
+ * am_block_release: entries [keep_blocks[r], table_stride) of row r that hold a block go
+ * back onto the stack in row-major order and become -1; a release that would overflow the
+ * stack changes nothing and sets AM_STATUS_BAD_BLOCK.
+ */
+int am_block_reserve(int32_t* free_ids, int32_t* free_top, int32_t num_blocks, int32_t* table,
+                     int32_t table_stride, int32_t rows, const int32_t* lengths,
+                     const int32_t* add, int32_t block_tokens, int32_t* status, void* stream);
+int am_block_release(int32_t* free_ids, int32_t* free_top, int32_t num_blocks, int32_t* table,
+                     int32_t table_stride, int32_t rows, const int32_t* keep_blocks,
+                     int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

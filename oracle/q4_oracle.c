@@ -288,7 +288,7 @@ int amo_attention(const float* q, int B, int Hq, int L, int Hkv, int Dk, int Dv,
                   int layout, int64_t cap, int block_tokens, const int32_t* table,
                   int table_stride, const int32_t* kv_len, const int32_t* kv_start, int causal,
                   int window, int mask_kind, const float* mask, int64_t msb, int64_t msh,
-                  int64_t msl, int64_t msn, float scale, float* out) {
+                  int64_t msl, int64_t msn, float scale, const float* sinks, float* out) {
   const int n_rep = Hq / Hkv;
   const int rows_per_head = n_rep * L;
   const int RB = 64;  /* query rows per work item */
@@ -380,7 +380,16 @@ int amo_attention(const float* q, int B, int Hq, int L, int Hkv, int Dk, int Dv,
           const int l = rr / n_rep;
           const int h = hk * n_rep + rr % n_rep;
           float* o = out + (((int64_t)b * Hq + h) * L + l) * Dv;
-          for (int d = 0; d < Dv; d++) o[d] = n > 0 ? acc[(size_t)r * Dv + d] / lrow[r] : 0.0f;
+          /* attention sink: one extra logit per query head (scaled-score units) that joins
+             the softmax normaliser and contributes no value */
+          float w = 1.0f, den = lrow[r];
+          if (sinks) {
+            const float m_all = sinks[h] > mrow[r] ? sinks[h] : mrow[r];
+            w = mrow[r] == -INFINITY ? 0.0f : expf(mrow[r] - m_all);
+            den = lrow[r] * w + expf(sinks[h] - m_all);
+          }
+          for (int d = 0; d < Dv; d++)
+            o[d] = (n > 0 && den > 0.0f) ? acc[(size_t)r * Dv + d] * w / den : 0.0f;
         }
         free(kbuf);
         free(vbuf);

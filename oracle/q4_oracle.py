@@ -146,12 +146,14 @@ def structured_keep(n: int, L: int, kv_start: int = 0, causal: bool = True, wind
 
 
 def attention_np(q, k_q4, v_q4, scale, *, sdtype=F16, kv_len=None, kv_start=None, causal=True,
-                 window=0, mask=None, mask_kind=MASK_NONE, acc=np.float64):
+                 window=0, mask=None, mask_kind=MASK_NONE, sinks=None, acc=np.float64):
     """Reference-order attention over contiguous Q4 tensors, in float64 (or `acc`).
 
     q: [B, Hq, L, Dk] float; k_q4/v_q4: (codes [B,Hkv,N,D/8], scales, biases).
     kv_len/kv_start: per-sequence valid length / left padding (default N / 0).
     mask: optional dense [B or 1, Hq or 1, L, N] array (bool keep-mask or additive).
+    sinks: optional [Hq] sink logits appended to every row's scores before the softmax and
+    dropped after it.
     Returns [B, Hq, L, Dv] in `acc` precision.
     """
     q = np.asarray(q, dtype=acc)
@@ -180,10 +182,12 @@ def attention_np(q, k_q4, v_q4, scale, *, sdtype=F16, kv_len=None, kv_start=None
                 else:
                     s = s + mb.astype(acc)
             s = np.where(kk, s, masked)
+            if sinks is not None:
+                s = np.concatenate([s, np.full((L, 1), acc(sinks[h]))], axis=-1)
             s = s - s.max(axis=-1, keepdims=True)
             p = np.exp(s)
             p = p / p.sum(axis=-1, keepdims=True)
-            out[b, h] = p @ v[b, hk, :n]
+            out[b, h] = p[:, :n] @ v[b, hk, :n]
     return out
 
 
@@ -250,7 +254,7 @@ def lib():
         L.amo_dequantize.argtypes = [p, p, p, i32, i64, i32, p]
         L.amo_attention.argtypes = [p, i32, i32, i32, i32, i32, i32, p, p, p, p, p, p, i32, i32,
                                     i64, i32, p, i32, p, p, i32, i32, i32, p, i64, i64, i64, i64,
-                                    f32, p]
+                                    f32, p, p]
         L.amo_attention.restype = i32
         L.amo_num_threads.restype = i32
         L.amo_set_threads.argtypes = [i32]
@@ -311,8 +315,12 @@ def dequantize(codes, scales, biases, dtype: int = F16) -> np.ndarray:
 
 def attention(q, k_q4, v_q4, scale, *, sdtype=F16, n_kv_heads=None, layout=CONTIGUOUS,
               block_table=None, block_tokens=256, kv_len=None, kv_start=None, causal=True,
-              window=0, mask=None, mask_kind=MASK_NONE):
+              window=0, mask=None, mask_kind=MASK_NONE, sinks=None):
     """C restatement of the attention path (fp32 accumulation, OpenMP).
+
+    sinks: optional [Hq] attention-sink logits (in scaled-score units): each joins its
+    head's softmax normaliser as one extra key with no value (mlx_sink_compat.py:46-69
+    hands them to mx.fast.scaled_dot_product_attention).
 
     Contiguous: k_q4 = (codes [B,Hkv,cap,Dk/8], scales [B,Hkv,cap,Dk/64], biases).
     Paged:      k_q4 = (codes [num_blocks,Hkv,block_tokens,Dk/8], ...), with
@@ -351,11 +359,14 @@ def attention(q, k_q4, v_q4, scale, *, sdtype=F16, n_kv_heads=None, layout=CONTI
         st = [s // 4 if dim > 1 else 0 for s, dim in zip(m.strides, m.shape)]
         mstr = tuple(st)
         mask = m
+    if sinks is not None:
+        sinks = np.ascontiguousarray(np.asarray(sinks, dtype=np.float32).reshape(Hq))
     out = np.empty((B, Hq, L, Dv), np.float32)
     rc = lib().amo_attention(_ptr(q), B, Hq, L, Hkv, Dk, Dv, _ptr(kc), _ptr(ks), _ptr(kb),
                              _ptr(vc), _ptr(vs), _ptr(vb), sdtype, layout, cap, block_tokens,
                              _ptr(table), tstride, _ptr(kv_len), _ptr(kv_start), int(causal),
-                             int(window), mask_kind, _ptr(mask), *mstr, float(scale), _ptr(out))
+                             int(window), mask_kind, _ptr(mask), *mstr, float(scale), _ptr(sinks),
+                             _ptr(out))
     if rc != 0:
         raise ValueError("block table entry out of range")
     return out

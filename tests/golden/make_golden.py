@@ -10,7 +10,7 @@ Three kinds of fixtures:
   here: BatchQuantizedKVCache (mlx_quantized_extensions.py) driven through merge /
   update_and_fetch / make_mask / extend / filter / extract / trim, the patched
   quantized SDPA of mlx_fused_attention.py (op order, GQA reshape, mask handling, batch
-  split), and BlockPool (domain/services.py).  mlx is not installed, so the reference runs
+  split), the sink shim of mlx_sink_compat.py, and BlockPool (domain/services.py).  mlx is not installed, so the reference runs
   over tests/golden/mlx_standin.py (NumPy arrays, oracle numerics).
 * nothing here is read at test time except the .npz/.json files.
 """
@@ -157,6 +157,37 @@ def sdpa_cases(fused, base, ext, cache_mod):
         np.savez_compressed(HERE / f"ref_sdpa_{name}.npz", kind="ref_sdpa", **arrays)
 
 
+def sink_cases(base):
+    """The reference's sink shim (mlx_sink_compat.py:36-69: dequantize the Q4 tuples, then
+    fast SDPA with sinks) on seeded GPT-OSS-shaped inputs (head_dim 64, n_rep 8)."""
+    importlib.import_module("agent_memory.adapters.outbound.mlx_sink_compat")  # patches on import
+    sdpa = base.scaled_dot_product_attention
+    rng = np.random.default_rng(23)
+    cache = type("Q4Cache", (), {"bits": 4, "group_size": 64})()
+
+    def run(name, B, Hq, Hkv, N, D, L, mask, scale):
+        k = orc.quantize_np(f16(rng, B, Hkv, N, D).view(np.uint16), orc.F16)
+        v = orc.quantize_np(f16(rng, B, Hkv, N, D).view(np.uint16), orc.F16)
+        q = f16(rng, B, Hq, L, D)
+        sinks = (rng.standard_normal(Hq) * 2).astype(np.float32)
+        as_mx = lambda t: (t[0], t[1].view(np.float16), t[2].view(np.float16))  # noqa: E731
+        out = sdpa(q, as_mx(k), as_mx(v), cache, scale=scale, mask=mask, sinks=sinks)
+        arrays = {"q": q.view(np.uint16), "kc": k[0], "ks": k[1], "kb": k[2], "vc": v[0],
+                  "vs": v[1], "vb": v[2], "out": np.asarray(out).view(np.uint16),
+                  "scale": np.float32(scale), "sinks": sinks}
+        if isinstance(mask, str):
+            arrays["mask_str"] = mask
+        elif mask is not None:
+            arrays["mask"] = np.asarray(mask)
+        np.savez_compressed(HERE / f"ref_sinks_{name}.npz", kind="ref_sinks", **arrays)
+
+    run("decode", 2, 16, 2, 90, 64, 1, None, 0.125)
+    run("prefill_causal", 1, 16, 2, 70, 64, 8, "causal", 0.125)
+    keep = np.zeros((1, 1, 1, 100), dtype=bool)
+    keep[..., 100 - 32:] = True  # a 32-key sliding window for the one query
+    run("window_bool", 1, 8, 1, 100, 64, 1, keep, 0.125)
+
+
 def block_pool_ops(services, vo):
     spec = vo.ModelCacheSpec(n_layers=4, n_kv_heads=8, head_dim=128, block_tokens=256,
                              layer_types=["global"] * 4)
@@ -195,6 +226,7 @@ def main():
     assert ext.validate_q4_pipeline() is True
     cache_lifecycle(ext, cache_mod)
     sdpa_cases(fused, base, ext, cache_mod)
+    sink_cases(base)
     block_pool_ops(services, vo)
     print("fixtures written to", HERE)
 

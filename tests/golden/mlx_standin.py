@@ -190,6 +190,46 @@ def _original_qsdpa(queries, q_keys, q_values, scale, mask, group_size=64, bits=
     return out
 
 
+class _Array:
+    """mx.array: a type (annotations such as ``mx.array | tuple`` are evaluated at import)
+    whose construction returns a NumPy array."""
+
+    def __new__(cls, x, dtype=None):
+        return np.array(x, dtype=_npdt(dtype))
+
+
+def _fast_sdpa(queries, keys, values, scale, mask=None, sinks=None):
+    """mx.fast.scaled_dot_product_attention as documented: GQA by head repetition, boolean
+    masks keep True, additive masks add, "causal" aligns the last query with the last key,
+    and each head's sink logit joins the softmax as one extra column with no value.
+    Computed in fp32, returned in the query dtype."""
+    q = np.asarray(queries)
+    B, Hq, L, _ = q.shape
+    Hkv = np.asarray(keys).shape[1]
+    n_rep = Hq // Hkv
+    k = np.repeat(np.asarray(keys, dtype=np.float32), n_rep, axis=1)
+    v = np.repeat(np.asarray(values, dtype=np.float32), n_rep, axis=1)
+    s = (q.astype(np.float32) * np.float32(scale)) @ np.swapaxes(k, -1, -2)
+    if mask is not None:
+        if isinstance(mask, str):
+            kL = s.shape[-1]
+            mask = np.arange(kL - L, kL)[:, None] >= np.arange(kL)[None]
+        mask = np.asarray(mask)
+        if mask.dtype == np.bool_:
+            s = np.where(mask, s, -np.inf)
+        else:
+            s = s + mask.astype(np.float32)
+    if sinks is not None:
+        sk = np.broadcast_to(np.asarray(sinks, dtype=np.float32).reshape(1, Hq, 1, 1), (B, Hq, L, 1))
+        s = np.concatenate([s, sk], axis=-1)
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p = p / p.sum(axis=-1, keepdims=True)
+    if sinks is not None:
+        p = p[..., :-1]
+    return (p @ v).astype(q.dtype)
+
+
 def install() -> types.SimpleNamespace:
     """Register the stand-in modules in sys.modules; returns the mlx_lm.models.base module."""
     core = types.ModuleType("mlx.core")
@@ -199,7 +239,7 @@ def install() -> types.SimpleNamespace:
     core.float32 = _DType("float32", np.float32)
     core.bfloat16 = _DType("bfloat16", np.float32)  # unused by the fixtures (no NumPy bf16)
     core.bool_ = _DType("bool_", np.bool_)
-    core.array = lambda x, dtype=None: np.array(x, dtype=_npdt(dtype))
+    core.array = _Array
     core.zeros = lambda shape, dtype=core.float32: np.zeros(shape, dtype=_npdt(dtype))
     core.concatenate = lambda arrs, axis=0: np.concatenate(arrs, axis=axis)
     core.eval = lambda *a, **k: None
@@ -216,7 +256,7 @@ def install() -> types.SimpleNamespace:
     core.dequantize = _dequantize
     core.quantized_matmul = _quantized_matmul
     core.compile = lambda fn=None, shapeless=False: fn
-    core.fast = types.SimpleNamespace(metal_kernel=None, scaled_dot_product_attention=None)
+    core.fast = types.SimpleNamespace(metal_kernel=None, scaled_dot_product_attention=_fast_sdpa)
     mlx = types.ModuleType("mlx")
     mlx.core = core
     utils = types.ModuleType("mlx.utils")
@@ -230,6 +270,7 @@ def install() -> types.SimpleNamespace:
     base = types.ModuleType("mlx_lm.models.base")
     base.create_causal_mask = create_causal_mask
     base.quantized_scaled_dot_product_attention = _original_qsdpa
+    base.scaled_dot_product_attention = None  # replaced by the reference's sink patch
     mlx_lm.models = models
     models.cache = cache
     models.base = base

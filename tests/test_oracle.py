@@ -188,6 +188,23 @@ def test_golden_fixture(orc, name):
         got = orc.attention(q, kq, vq, float(f["scale"]), causal=causal, mask=mask, mask_kind=mk)
         ref = f["out"].view(np.float16).astype(np.float32)
         assert np.all(np.abs(got - ref) <= 2e-3 + 1e-3 * np.abs(ref))
+    elif kind == "ref_sinks":
+        # output of the reference's sink shim (mlx_sink_compat.py: dequantize, then fast SDPA
+        # with per-head sink logits) over the stand-in: pins the oracle's sink rule
+        q = f["q"].view(np.float16).astype(np.float32)
+        kq = (f["kc"], f["ks"], f["kb"])
+        vq = (f["vc"], f["vs"], f["vb"])
+        mask, mk, causal = None, 0, "mask_str" in f.files
+        if "mask" in f.files:
+            mask = f["mask"].astype(np.float32)
+            mk = 1
+        got = orc.attention(q, kq, vq, float(f["scale"]), causal=causal, mask=mask, mask_kind=mk,
+                            sinks=f["sinks"])
+        ref = f["out"].view(np.float16).astype(np.float32)
+        assert np.all(np.abs(got - ref) <= 2e-3 + 1e-3 * np.abs(ref))
+        # the sinks matter: without them the outputs differ
+        plain = orc.attention(q, kq, vq, float(f["scale"]), causal=causal, mask=mask, mask_kind=mk)
+        assert np.abs(plain - ref).max() > 1e-2
     elif kind == "cache_lifecycle":
         # the recorded inputs re-quantized by the oracle reproduce the reference cache's
         # packed codes (the cache bookkeeping itself is replayed on the GPU)
