@@ -15,14 +15,16 @@ from .cache import BatchQuantizedKVCache, QuantizedKVCache, validate_q4_pipeline
 from .kernels import dequantize, quantize
 from .masks import CausalMask, create_causal_mask
 from .paged import PagedLayerCache, PagedQ4Pool, lpt_partition, shuffled_allocator
-from .paged_cache import DeviceBlockPool, PagedBatchQuantizedKVCache, PagedKV, PagedMask
+from .paged_cache import (DeviceBlockPool, PagedBatchQuantizedKVCache, PagedKV, PagedMask,
+                          extract_agent_blocks, reconstruct_cache, slice_cache_to_length)
 
 __all__ = [
     "AgentBlocks", "BLOCK_SIZE_TOKENS", "BatchQuantizedKVCache", "BlockPool", "CausalMask",
     "DeviceBlockPool", "KVBlock", "ModelCacheSpec", "PagedBatchQuantizedKVCache", "PagedKV",
     "PagedLayerCache", "PagedMask", "PagedQ4Pool", "PoolExhaustedError",
     "Q4KernelError", "Q4KernelUnavailable", "QuantizedKVCache", "apply_fused_attention_patch",
-    "create_causal_mask", "dequantize", "lpt_partition", "quantize",
+    "create_causal_mask", "dequantize", "extract_agent_blocks", "lpt_partition", "quantize",
+    "reconstruct_cache", "slice_cache_to_length",
     "quantized_scaled_dot_product_attention", "scaled_dot_product_attention",
     "shuffled_allocator", "validate_q4_pipeline",
 ]

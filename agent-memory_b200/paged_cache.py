@@ -29,7 +29,8 @@ from typing import Sequence
 import torch
 
 from . import _lib, kernels
-from .block_pool import BlockOperationError, BlockPool, PoolExhaustedError
+from .block_pool import (AgentBlocks, BlockOperationError, BlockPool, KVBlock,
+                         PoolExhaustedError)
 from .paged import PagedQ4Pool
 
 
@@ -68,6 +69,26 @@ class DeviceBlockPool:
 
     def release(self, table: torch.Tensor, keep_blocks: torch.Tensor) -> None:
         kernels.block_release(self.free_ids, self.free_top, table, keep_blocks, self.status)
+
+    def allocate(self, n_blocks: int, layer_id: int = 0, agent_id: str = "") -> list[KVBlock]:
+        """BlockPool.allocate (services.py:111-175) from the host: pops n ids (LIFO) and
+        returns them as KVBlocks; PoolExhaustedError leaves the pool unchanged.  Syncs."""
+        if n_blocks <= 0:
+            raise BlockOperationError(f"n_blocks must be > 0, got {n_blocks}")
+        tab = torch.full((1, n_blocks), -1, dtype=torch.int32, device=self.device)
+        zero = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.reserve(tab, zero, torch.full((1,), n_blocks, dtype=torch.int32, device=self.device), 1)
+        self.check()
+        return [KVBlock(block_id=int(i), layer_id=layer_id, token_count=0, layer_data=None,
+                        metadata={"agent_id": agent_id}) for i in tab[0].tolist()]
+
+    def free(self, blocks: Sequence[KVBlock], agent_id: str = "") -> None:
+        """BlockPool.free (services.py:177-223): the ids go back on the stack in order."""
+        ids = [int(b.block_id) for b in blocks]
+        if not ids:
+            return
+        tab = torch.tensor([ids], dtype=torch.int32, device=self.device)
+        self.release(tab, torch.zeros(1, dtype=torch.int32, device=self.device))
 
     def available_blocks(self) -> int:
         return int(self.free_top.item())
@@ -296,3 +317,74 @@ class PagedBatchQuantizedKVCache:
             out.append(tuple(arrs))
         lp = torch.tensor([N - L for L in self.lengths], dtype=torch.int32, device=self.pool.device)
         return out[0], out[1], self.kv_len.clone(), lp
+
+
+# ---------------------------------------------------------------------- engine glue
+
+
+def reconstruct_cache(agent_blocks: AgentBlocks, pool: PagedQ4Pool, allocator: DeviceBlockPool,
+                      n_layers: int, max_tokens: int | None = None) -> list[PagedBatchQuantizedKVCache]:
+    """BatchEngine._reconstruct_cache (batch_engine.py:1745-1882) over pool blocks: one
+    single-row cache per layer whose block table lists the agent's blocks -- no
+    concatenation, no copy.  With max_tokens, blocks after the first max_tokens tokens are
+    not loaded (the EXACT-match shortcut) and go back to the free list.  The caches take
+    ownership of the blocks."""
+    caches = []
+    for layer in range(n_layers):
+        blocks = agent_blocks.blocks_for_layer(layer)
+        taken, loaded = [], 0
+        for blk in blocks:
+            if max_tokens is not None and loaded >= max_tokens:
+                break
+            taken.append(blk)
+            loaded += blk.token_count
+        rest = blocks[len(taken):]
+        if rest:
+            allocator.free(rest)
+        length = loaded if max_tokens is not None else (agent_blocks.total_tokens if taken else 0)
+        c = PagedBatchQuantizedKVCache(pool, allocator, max(1, len(taken)), rows=1)
+        if taken:
+            c.table[0, :len(taken)] = torch.tensor([b.block_id for b in taken], dtype=torch.int32,
+                                                   device=pool.device)
+        c._set_rows(c.table, [length])
+        caches.append(c)
+    return caches
+
+
+def slice_cache_to_length(caches: Sequence[PagedBatchQuantizedKVCache], target_length: int) -> None:
+    """BatchEngine._slice_cache_to_length (batch_engine.py:1690-1743): every row of every
+    layer keeps its first target_length tokens; the blocks past them return to the free
+    list (a table edit, no copy)."""
+    for c in caches:
+        if c.rows == 0:
+            continue
+        bt = c.pool.block_tokens
+        c.lengths = [min(L, max(0, int(target_length))) for L in c.lengths]
+        keep = torch.tensor([-(-L // bt) for L in c.lengths], dtype=torch.int32, device=c.pool.device)
+        c.allocator.release(c.table, keep)
+        c.kv_len = torch.tensor(c.lengths, dtype=torch.int32, device=c.pool.device)
+
+
+def extract_agent_blocks(agent_id: str, caches: Sequence[PagedBatchQuantizedKVCache],
+                         token_sequence: list[int] | None = None,
+                         prompt_text: str = "") -> AgentBlocks:
+    """BatchEngine._extract_cache (batch_engine.py:1884-2064) for single-row paged caches
+    (one per layer, e.g. from PagedBatchQuantizedKVCache.extract): the row's block table is
+    already the block list, so the AgentBlocks name those pool blocks (block_id = pool row,
+    token_count = tokens held) without allocating or slicing anything."""
+    blocks: dict[int, list[KVBlock]] = {}
+    total = 0
+    for layer, c in enumerate(caches):
+        if c.rows != 1:
+            raise ValueError("extract_agent_blocks takes single-sequence caches")
+        n = c.lengths[0]
+        if n == 0:
+            continue
+        bt = c.pool.block_tokens
+        ids = c.table[0, :-(-n // bt)].tolist()
+        blocks[layer] = [KVBlock(block_id=int(bid), layer_id=layer, token_count=min(bt, n - j * bt),
+                                 layer_data=None, metadata={"agent_id": agent_id})
+                         for j, bid in enumerate(ids)]
+        total = max(total, n)
+    return AgentBlocks(agent_id=agent_id, blocks=blocks, total_tokens=total,
+                       token_sequence=list(token_sequence or []), prompt_text=prompt_text)

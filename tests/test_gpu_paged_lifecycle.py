@@ -235,3 +235,54 @@ def test_load_reference_layout_file(cuda, tmp_path):
     a = pkg.kernels.attention(pool.view(table), q, D ** -0.5, kv_len, n)
     b = pkg.quantized_scaled_dot_product_attention(q, kq, vq, D ** -0.5, None)
     assert_close(a.float().cpu().numpy(), b.float().cpu().numpy(), what="loaded reference file")
+
+
+def test_engine_glue_extract_save_load_reconstruct(cuda, tmp_path):
+    """_extract_cache -> save -> load -> _reconstruct_cache -> _slice_cache_to_length
+    (batch_engine.py:1690-2064) over pool blocks: the agent's blocks never leave the pool
+    except through the file, and attention after the round trip is unchanged."""
+    g = torch.Generator().manual_seed(11)
+    layers, n = 2, 650
+    pool = pkg.PagedQ4Pool(H, D, D, 40, BT, torch.float16, cuda)
+    alloc = pkg.DeviceBlockPool(40, cuda)
+    kv = [_kv(g, 1, n, cuda) for _ in range(layers)]
+    caches = []
+    for k, v in kv:
+        c = pkg.PagedBatchQuantizedKVCache(pool, alloc, 1, rows=1)
+        c.update_and_fetch(k, v)
+        caches.append(c)
+    q = torch.randn(1, HQ, 1, D, generator=g).half().to(cuda)
+
+    def attend(cs):
+        return [pkg.quantized_scaled_dot_product_attention(q, pkg.PagedKV(c, "k"), pkg.PagedKV(c, "v"),
+                                                           D ** -0.5, None).float().cpu()
+                for c in cs]
+
+    before = attend(caches)
+    blocks = pkg.extract_agent_blocks("agent_7", caches, token_sequence=list(range(n)))
+    assert blocks.total_tokens == n and [b.token_count for b in blocks.blocks[0]] == [256, 256, 138]
+    store = persistence.SafetensorsQ4Store(tmp_path, pool, alloc)
+    path = store.save("agent_7", blocks, {"block_tokens": BT})
+    for c in caches:
+        c.free()
+    assert alloc.available_blocks() == 40
+    loaded, _ = store.load(path)
+    agent = pkg.AgentBlocks(agent_id="agent_7", blocks=loaded, total_tokens=n)
+    rebuilt = pkg.reconstruct_cache(agent, pool, alloc, layers)
+    for a, b in zip(before, attend(rebuilt)):
+        assert torch.equal(a, b)
+    # warm hit: keep a 300-token prefix (EXACT-match shortcut + slice to length)
+    for c in rebuilt:
+        c.free()
+    loaded, _ = store.load(path)
+    agent = pkg.AgentBlocks(agent_id="agent_7", blocks=loaded, total_tokens=n)
+    pref = pkg.reconstruct_cache(agent, pool, alloc, layers, max_tokens=300)
+    assert [c.lengths[0] for c in pref] == [512, 512]  # whole blocks up to >= 300 tokens
+    assert alloc.available_blocks() == 40 - 2 * 2
+    pkg.slice_cache_to_length(pref, 300)
+    assert alloc.available_blocks() == 40 - 2 * 2 and [c.lengths[0] for c in pref] == [300, 300]
+    got = attend(pref)
+    for (k, v), a in zip(kv, got):
+        kq, vq = pkg.quantize(k[:, :, :300]), pkg.quantize(v[:, :, :300])
+        want = pkg.quantized_scaled_dot_product_attention(q, kq, vq, D ** -0.5, None).float().cpu()
+        assert_close(a.numpy(), want.numpy(), what="prefix after slice")
