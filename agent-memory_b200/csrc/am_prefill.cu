@@ -4,13 +4,14 @@
 // pairs, token-major: 128 / n_rep query tokens times the n_rep heads that share the KV
 // head, so each dequantized K/V tile feeds all of them.  256 threads, warp-specialised:
 //   * producer warps 4-7 dequantize the Q4 K and V rows of 128-key tile j (one token per
-//     thread) into fp16 operand tiles in shared memory (128-byte swizzle; K K-major,
-//     V MN-major; two buffers), then one producer thread issues S_j = Q . K_j^T
-//     (tcgen05.mma kind::f16, M=128, N=128, K=16 steps) into TMEM S[j%2] and, once the
-//     softmax warps have written P_{j-1}, O_{j-1} = P_{j-1} . V_{j-1} into TMEM O[(j-1)%2];
+//     thread, raw rows prefetched one tile ahead; fp16 FMA dequantisation) into fp16
+//     operand tiles in shared memory (128-byte swizzle; K K-major, V MN-major; two
+//     buffers), then one producer thread issues S_j = Q . K_j^T (tcgen05.mma kind::f16,
+//     M=128, N=128, K=16 steps) into TMEM S[j%2];
 //   * softmax warps 0-3 own TMEM lanes 0-127 (one query row per thread): tcgen05.ld of
-//     their S row, fp32 online softmax, P (fp16, K-major) into shared memory, and the
-//     previous tile's O row folded into fp32 registers with the running-max correction.
+//     their S row, fp32 online softmax, P (fp16, K-major) into shared memory, the previous
+//     tile's O row folded into fp32 registers with the running-max correction; then one
+//     softmax thread issues O_j = P_j . V_j into TMEM O[j%2].
 // mbarriers (MMA commits and 128-thread arrivals) chain the stages so the dequantisation
 // of tile j+1, the MMAs of tile j and the softmax of tile j overlap.  TMEM: S x2 + O x2
 // (512 columns, one CTA per SM).  Operands are fp16 for every query dtype: bf16 queries
@@ -86,6 +87,44 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 #undef AM_R8
 
+// Warp loads 32 lanes x 128 consecutive fp32 columns of TMEM in one instruction (a whole
+// S row per thread: one TMEM round trip per tile).
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
+  uint32_t r[128];
+#define AM_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), \
+                 "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,"
+      "%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,"
+      "%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,"
+      "%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,"
+      "%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n"
+      : AM_R8(0), AM_R8(8), AM_R8(16), AM_R8(24), AM_R8(32), AM_R8(40), AM_R8(48), AM_R8(56),
+        AM_R8(64), AM_R8(72), AM_R8(80), AM_R8(88), AM_R8(96), AM_R8(104), AM_R8(112), AM_R8(120)
+      : "r"(taddr));
+#undef AM_R8
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Warp stores 32 lanes x 32 consecutive fp32 columns of TMEM (thread i -> lane base+i).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
+      "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]),
+      "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
+      "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
 // Byte offset inside a 1024-byte-aligned 128B-swizzled region.
 __device__ __forceinline__ uint32_t swz(uint32_t off) { return off ^ (((off >> 7) & 7u) << 4); }
 
@@ -102,25 +141,76 @@ struct PrefillLayout {
   static constexpr int OFF_QF = OFF_P + P_BYTES;  // per-row query factor (128 floats)
   static constexpr int OFF_BAR = OFF_QF + 128 * 4;
   static constexpr int SMEM = OFF_BAR + 128 + 1024;  // barriers + slack for 1024-byte alignment
-  static constexpr uint32_t TMEM_COLS = 512;     // S x2 (256) + O x2 (2 x D)
+  static constexpr uint32_t TMEM_COLS = 512;     // S x2 (256) + O (D, accumulated over tiles)
   static_assert(D <= 128, "tiles sized for D <= 128");
 };
 
-// o_acc = o_acc * scale_old + (this thread's TMEM row of an O tile at taddr)
+// Multiply this thread's TMEM row of the O accumulator (D columns at taddr) by f.
 template <int D>
-__device__ __forceinline__ void fold_o(float (&o_acc)[D], uint32_t taddr, float scale_old) {
-#pragma unroll
+__device__ __forceinline__ void rescale_o(uint32_t taddr, float f) {
+#pragma unroll 1
   for (int c = 0; c < D / 32; ++c) {
     float v[32];
     tc::tmem_ld32(taddr + c * 32, v);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) o_acc[c * 32 + j] = fmaf(o_acc[c * 32 + j], scale_old, v[j]);
+    for (int j = 0; j < 32; ++j) v[j] *= f;
+    tc::tmem_st32(taddr + c * 32, v);
+  }
+}
+
+// Lazy rescaling: a row's running max is raised only when a tile's max exceeds it by more
+// than 2^8 (log2 units), so P <= 256 (exact range for the fp16 P operand) and the O
+// accumulator in TMEM is rescaled rarely.
+constexpr float kPrefillRescaleSlack = 8.0f;
+
+// Operand tiles hold the 8 head dims of every 16-byte chunk in the order the dequantiser
+// produces them, kPerm8[p] = head dim of position p: the Q4 word of 8 nibbles n0..n7 (dims
+// 0..7) becomes the half pairs (n0, n4) (n1, n5) (n2, n6) (n3, n7) with one mask each.  Q
+// carries the same order (so S = Q . K^T is unchanged) and O's columns come out in it, so
+// the epilogue puts them back.
+__device__ __forceinline__ constexpr int perm8(int p) { return (p & 1) ? (p >> 1) + 4 : (p >> 1); }
+
+// 8 Q4 codes of one word -> 8 fp16 values code * s + b in perm8 order (16 bytes).  A code
+// OR-ed into the mantissa of 1024.0 is the fp16 value 1024 + code; subtracting 1024 leaves
+// the code exactly, then one fp16 FMA applies scale and bias with a single rounding.
+__device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 s2, __half2 b2) {
+  const __half2 k1024 = __half2half2(__ushort_as_half(0x6400));
+  uint32_t out[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const uint32_t x = ((w >> (4 * e)) & 0x000F000Fu) | 0x64006400u;
+    __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&x), k1024);
+    h = __hfma2(h, s2, b2);
+    out[e] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+template <bool BF16>
+__device__ __forceinline__ __half2 scale_h2(uint16_t bits) {
+  if constexpr (BF16) {
+    return __half2half2(__float2half_rn(h2f<true>(bits)));
+  } else {
+    return __half2half2(__ushort_as_half(bits));
   }
 }
 
 // mbarrier slots (8 bytes each) inside OFF_BAR
-enum { B_SFULL = 0, B_SFREE = 2, B_PFULL = 4, B_OFULL = 5, B_KVFREE = 7, B_COUNT = 9 };
+enum { B_SFULL = 0, B_SFREE = 2, B_OFULL = 4, B_KVFREE = 5, B_PFULL = 7, B_COUNT = 8 };
 
+// Named barrier over one 128-thread warp group that also ORs a flag across it: every
+// thread gets the same answer, so a group leaves its loop together even if the shared
+// abort flag changes while its threads read it.
+__device__ __forceinline__ bool group_bar_any(int id, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, %2, 128, p;\n"
+      "selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id)
+      : "memory");
+  return r != 0;
+}
 __device__ __forceinline__ void named_bar_producers() {
   asm volatile("bar.sync 1, 128;\n" ::: "memory");
 }
@@ -170,9 +260,8 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
     mbar_init(bar(B_SFULL + 1), 1);
     mbar_init(bar(B_SFREE), 128);
     mbar_init(bar(B_SFREE + 1), 128);
-    mbar_init(bar(B_PFULL), 128);
     mbar_init(bar(B_OFULL), 1);
-    mbar_init(bar(B_OFULL + 1), 1);
+    mbar_init(bar(B_PFULL), 128);
     mbar_init(bar(B_KVFREE), 1);
     mbar_init(bar(B_KVFREE + 1), 1);
     fence_mbar_init();
@@ -218,10 +307,15 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
       if (row_ok) {
         const uint4 raw = *reinterpret_cast<const uint4*>(qrow + c * 8);
         const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+        float qv[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          qv[2 * i] = h2f_rt(u[i] & 0xffffu, p.q_bf16) * pw;
+          qv[2 * i + 1] = h2f_rt(u[i] >> 16, p.q_bf16) * pw;
+        }
         uint32_t o4[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o4[i] = pack_half2(h2f_rt(u[i] & 0xffffu, p.q_bf16) * pw, h2f_rt(u[i] >> 16, p.q_bf16) * pw);
+        for (int i = 0; i < 4; ++i) o4[i] = pack_half2(qv[perm8(2 * i)], qv[perm8(2 * i + 1)]);
         outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
       }
       const uint32_t off = (c / 8) * (128 * 128) + r * 128 + (c % 8) * 16;
@@ -239,24 +333,23 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
   if (producer) {
     // ================================================================ producer warps
     const int r = tid - 128;  // token row of each K/V tile this thread dequantizes
-    for (int j = 0; j < n_tiles; ++j) {
-      const int buf = j & 1;
-      if (j >= 2 && !*abort_flag) {
-        if (!mbar_wait_bounded(bar(B_KVFREE + buf), ((j - 2) >> 1) & 1)) *abort_flag = 1;
-      }
-      // every producer thread reads the flag after the same barrier, so all of them leave
-      // the loop together (no thread may be left waiting in bar.sync 1)
-      named_bar_producers();
-      if (*abort_flag) break;
+    // Raw Q4 data of this thread's row of a tile, loaded one tile ahead so the global
+    // loads of tile j+1 are in flight while tile j is dequantized.
+    struct RawRow {
+      uint4 k[NG * 2], v[NG * 2];
+      uint16_t ks[NG], kb[NG], vs[NG], vb[NG];
+      bool valid;
+    };
+    auto load_raw = [&](int j, RawRow& R) {
       const int tok = lo + j * 128 + r;
-      bool valid = tok < n && tok >= 0;
+      R.valid = tok < n && tok >= 0;
       int64_t row = 0;
-      if (valid) {
+      if (R.valid) {
         if constexpr (PAGED) {
           const int bi = tok / p.block_tokens;
           const int32_t blk = bi < p.table_stride ? p.table[(int64_t)b * p.table_stride + bi] : -1;
           if (blk < 0 || blk >= p.capacity) {
-            valid = false;
+            R.valid = false;
             flag_status(p.status, AM_STATUS_BAD_BLOCK);
           } else {
             row = ((int64_t)blk * p.hkv + h) * p.block_tokens + tok % p.block_tokens;
@@ -265,46 +358,54 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
           row = ((int64_t)b * p.hkv + h) * p.capacity + tok;
         }
       }
-      const uint32_t* kc = p.kc + row * (D / 8);
-      const uint32_t* vc = p.vc + row * (D / 8);
+      const uint4* kc = reinterpret_cast<const uint4*>(p.kc + row * (D / 8));
+      const uint4* vc = reinterpret_cast<const uint4*>(p.vc + row * (D / 8));
+#pragma unroll
+      for (int i = 0; i < NG * 2; ++i) {
+        R.k[i] = R.valid ? kc[i] : make_uint4(0, 0, 0, 0);
+        R.v[i] = R.valid ? vc[i] : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int G = 0; G < NG; ++G) {
+        R.ks[G] = R.valid ? p.ks[row * NG + G] : 0;
+        R.kb[G] = R.valid ? p.kb[row * NG + G] : 0;
+        R.vs[G] = R.valid ? p.vs[row * NG + G] : 0;
+        R.vb[G] = R.valid ? p.vb[row * NG + G] : 0;
+      }
+    };
+    RawRow cur;
+    if (n_tiles > 0) load_raw(0, cur);
+    for (int j = 0; j < n_tiles; ++j) {
+      const int buf = j & 1;
+      if (j >= 2 && !*abort_flag) {
+        if (!mbar_wait_bounded(bar(B_KVFREE + buf), ((j - 2) >> 1) & 1)) *abort_flag = 1;
+      }
+      // the producers decide together (no thread may be left waiting in barrier 1)
+      if (group_bar_any(1, *abort_flag != 0)) break;
+      RawRow nxt;
+      if (j + 1 < n_tiles) load_raw(j + 1, nxt);
       uint8_t* kdst = smem + LY::OFF_K + buf * LY::TILE;
       uint8_t* vdst = smem + LY::OFF_V + buf * LY::TILE;
 #pragma unroll
       for (int G = 0; G < NG; ++G) {
-        float ks = 0.f, kb = 0.f, vs = 0.f, vb = 0.f;
-        if (valid) {
-          ks = h2f<SBF16>(p.ks[row * NG + G]);
-          kb = h2f<SBF16>(p.kb[row * NG + G]);
-          vs = h2f<SBF16>(p.vs[row * NG + G]);
-          vb = h2f<SBF16>(p.vb[row * NG + G]);
-        }
+        const __half2 ks2 = scale_h2<SBF16>(cur.ks[G]), kb2 = scale_h2<SBF16>(cur.kb[G]);
+        const __half2 vs2 = scale_h2<SBF16>(cur.vs[G]), vb2 = scale_h2<SBF16>(cur.vb[G]);
 #pragma unroll
         for (int w4 = 0; w4 < 2; ++w4) {
-          uint4 kw = make_uint4(0, 0, 0, 0), vw = make_uint4(0, 0, 0, 0);
-          if (valid) {
-            kw = *reinterpret_cast<const uint4*>(kc + G * 8 + w4 * 4);
-            vw = *reinterpret_cast<const uint4*>(vc + G * 8 + w4 * 4);
-          }
+          const uint4 kw = cur.k[G * 2 + w4], vw = cur.v[G * 2 + w4];
           const uint32_t kk[4] = {kw.x, kw.y, kw.z, kw.w};
           const uint32_t vv[4] = {vw.x, vw.y, vw.z, vw.w};
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int wi = G * 8 + w4 * 4 + i;
-            uint32_t ko[4], vo[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              ko[e] = pack_half2(fmaf(static_cast<float>((kk[i] >> (8 * e)) & 0xfu), ks, kb),
-                              fmaf(static_cast<float>((kk[i] >> (8 * e + 4)) & 0xfu), ks, kb));
-              vo[e] = pack_half2(fmaf(static_cast<float>((vv[i] >> (8 * e)) & 0xfu), vs, vb),
-                              fmaf(static_cast<float>((vv[i] >> (8 * e + 4)) & 0xfu), vs, vb));
-            }
             const uint32_t koff = (wi / 8) * (128 * 128) + r * 128 + (wi % 8) * 16;
-            *reinterpret_cast<uint4*>(kdst + tc::swz(koff)) = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+            *reinterpret_cast<uint4*>(kdst + tc::swz(koff)) = dequant8(kk[i], ks2, kb2);
             const uint32_t voff = (wi / 8) * (128 * 128) + (r / 8) * 1024 + (r % 8) * 128 + (wi % 8) * 16;
-            *reinterpret_cast<uint4*>(vdst + tc::swz(voff)) = make_uint4(vo[0], vo[1], vo[2], vo[3]);
+            *reinterpret_cast<uint4*>(vdst + tc::swz(voff)) = dequant8(vv[i], vs2, vb2);
           }
         }
       }
+      cur = nxt;
       tc::fence_proxy_async();
       named_bar_producers();
       if (r == 0) {
@@ -320,43 +421,9 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
                     ID_S, ks > 0 ? 1u : 0u);
           }
           tc::commit(bar(B_SFULL + buf));
-          if (j >= 1) {
-            ok = mbar_wait_bounded(bar(B_PFULL), (j - 1) & 1);
-            if (ok) {
-              tc::fence_after();
-              const int pb = (j - 1) & 1;
-              const uint32_t vb_addr = sV + pb * LY::TILE;
-#pragma unroll
-              for (int ks = 0; ks < 8; ++ks) {
-                const uint32_t poff = (ks / 4) * (128 * 128) + (ks % 4) * 32;
-                tc::mma(tmem + 256 + pb * D, tc::sdesc(sP + poff, 16, 1024),
-                        tc::sdesc(vb_addr + ks * 2048, 128 * 128, 1024), ID_O, ks > 0 ? 1u : 0u);
-              }
-              tc::commit(bar(B_OFULL + pb));
-              tc::commit(bar(B_KVFREE + pb));
-            }
-          }
+        } else {
+          *abort_flag = 1;
         }
-        if (!ok) *abort_flag = 1;
-      }
-    }
-    // last P . V
-    if (tid == 128 && n_tiles > 0 && !*abort_flag) {
-      const int j = n_tiles;
-      if (mbar_wait_bounded(bar(B_PFULL), (j - 1) & 1)) {
-        tc::fence_after();
-        const int pb = (j - 1) & 1;
-        const uint32_t vb_addr = sV + pb * LY::TILE;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t poff = (ks / 4) * (128 * 128) + (ks % 4) * 32;
-          tc::mma(tmem + 256 + pb * D, tc::sdesc(sP + poff, 16, 1024),
-                  tc::sdesc(vb_addr + ks * 2048, 128 * 128, 1024), ID_O, ks > 0 ? 1u : 0u);
-        }
-        tc::commit(bar(B_OFULL + pb));
-        tc::commit(bar(B_KVFREE + pb));
-      } else {
-        *abort_flag = 1;
       }
     }
   } else {
@@ -372,13 +439,12 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
     const int tlo = max(st, p.window > 0 ? pos_max - p.window + 1 : 0);  // CTA-wide safe range
     const int thi = p.causal ? min(n, pos_min + 1) : n;
     const float q_fac = sqf[r];
+    const bool q_pos = q_fac >= 0.0f;
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
 
-    float o_acc[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o_acc[i] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
-
+    float m_run = -INFINITY, l_run = 0.0f;
+    const uint32_t o_row = tmem + 256 + lane_base;  // this thread's row of the O accumulator
+    const int lane_id = tid & 31;
     auto masked = [&](float s, int tok) -> float {
       if (!(row_ok && tok >= klo && tok < khi)) return -INFINITY;
       if constexpr (DENSE) {
@@ -397,90 +463,139 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
       return s;
     };
 
+    // O accumulates in TMEM over all tiles (P . V with accumulate after the first tile);
+    // a row's O is rescaled in TMEM only when its max moves by more than the slack.  Lane 0
+    // of softmax warp 0 issues P . V of each tile once all 128 rows of P are written (an
+    // mbarrier of 128 arrivals), so only warp 0 waits for the slowest row and the K/V
+    // buffer is released without waiting for the producers' next dequantisation.
     for (int i = 0; i < n_tiles; ++i) {
       const int buf = i & 1;
       const int t0 = lo + i * 128;
-      // warp-uniform decisions: the tcgen05.ld below is a warp-collective instruction
+      // warp-uniform decisions: tcgen05.ld / st are warp-collective instructions
       bool ok = !*abort_flag && mbar_wait_bounded(bar(B_SFULL + buf), (i >> 1) & 1);
-      if (!__all_sync(0xffffffffu, ok)) {
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc::fence_after();
+        const bool need_mask =
+            __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + 128 > thi);  // warp-uniform
+        const uint32_t s_addr = tmem + buf * 128 + lane_base;
+        // the whole S row in registers: one TMEM round trip per tile
+        float v[128];
+        tc::tmem_ld128(s_addr, v);
+        if (need_mask) {
+#pragma unroll
+          for (int j2 = 0; j2 < 128; ++j2) v[j2] = masked(v[j2] * q_fac, t0 + j2);
+        }
+        // row max with 8 independent partial maxima (raw scores when unmasked: the factor
+        // is applied once after, as a max for a positive scale and a min for a negative one)
+        float mp[8];
+        const bool take_max = need_mask || q_pos;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mp[k] = take_max ? -INFINITY : INFINITY;
+#pragma unroll
+        for (int j2 = 0; j2 < 128; ++j2)
+          mp[j2 & 7] = take_max ? fmaxf(mp[j2 & 7], v[j2]) : fminf(mp[j2 & 7], v[j2]);
+#pragma unroll
+        for (int k = 1; k < 8; ++k) mp[0] = take_max ? fmaxf(mp[0], mp[k]) : fminf(mp[0], mp[k]);
+        const float tile_max = need_mask ? mp[0] : mp[0] * q_fac;
+        // P . V of the previous tile must be done before P is rewritten (single P buffer)
+        // and before O is rescaled
+        if (i >= 1) {
+          ok = mbar_wait_bounded(bar(B_OFULL), (i - 1) & 1);
+          ok = __all_sync(0xffffffffu, ok);
+        }
+        if (ok) {
+          tc::fence_after();
+          const bool raise = tile_max > m_run + kPrefillRescaleSlack;
+          if (__any_sync(0xffffffffu, raise)) {
+            const float m_new = raise ? tile_max : m_run;
+            const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
+            if (i >= 1) rescale_o<D>(o_row, alpha);
+            l_run *= alpha;
+            m_run = m_new;
+          }
+          const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
+          const float fac = need_mask ? 1.0f : q_fac;  // masked scores already carry q_fac
+          float lp[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) lp[k] = 0.0f;
+#pragma unroll
+          for (int key0 = 0; key0 < 128; key0 += 8) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float p0 = ex2(fmaf(v[key0 + 2 * e], fac, -m_safe));
+              const float p1 = ex2(fmaf(v[key0 + 2 * e + 1], fac, -m_safe));
+              lp[(2 * e) & 7] += p0;
+              lp[(2 * e + 1) & 7] += p1;
+              pk[e] = pack_half2(p0, p1);
+            }
+            const uint32_t off = (key0 / 64) * (128 * 128) + r * 128 + ((key0 % 64) / 8) * 16;
+            *reinterpret_cast<uint4*>(smem + LY::OFF_P + tc::swz(off)) =
+                make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) l_run += lp[k];
+          tc::fence_proxy_async();
+          tc::fence_before();
+          mbar_arrive(bar(B_SFREE + buf));
+          mbar_arrive(bar(B_PFULL));
+        }
+      }
+      if (!ok) {
         *abort_flag = 1;
         break;
       }
-      tc::fence_after();
-      const bool need_mask =
-          __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + 128 > thi);  // warp-uniform
-      const uint32_t s_addr = tmem + buf * 128 + lane_base;
-      float tile_max = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tc::tmem_ld32(s_addr + c * 32, v);
-        if (need_mask) {
-#pragma unroll
-          for (int j2 = 0; j2 < 32; ++j2) tile_max = fmaxf(tile_max, masked(v[j2] * q_fac, t0 + c * 32 + j2));
-        } else {
-#pragma unroll
-          for (int j2 = 0; j2 < 32; ++j2) tile_max = fmaxf(tile_max, v[j2] * q_fac);
-        }
-      }
-      const float m_new = fmaxf(m_run, tile_max);
-      const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
-      if (i >= 1) {
-        // O of the previous tile is relative to the previous max: fold it in now
-        ok = !*abort_flag && mbar_wait_bounded(bar(B_OFULL + ((i - 1) & 1)), ((i - 1) >> 1) & 1);
-        if (!__all_sync(0xffffffffu, ok)) {
+      if (warp == 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(B_PFULL), i & 1));
+        if (!ok) {
           *abort_flag = 1;
           break;
         }
-        tc::fence_after();
-        fold_o<D>(o_acc, tmem + 256 + ((i - 1) & 1) * D + lane_base, alpha_prev);
-      }
-      l_run *= alpha;
-      m_run = m_new;
-      alpha_prev = alpha;
-      const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
-      // P row r (fp16, K-major over keys), written once the previous P . V has read P
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tc::tmem_ld32(s_addr + c * 32, v);
-        uint32_t pk[16];
+        if (lane_id == 0) {
+          tc::fence_after();
+          const uint32_t vb_addr = sV + buf * LY::TILE;
 #pragma unroll
-        for (int j2 = 0; j2 < 32; j2 += 2) {
-          float s0 = v[j2] * q_fac, s1 = v[j2 + 1] * q_fac;
-          if (need_mask) {
-            s0 = masked(s0, t0 + c * 32 + j2);
-            s1 = masked(s1, t0 + c * 32 + j2 + 1);
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t poff = (ks / 4) * (128 * 128) + (ks % 4) * 32;
+            tc::mma(tmem + 256, tc::sdesc(sP + poff, 16, 1024),
+                    tc::sdesc(vb_addr + ks * 2048, 128 * 128, 1024), ID_O, (i > 0 || ks > 0) ? 1u : 0u);
           }
-          const float p0 = ex2(s0 - m_safe), p1 = ex2(s1 - m_safe);
-          l_run += p0 + p1;
-          pk[j2 / 2] = pack_half2(p0, p1);
+          tc::commit(bar(B_OFULL));
+          tc::commit(bar(B_KVFREE + buf));
         }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int key0 = c * 32 + q4 * 8;
-          const uint32_t off = (key0 / 64) * (128 * 128) + r * 128 + ((key0 % 64) / 8) * 16;
-          *reinterpret_cast<uint4*>(smem + LY::OFF_P + tc::swz(off)) =
-              make_uint4(pk[q4 * 4], pk[q4 * 4 + 1], pk[q4 * 4 + 2], pk[q4 * 4 + 3]);
-        }
+        __syncwarp();
       }
-      tc::fence_proxy_async();
-      tc::fence_before();
-      mbar_arrive(bar(B_SFREE + buf));
-      mbar_arrive(bar(B_PFULL));
     }
+    float o_acc[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) o_acc[d] = 0.0f;
     if (n_tiles > 0 && __all_sync(0xffffffffu, !*abort_flag)) {
-      const int i = n_tiles;
-      const bool ok = mbar_wait_bounded(bar(B_OFULL + ((i - 1) & 1)), ((i - 1) >> 1) & 1);
+      const bool ok = mbar_wait_bounded(bar(B_OFULL), (n_tiles - 1) & 1);
       if (__all_sync(0xffffffffu, ok)) {
         tc::fence_after();
-        fold_o<D>(o_acc, tmem + 256 + ((i - 1) & 1) * D + lane_base, alpha_prev);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tc::tmem_ld32(o_row + c * 32, v);
+#pragma unroll
+          for (int j2 = 0; j2 < 32; ++j2) o_acc[c * 32 + j2] = v[j2];
+        }
       } else {
         *abort_flag = 1;
       }
     }
     // ---- epilogue: this thread's output row
     if (row_ok && !*abort_flag) {
+      // O columns arrive in perm8 order within each 8-dim chunk: put them back
+#pragma unroll
+      for (int c8 = 0; c8 < D / 8; ++c8) {
+        float t8[8];
+#pragma unroll
+        for (int q8 = 0; q8 < 8; ++q8) t8[q8] = o_acc[c8 * 8 + q8];
+#pragma unroll
+        for (int q8 = 0; q8 < 8; ++q8) o_acc[c8 * 8 + perm8(q8)] = t8[q8];
+      }
       const bool sink = p.sinks != nullptr;
       const float inv =
           softmax_out_factor(m_run, l_run, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
