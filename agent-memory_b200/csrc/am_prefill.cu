@@ -87,6 +87,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 #undef AM_R8
 
+// Warp loads 32 lanes x 64 consecutive fp32 columns of TMEM in one instruction.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+#define AM_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), \
+                 "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n"
+      : AM_R8(0), AM_R8(8), AM_R8(16), AM_R8(24), AM_R8(32), AM_R8(40), AM_R8(48), AM_R8(56)
+      : "r"(taddr));
+#undef AM_R8
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Warp loads 32 lanes x 128 consecutive fp32 columns of TMEM in one instruction (a whole
 // S row per thread: one TMEM round trip per tile).
 __device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
@@ -139,7 +158,8 @@ struct PrefillLayout {
   static constexpr int OFF_V = OFF_K + 2 * TILE;  // two V buffers
   static constexpr int OFF_P = OFF_V + 2 * TILE;
   static constexpr int OFF_QF = OFF_P + P_BYTES;  // per-row query factor (128 floats)
-  static constexpr int OFF_BAR = OFF_QF + 128 * 4;
+  static constexpr int OFF_RX = OFF_QF + 128 * 4;   // per-row exchange between column halves [2][128]
+  static constexpr int OFF_BAR = OFF_RX + 2 * 128 * 4;
   static constexpr int SMEM = OFF_BAR + 128 + 1024;  // barriers + slack for 1024-byte alignment
   static constexpr uint32_t TMEM_COLS = 512;     // S x2 (256) + O (D, accumulated over tiles)
   static_assert(D <= 128, "tiles sized for D <= 128");
@@ -195,19 +215,24 @@ __device__ __forceinline__ __half2 scale_h2(uint16_t bits) {
   }
 }
 
+// 12 warps: softmax warps 0-7 (warp w: S rows 32 (w % 4) .. +31, key columns 64 (w / 4)
+// .. +63 -- TMEM lane quarter w % 4 is the only one warp w may access), producer warps 8-11.
+constexpr int kPrefillThreads = 384;
+constexpr int kSoftmaxThreads = 256;
+
 // mbarrier slots (8 bytes each) inside OFF_BAR
 enum { B_SFULL = 0, B_SFREE = 2, B_OFULL = 4, B_KVFREE = 5, B_PFULL = 7, B_COUNT = 8 };
 
 // Named barrier over one 128-thread warp group that also ORs a flag across it: every
 // thread gets the same answer, so a group leaves its loop together even if the shared
 // abort flag changes while its threads read it.
-__device__ __forceinline__ bool group_bar_any(int id, bool v) {
+__device__ __forceinline__ bool group_bar_any(int id, bool v, int count = 128) {
   uint32_t r;
   asm volatile(
-      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, %2, 128, p;\n"
+      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.or.pred q, %2, %3, p;\n"
       "selp.u32 %0, 1, 0, q;\n}\n"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "r"(id)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(count)
       : "memory");
   return r != 0;
 }
@@ -216,7 +241,7 @@ __device__ __forceinline__ void named_bar_producers() {
 }
 
 template <int D, bool SBF16, bool PAGED, bool DENSE>
-__global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const DecodeParams p) {
   using LY = PrefillLayout<D>;
   constexpr int NG = D / 64;
   constexpr int KSTEPS = D / 16;
@@ -236,7 +261,7 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-  const bool producer = warp >= 4;
+  const bool producer = warp >= 8;
   const int b = blockIdx.z, h = blockIdx.y;
   const int n_rep = p.n_rep;
   const int tok_per_cta = 128 / n_rep;
@@ -258,10 +283,10 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
   if (tid == 0) {
     mbar_init(bar(B_SFULL), 1);
     mbar_init(bar(B_SFULL + 1), 1);
-    mbar_init(bar(B_SFREE), 128);
-    mbar_init(bar(B_SFREE + 1), 128);
+    mbar_init(bar(B_SFREE), kSoftmaxThreads);
+    mbar_init(bar(B_SFREE + 1), kSoftmaxThreads);
     mbar_init(bar(B_OFULL), 1);
-    mbar_init(bar(B_PFULL), 128);
+    mbar_init(bar(B_PFULL), kSoftmaxThreads);
     mbar_init(bar(B_KVFREE), 1);
     mbar_init(bar(B_KVFREE + 1), 1);
     fence_mbar_init();
@@ -274,8 +299,8 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
   }
   if (producer) {
-    // query row r = tid - 128 -> fp16 with a power-of-two prescale (exact for fp16 / bf16)
-    const int r = tid - 128;
+    // query row r = tid - 256 -> fp16 with a power-of-two prescale (exact for fp16 / bf16)
+    const int r = tid - kSoftmaxThreads;
     const int rl = r / n_rep;
     const bool row_ok = r < tok_per_cta * n_rep && l0 + rl < p.q_len;
     const int l = l0 + (row_ok ? rl : 0);
@@ -332,7 +357,7 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
 
   if (producer) {
     // ================================================================ producer warps
-    const int r = tid - 128;  // token row of each K/V tile this thread dequantizes
+    const int r = tid - kSoftmaxThreads;  // token row of each K/V tile this thread dequantizes
     // Raw Q4 data of this thread's row of a tile, loaded one tile ahead so the global
     // loads of tile j+1 are in flight while tile j is dequantized.
     struct RawRow {
@@ -428,7 +453,14 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
     }
   } else {
     // ================================================================ softmax warps
-    const int r = tid;  // query row == TMEM lane
+    // Warp w owns S rows 32 (w % 4) .. +31 (its TMEM lane quarter) and key columns
+    // 64 (w / 4) .. +63 of every tile; warps w and w + 4 share rows, exchange their row
+    // maxima through shared memory (a 64-thread named barrier per pair) and keep partial
+    // sums that are added at the end.  Each also rescales and writes back half of O.
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + (tid & 31);  // query row == TMEM lane
+    const int lane_id = tid & 31;
+    const int pair_bar = 3 + quarter;        // named barrier of warps quarter and quarter + 4
     const int rl = r / n_rep;
     const bool row_ok = r < tok_per_cta * n_rep && l0 + rl < p.q_len;
     const int l = l0 + (row_ok ? rl : 0);
@@ -440,11 +472,12 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
     const int thi = p.causal ? min(n, pos_min + 1) : n;
     const float q_fac = sqf[r];
     const bool q_pos = q_fac >= 0.0f;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    float* rx = reinterpret_cast<float*>(smem + LY::OFF_RX);  // [2][128]
+    constexpr int DH = D / 2;  // O columns this warp rescales and stores
 
     float m_run = -INFINITY, l_run = 0.0f;
     const uint32_t o_row = tmem + 256 + lane_base;  // this thread's row of the O accumulator
-    const int lane_id = tid & 31;
     auto masked = [&](float s, int tok) -> float {
       if (!(row_ok && tok >= klo && tok < khi)) return -INFINITY;
       if constexpr (DENSE) {
@@ -465,94 +498,88 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
 
     // O accumulates in TMEM over all tiles (P . V with accumulate after the first tile);
     // a row's O is rescaled in TMEM only when its max moves by more than the slack.  Lane 0
-    // of softmax warp 0 issues P . V of each tile once all 128 rows of P are written (an
-    // mbarrier of 128 arrivals), so only warp 0 waits for the slowest row and the K/V
-    // buffer is released without waiting for the producers' next dequantisation.
+    // of softmax warp 0 issues P . V of each tile once all rows of P are written (an
+    // mbarrier of 256 arrivals), so the K/V buffer is released without waiting for the
+    // producers' next dequantisation.  Every wait result is agreed by a warp pair through
+    // an OR barrier, so both halves of a row leave together.
     for (int i = 0; i < n_tiles; ++i) {
       const int buf = i & 1;
-      const int t0 = lo + i * 128;
-      // warp-uniform decisions: tcgen05.ld / st are warp-collective instructions
+      const int t0 = lo + i * 128 + half * 64;  // first key of this warp's columns
       bool ok = !*abort_flag && mbar_wait_bounded(bar(B_SFULL + buf), (i >> 1) & 1);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        tc::fence_after();
-        const bool need_mask =
-            __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + 128 > thi);  // warp-uniform
-        const uint32_t s_addr = tmem + buf * 128 + lane_base;
-        // the whole S row in registers: one TMEM round trip per tile
-        float v[128];
-        tc::tmem_ld128(s_addr, v);
-        if (need_mask) {
-#pragma unroll
-          for (int j2 = 0; j2 < 128; ++j2) v[j2] = masked(v[j2] * q_fac, t0 + j2);
-        }
-        // row max with 8 independent partial maxima (raw scores when unmasked: the factor
-        // is applied once after, as a max for a positive scale and a min for a negative one)
-        float mp[8];
-        const bool take_max = need_mask || q_pos;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mp[k] = take_max ? -INFINITY : INFINITY;
-#pragma unroll
-        for (int j2 = 0; j2 < 128; ++j2)
-          mp[j2 & 7] = take_max ? fmaxf(mp[j2 & 7], v[j2]) : fminf(mp[j2 & 7], v[j2]);
-#pragma unroll
-        for (int k = 1; k < 8; ++k) mp[0] = take_max ? fmaxf(mp[0], mp[k]) : fminf(mp[0], mp[k]);
-        const float tile_max = need_mask ? mp[0] : mp[0] * q_fac;
-        // P . V of the previous tile must be done before P is rewritten (single P buffer)
-        // and before O is rescaled
-        if (i >= 1) {
-          ok = mbar_wait_bounded(bar(B_OFULL), (i - 1) & 1);
-          ok = __all_sync(0xffffffffu, ok);
-        }
-        if (ok) {
-          tc::fence_after();
-          const bool raise = tile_max > m_run + kPrefillRescaleSlack;
-          if (__any_sync(0xffffffffu, raise)) {
-            const float m_new = raise ? tile_max : m_run;
-            const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
-            if (i >= 1) rescale_o<D>(o_row, alpha);
-            l_run *= alpha;
-            m_run = m_new;
-          }
-          const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
-          const float fac = need_mask ? 1.0f : q_fac;  // masked scores already carry q_fac
-          float lp[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) lp[k] = 0.0f;
-#pragma unroll
-          for (int key0 = 0; key0 < 128; key0 += 8) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float p0 = ex2(fmaf(v[key0 + 2 * e], fac, -m_safe));
-              const float p1 = ex2(fmaf(v[key0 + 2 * e + 1], fac, -m_safe));
-              lp[(2 * e) & 7] += p0;
-              lp[(2 * e + 1) & 7] += p1;
-              pk[e] = pack_half2(p0, p1);
-            }
-            const uint32_t off = (key0 / 64) * (128 * 128) + r * 128 + ((key0 % 64) / 8) * 16;
-            *reinterpret_cast<uint4*>(smem + LY::OFF_P + tc::swz(off)) =
-                make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          }
-#pragma unroll
-          for (int k = 0; k < 8; ++k) l_run += lp[k];
-          tc::fence_proxy_async();
-          tc::fence_before();
-          mbar_arrive(bar(B_SFREE + buf));
-          mbar_arrive(bar(B_PFULL));
-        }
-      }
-      if (!ok) {
+      if (group_bar_any(pair_bar, !ok, 64)) {
         *abort_flag = 1;
         break;
       }
-      if (warp == 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(B_PFULL), i & 1));
-        if (!ok) {
-          *abort_flag = 1;
-          break;
+      tc::fence_after();
+      const bool need_mask =
+          __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + 64 > thi);  // warp-uniform
+      float v[64];
+      tc::tmem_ld64(tmem + buf * 128 + half * 64 + lane_base, v);
+      if (need_mask) {
+#pragma unroll
+        for (int j2 = 0; j2 < 64; ++j2) v[j2] = masked(v[j2] * q_fac, t0 + j2);
+      }
+      float mp[8];
+      const bool take_max = need_mask || q_pos;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mp[k] = take_max ? -INFINITY : INFINITY;
+#pragma unroll
+      for (int j2 = 0; j2 < 64; ++j2)
+        mp[j2 & 7] = take_max ? fmaxf(mp[j2 & 7], v[j2]) : fminf(mp[j2 & 7], v[j2]);
+#pragma unroll
+      for (int k = 1; k < 8; ++k) mp[0] = take_max ? fmaxf(mp[0], mp[k]) : fminf(mp[0], mp[k]);
+      const float my_max = need_mask ? mp[0] : mp[0] * q_fac;
+      rx[half * 128 + r] = my_max;
+      // P . V of the previous tile must be done before P is rewritten (single P buffer)
+      // and before O is rescaled
+      ok = i == 0 || mbar_wait_bounded(bar(B_OFULL), (i - 1) & 1);
+      if (group_bar_any(pair_bar, !ok, 64)) {  // also publishes rx between the pair
+        *abort_flag = 1;
+        break;
+      }
+      tc::fence_after();
+      const float tile_max = fmaxf(my_max, rx[(half ^ 1) * 128 + r]);
+      const bool raise = tile_max > m_run + kPrefillRescaleSlack;
+      if (__any_sync(0xffffffffu, raise)) {  // the same rows, so the same answer in both halves
+        const float m_new = raise ? tile_max : m_run;
+        const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
+        if (i >= 1) rescale_o<DH>(o_row + half * DH, alpha);
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
+      const float fac = need_mask ? 1.0f : q_fac;  // masked scores already carry q_fac
+      float lp[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) lp[k] = 0.0f;
+#pragma unroll
+      for (int key0 = 0; key0 < 64; key0 += 8) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = ex2(fmaf(v[key0 + 2 * e], fac, -m_safe));
+          const float p1 = ex2(fmaf(v[key0 + 2 * e + 1], fac, -m_safe));
+          lp[(2 * e) & 7] += p0;
+          lp[(2 * e + 1) & 7] += p1;
+          pk[e] = pack_half2(p0, p1);
         }
-        if (lane_id == 0) {
+        const int key = half * 64 + key0;
+        const uint32_t off = (key / 64) * (128 * 128) + r * 128 + ((key % 64) / 8) * 16;
+        *reinterpret_cast<uint4*>(smem + LY::OFF_P + tc::swz(off)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) l_run += lp[k];
+      tc::fence_proxy_async();
+      tc::fence_before();
+      mbar_arrive(bar(B_SFREE + buf));
+      mbar_arrive(bar(B_PFULL));
+      if (warp == 0) {
+        // a failed wait only raises the flag: warp 0 must not leave its pair (warp 4)
+        // waiting in their barrier, so both see the flag at the next pair barrier
+        ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(B_PFULL), i & 1));
+        if (!ok) *abort_flag = 1;
+        if (ok && lane_id == 0) {
           tc::fence_after();
           const uint32_t vb_addr = sV + buf * LY::TILE;
 #pragma unroll
@@ -567,70 +594,72 @@ __global__ void __launch_bounds__(256, 1) prefill_kernel(const DecodeParams p) {
         __syncwarp();
       }
     }
-    float o_acc[D];
+    // ---- epilogue: this thread's half of its output row.  The pair adds its partial sums
+    // (the OR barrier also publishes them); O columns arrive in perm8 order within each
+    // 8-dim chunk and are put back before the store.
+    bool fin = n_tiles > 0 && !*abort_flag;
+    if (fin) fin = mbar_wait_bounded(bar(B_OFULL), (n_tiles - 1) & 1);
+    fin = __all_sync(0xffffffffu, fin);
+    rx[half * 128 + r] = l_run;
+    const bool bad = group_bar_any(pair_bar, !fin, 64);
+    if (!bad) {
+      tc::fence_after();
+      float o_acc[DH];
 #pragma unroll
-    for (int d = 0; d < D; ++d) o_acc[d] = 0.0f;
-    if (n_tiles > 0 && __all_sync(0xffffffffu, !*abort_flag)) {
-      const bool ok = mbar_wait_bounded(bar(B_OFULL), (n_tiles - 1) & 1);
-      if (__all_sync(0xffffffffu, ok)) {
-        tc::fence_after();
+      for (int c = 0; c < DH / 32; ++c) {
+        float t32[32];
+        tc::tmem_ld32(o_row + half * DH + c * 32, t32);
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tc::tmem_ld32(o_row + c * 32, v);
-#pragma unroll
-          for (int j2 = 0; j2 < 32; ++j2) o_acc[c * 32 + j2] = v[j2];
-        }
-      } else {
-        *abort_flag = 1;
+        for (int j2 = 0; j2 < 32; ++j2) o_acc[c * 32 + j2] = t32[j2];
       }
-    }
-    // ---- epilogue: this thread's output row
-    if (row_ok && !*abort_flag) {
-      // O columns arrive in perm8 order within each 8-dim chunk: put them back
+      if (row_ok) {
+        const float l_tot = rx[r] + rx[128 + r];
 #pragma unroll
-      for (int c8 = 0; c8 < D / 8; ++c8) {
-        float t8[8];
+        for (int c8 = 0; c8 < DH / 8; ++c8) {
+          float t8[8];
 #pragma unroll
-        for (int q8 = 0; q8 < 8; ++q8) t8[q8] = o_acc[c8 * 8 + q8];
+          for (int q8 = 0; q8 < 8; ++q8) t8[q8] = o_acc[c8 * 8 + q8];
 #pragma unroll
-        for (int q8 = 0; q8 < 8; ++q8) o_acc[c8 * 8 + perm8(q8)] = t8[q8];
-      }
-      const bool sink = p.sinks != nullptr;
-      const float inv =
-          softmax_out_factor(m_run, l_run, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
-      const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl;
-      if (p.out_dtype == AM_DTYPE_F32) {
-        float* o = static_cast<float*>(p.out) + ob;
-        if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-#pragma unroll
-          for (int d = 0; d < D; d += 4)
-            *reinterpret_cast<float4*>(o + d) =
-                make_float4(o_acc[d] * inv, o_acc[d + 1] * inv, o_acc[d + 2] * inv, o_acc[d + 3] * inv);
-        } else {
-#pragma unroll
-          for (int d = 0; d < D; ++d) o[d] = o_acc[d] * inv;
+          for (int q8 = 0; q8 < 8; ++q8) o_acc[c8 * 8 + perm8(q8)] = t8[q8];
         }
-      } else {
-        const bool bf = p.out_dtype == AM_DTYPE_BF16;
-        uint16_t* o = static_cast<uint16_t*>(p.out) + ob;
-        if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+        const bool sink = p.sinks != nullptr;
+        const float inv =
+            softmax_out_factor(m_run, l_tot, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
+        const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + half * DH;
+        if (p.out_dtype == AM_DTYPE_F32) {
+          float* o = static_cast<float*>(p.out) + ob;
+          if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
-          for (int d = 0; d < D; d += 8) {
-            uint32_t w[4];
+            for (int d = 0; d < DH; d += 4)
+              *reinterpret_cast<float4*>(o + d) =
+                  make_float4(o_acc[d] * inv, o_acc[d + 1] * inv, o_acc[d + 2] * inv, o_acc[d + 3] * inv);
+          } else {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float a = o_acc[d + 2 * e] * inv, c2 = o_acc[d + 2 * e + 1] * inv;
-              w[e] = bf ? (static_cast<uint32_t>(f2h<true>(a)) | (static_cast<uint32_t>(f2h<true>(c2)) << 16))
-                        : pack_half2(a, c2);
-            }
-            *reinterpret_cast<uint4*>(o + d) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int d = 0; d < DH; ++d) o[d] = o_acc[d] * inv;
           }
         } else {
+          const bool bf = p.out_dtype == AM_DTYPE_BF16;
+          uint16_t* o = static_cast<uint16_t*>(p.out) + ob;
+          if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
-          for (int d = 0; d < D; ++d) o[d] = bf ? f2h<true>(o_acc[d] * inv) : f2h<false>(o_acc[d] * inv);
+            for (int d = 0; d < DH; d += 8) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float a = o_acc[d + 2 * e] * inv, c2 = o_acc[d + 2 * e + 1] * inv;
+                w[e] = bf ? (static_cast<uint32_t>(f2h<true>(a)) | (static_cast<uint32_t>(f2h<true>(c2)) << 16))
+                          : pack_half2(a, c2);
+              }
+              *reinterpret_cast<uint4*>(o + d) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+#pragma unroll
+            for (int d = 0; d < DH; ++d) o[d] = bf ? f2h<true>(o_acc[d] * inv) : f2h<false>(o_acc[d] * inv);
+          }
         }
       }
+    } else {
+      *abort_flag = 1;
     }
   }
 
@@ -660,7 +689,7 @@ static cudaError_t launch_prefill_t(const DecodeParams& p, int batch, cudaStream
   }
   const int tok_per_cta = 128 / p.n_rep;
   dim3 grid((p.q_len + tok_per_cta - 1) / tok_per_cta, p.hkv, batch);
-  kfn<<<grid, 256, LY::SMEM, stream>>>(p);
+  kfn<<<grid, kPrefillThreads, LY::SMEM, stream>>>(p);
   return cudaGetLastError();
 }
 
