@@ -82,6 +82,16 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Four 8x8 b16 matrices from shared memory, transposed: lane L supplies the row address
+// (16 bytes) of row L % 8 of matrix L / 8; lane (g, t) receives in r_k the b16 elements
+// (row 2t, column g) [low half] and (row 2t + 1, column g) [high half] of matrix k.
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
 // Transpose an 8x8 matrix of 16-bit values held in mma fragment layout across the warp.
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t y;
