@@ -510,35 +510,56 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       l_run[0] += pr[0] + pr[2];
       l_run[1] += pr[1] + pr[3];
       // scale / bias of the element's token row (g + 8 tr)
-      float sv[2][NGV], bv[2][NGV];
+      float bv[2][NGV];
 #pragma unroll
-      for (int tr = 0; tr < 2; ++tr) {
-        load_scales<NGV, SBF16>(stg + LY::OFF_VS, hh * 16 + g + 8 * tr, sv[tr]);
-        load_scales<NGV, SBF16>(stg + LY::OFF_VB, hh * 16 + g + 8 * tr, bv[tr]);
-      }
-      float svc[2][2][NGV], bvc[2][2][NGV];  // [tr][column][G]
+      for (int tr = 0; tr < 2; ++tr) load_scales<NGV, SBF16>(stg + LY::OFF_VB, hh * 16 + g + 8 * tr, bv[tr]);
+      float bvc[2][2][NGV];  // [tr][column][G]
 #pragma unroll
       for (int tr = 0; tr < 2; ++tr)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
+          for (int G = 0; G < NGV; ++G) bvc[tr][c][G] = bv[tr][G];
+      // B = P * scale_v per 64-dim group, as fp16 pairs (columns 2t, 2t+1) of token rows g
+      // and g + 8: fp16 scales multiply the packed P pairs directly (HMUL2); bf16 scales go
+      // through fp32
+      uint32_t bpk[2][NGV];
+      if constexpr (!SBF16) {
+        const __half2 p0 = __floats2half2_rn(pr[0], pr[1]), p1 = __floats2half2_rn(pr[2], pr[3]);
+#pragma unroll
+        for (int tr = 0; tr < 2; ++tr) {
+          const uint16_t* sr = reinterpret_cast<const uint16_t*>(stg + LY::OFF_VS) + (hh * 16 + g + 8 * tr) * NGV;
+          // an excluded row (p = 0 in both columns) may hold stale shared memory: a zero
+          // scale keeps 0 * scale from turning into NaN
+          const bool row_live = !masked_stage || pr[2 * tr] > 0.0f || pr[2 * tr + 1] > 0.0f;
+#pragma unroll
           for (int G = 0; G < NGV; ++G) {
-            svc[tr][c][G] = sv[tr][G];
-            bvc[tr][c][G] = bv[tr][G];
+            const __half sh = row_live ? __ushort_as_half(sr[G]) : __ushort_as_half(0);
+            const __half2 prod = __hmul2(tr ? p1 : p0, __half2half2(sh));
+            bpk[tr][G] = *reinterpret_cast<const uint32_t*>(&prod);
           }
+        }
+      } else {
+        float sv[2][NGV];
+#pragma unroll
+        for (int tr = 0; tr < 2; ++tr) load_scales<NGV, SBF16>(stg + LY::OFF_VS, hh * 16 + g + 8 * tr, sv[tr]);
+#pragma unroll
+        for (int tr = 0; tr < 2; ++tr)
+#pragma unroll
+          for (int G = 0; G < NGV; ++G) {
+            const bool l0 = !masked_stage || pr[2 * tr] > 0.0f, l1 = !masked_stage || pr[2 * tr + 1] > 0.0f;
+            bpk[tr][G] = pack_half2(l0 ? pr[2 * tr] * sv[tr][G] : 0.0f, l1 ? pr[2 * tr + 1] * sv[tr][G] : 0.0f);
+          }
+      }
       if (masked_stage) {
-        // rows of excluded keys may hold stale shared memory (not loaded, or beyond the
-        // written length): zero their scale and bias so p = 0 cannot meet a NaN
+        // rows of excluded keys may hold stale shared memory: zero their bias
 #pragma unroll
         for (int tr = 0; tr < 2; ++tr)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const bool live = pr[2 * tr + c] > 0.0f;
 #pragma unroll
-            for (int G = 0; G < NGV; ++G) {
-              svc[tr][c][G] = live ? svc[tr][c][G] : 0.0f;
-              bvc[tr][c][G] = live ? bvc[tr][c][G] : 0.0f;
-            }
+            for (int G = 0; G < NGV; ++G) bvc[tr][c][G] = live ? bvc[tr][c][G] : 0.0f;
           }
       }
       // V^T tiles by ldmatrix.trans: matrices (tokens 0-7 | 8-15) x (dims 0-31 | 32-63 of
@@ -550,8 +571,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       for (int G = 0; G < NGV; ++G) {
         vbias[0][G] = fmaf(pr[0], bvc[0][0][G], fmaf(pr[2], bvc[1][0][G], vbias[0][G]));
         vbias[1][G] = fmaf(pr[1], bvc[0][1][G], fmaf(pr[3], bvc[1][1][G], vbias[1][G]));
-        const uint32_t bl = movmatrix_trans(pack_half2(pr[0] * svc[0][0][G], pr[1] * svc[0][1][G]));
-        const uint32_t bh = movmatrix_trans(pack_half2(pr[2] * svc[1][0][G], pr[3] * svc[1][1][G]));
+        const uint32_t bl = movmatrix_trans(bpk[0][G]);
+        const uint32_t bh = movmatrix_trans(bpk[1][G]);
         uint32_t m0, m1, m2, m3;  // (tok 0-7, seg 0) (tok 0-7, seg 1) (tok 8-15, seg 0) (tok 8-15, seg 1)
         ldsm_x4_trans(vrow_addr + G * 32, m0, m1, m2, m3);
         const uint32_t h0 = m0 >> 8, h1 = m1 >> 8, h2 = m2 >> 8, h3 = m3 >> 8;
