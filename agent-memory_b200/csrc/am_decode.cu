@@ -336,14 +336,30 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     }
   }
   // Per-column (2t, 2t+1) constants.
-  float fac[2], qb[2][NGK];
+  // Bias term of the scores, sum_G bias_G[token] * qsum_G[column], as one MMA per 16-token
+  // tile: A holds the token's group biases (k = 2G, 2G + 1 both bias_G), B the column's
+  // scaled query sums split into a high and a low 16-bit part (k = 2G: high, 2G + 1: low),
+  // so the product keeps fp32 accuracy.  Lane (g, t) supplies B for column g, group t.
+  uint32_t yb = 0;
+  if (t < NGK) {
+    const float v = qsum_s[g * NGK + t] * p.scale_log2;
+    if constexpr (SBF16) {
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+      yb = static_cast<uint32_t>(__bfloat16_as_ushort(hi)) | (static_cast<uint32_t>(__bfloat16_as_ushort(lo)) << 16);
+    } else {
+      const __half hi = __float2half_rn(v);
+      const __half lo = __float2half_rn(v - __half2float(hi));
+      yb = static_cast<uint32_t>(__half_as_ushort(hi)) | (static_cast<uint32_t>(__half_as_ushort(lo)) << 16);
+    }
+  }
+  float fac[2];
   int pos_c[2], l_c[2], hq_c[2];
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const int col = 2 * t + c;
     fac[c] = 16777216.0f / col_pw[col] * p.scale_log2;  // 2^24 undoes the subnormal code encoding
 #pragma unroll
-    for (int G = 0; G < NGK; ++G) qb[c][G] = qsum_s[col * NGK + G] * p.scale_log2;
     hq_c[c] = col_i[col * 4 + 0];
     l_c[c] = col_i[col * 4 + 1];
     pos_c[c] = col_i[col * 4 + 2];
@@ -417,21 +433,32 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
     float s2[NH][4];
 #pragma unroll
     for (int hh = 0; hh < NH; ++hh) {
+      float y[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      {
+        uint32_t ya0 = 0, ya1 = 0;
+        if (t < NGK) {
+          const uint16_t* kb = reinterpret_cast<const uint16_t*>(stg + LY::OFF_KB);
+          const uint32_t b0 = kb[(hh * 16 + g) * NGK + t], b8 = kb[(hh * 16 + g + 8) * NGK + t];
+          ya0 = b0 | (b0 << 16);
+          ya1 = b8 | (b8 << 16);
+        }
+        if constexpr (SBF16) {
+          mma_bf16_16816(y, ya0, ya1, 0u, 0u, yb, 0u);
+        } else {
+          mma_f16_16816(y, ya0, ya1, 0u, 0u, yb, 0u);
+        }
+      }
 #pragma unroll
       for (int tr = 0; tr < 2; ++tr) {
-        float sk[NGK], bk[NGK];
+        float sk[NGK];
         load_scales<NGK, SBF16>(stg + LY::OFF_KS, hh * 16 + g + 8 * tr, sk);
-        load_scales<NGK, SBF16>(stg + LY::OFF_KB, hh * 16 + g + 8 * tr, bk);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           const int e = 2 * tr + c;
-          float x = 0.0f, y = 0.0f;
+          float x = 0.0f;
 #pragma unroll
-          for (int G = 0; G < NGK; ++G) {
-            x = fmaf(sk[G], acc[hh][G][e], x);
-            y = fmaf(bk[G], qb[c][G], y);
-          }
-          s2[hh][e] = fmaf(x, fac[c], y);
+          for (int G = 0; G < NGK; ++G) x = fmaf(sk[G], acc[hh][G][e], x);
+          s2[hh][e] = fmaf(x, fac[c], y[e]);
         }
       }
     }
