@@ -106,6 +106,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   constexpr int KROW = LY::KROW, VROW = LY::VROW;
   constexpr int KSTEPS = DK / 16;
   constexpr int MT = DV / 16;
+  constexpr bool V_LDSM = VROW <= 64;  // ldmatrix V tiles unless the rows are 128 bytes
 
   extern __shared__ __align__(128) uint8_t smem[];
 
@@ -589,28 +590,54 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
             for (int G = 0; G < NGV; ++G) bvc[tr][c][G] = live ? bvc[tr][c][G] : 0.0f;
           }
       }
-      // V^T tiles by ldmatrix.trans: matrices (tokens 0-7 | 8-15) x (dims 0-31 | 32-63 of
-      // group G); lane (g, t) gets the 4 codes of dims 4g..4g+3 of tokens 2t and 2t+1 in
-      // one register, and nibble j of each half is MMA row g's operand for MMA j
-      const uint32_t vrow_addr = smem_u32(stg + LY::OFF_V) +
-                                 (hh * 16 + ((lane >> 4) << 3) + (lane & 7)) * VROW + ((lane >> 3) & 1) * 16;
+      if constexpr (V_LDSM) {
+        // V^T tiles by ldmatrix.trans: matrices (tokens 0-7 | 8-15) x (dims 0-31 | 32-63 of
+        // group G); lane (g, t) gets the 4 codes of dims 4g..4g+3 of tokens 2t and 2t+1 in
+        // one register, and nibble j of each half is MMA row g's operand for MMA j
+        const uint32_t vrow_addr = smem_u32(stg + LY::OFF_V) +
+                                   (hh * 16 + ((lane >> 4) << 3) + (lane & 7)) * VROW + ((lane >> 3) & 1) * 16;
 #pragma unroll
-      for (int G = 0; G < NGV; ++G) {
-        vbias[0][G] = fmaf(pr[0], bvc[0][0][G], fmaf(pr[2], bvc[1][0][G], vbias[0][G]));
-        vbias[1][G] = fmaf(pr[1], bvc[0][1][G], fmaf(pr[3], bvc[1][1][G], vbias[1][G]));
-        const uint32_t bl = movmatrix_trans(bpk[0][G]);
-        const uint32_t bh = movmatrix_trans(bpk[1][G]);
-        uint32_t m0, m1, m2, m3;  // (tok 0-7, seg 0) (tok 0-7, seg 1) (tok 8-15, seg 0) (tok 8-15, seg 1)
-        ldsm_x4_trans(vrow_addr + G * 32, m0, m1, m2, m3);
-        const uint32_t h0 = m0 >> 8, h1 = m1 >> 8, h2 = m2 >> 8, h3 = m3 >> 8;
-        mma_f16_16816(o[4 * G + 0], m0 & 0x000F000Fu, m1 & 0x000F000Fu, m2 & 0x000F000Fu,
-                      m3 & 0x000F000Fu, bl, bh);
-        mma_f16_16816(o[4 * G + 1], m0 & 0x00F000F0u, m1 & 0x00F000F0u, m2 & 0x00F000F0u,
-                      m3 & 0x00F000F0u, bl, bh);
-        mma_f16_16816(o[4 * G + 2], h0 & 0x000F000Fu, h1 & 0x000F000Fu, h2 & 0x000F000Fu,
-                      h3 & 0x000F000Fu, bl, bh);
-        mma_f16_16816(o[4 * G + 3], h0 & 0x00F000F0u, h1 & 0x00F000F0u, h2 & 0x00F000F0u,
-                      h3 & 0x00F000F0u, bl, bh);
+        for (int G = 0; G < NGV; ++G) {
+          vbias[0][G] = fmaf(pr[0], bvc[0][0][G], fmaf(pr[2], bvc[1][0][G], vbias[0][G]));
+          vbias[1][G] = fmaf(pr[1], bvc[0][1][G], fmaf(pr[3], bvc[1][1][G], vbias[1][G]));
+          const uint32_t bl = movmatrix_trans(bpk[0][G]);
+          const uint32_t bh = movmatrix_trans(bpk[1][G]);
+          uint32_t m0, m1, m2, m3;  // (tok 0-7, seg 0) (tok 0-7, seg 1) (tok 8-15, seg 0) (tok 8-15, seg 1)
+          ldsm_x4_trans(vrow_addr + G * 32, m0, m1, m2, m3);
+          const uint32_t h0 = m0 >> 8, h1 = m1 >> 8, h2 = m2 >> 8, h3 = m3 >> 8;
+          mma_f16_16816(o[4 * G + 0], m0 & 0x000F000Fu, m1 & 0x000F000Fu, m2 & 0x000F000Fu,
+                        m3 & 0x000F000Fu, bl, bh);
+          mma_f16_16816(o[4 * G + 1], m0 & 0x00F000F0u, m1 & 0x00F000F0u, m2 & 0x00F000F0u,
+                        m3 & 0x00F000F0u, bl, bh);
+          mma_f16_16816(o[4 * G + 2], h0 & 0x000F000Fu, h1 & 0x000F000Fu, h2 & 0x000F000Fu,
+                        h3 & 0x000F000Fu, bl, bh);
+          mma_f16_16816(o[4 * G + 3], h0 & 0x00F000F0u, h1 & 0x00F000F0u, h2 & 0x00F000F0u,
+                        h3 & 0x00F000F0u, bl, bh);
+        }
+      } else {
+        // 128-byte V rows (Dv = 256) would put all 8 rows of an ldmatrix tile in one bank
+        // group: gather token pairs with byte permutes instead (row-to-row stride 4 lanes)
+        const uint8_t* vbase = stg + LY::OFF_V + hh * 16 * VROW;
+#pragma unroll
+        for (int G = 0; G < NGV; ++G) {
+          vbias[0][G] = fmaf(pr[0], bvc[0][0][G], fmaf(pr[2], bvc[1][0][G], vbias[0][G]));
+          vbias[1][G] = fmaf(pr[1], bvc[0][1][G], fmaf(pr[3], bvc[1][1][G], vbias[1][G]));
+          const uint32_t bl = movmatrix_trans(bpk[0][G]);
+          const uint32_t bh = movmatrix_trans(bpk[1][G]);
+          const int woff = (8 * G + g) * 4;
+          const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * VROW + woff);
+          const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * VROW + woff);
+          const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * VROW + woff);
+          const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * VROW + woff);
+#pragma unroll
+          for (int beta = 0; beta < 4; ++beta) {
+            const uint32_t sel = beta | ((4 + beta) << 8);
+            const uint32_t r01 = __byte_perm(v0, v1, sel);
+            const uint32_t r23 = __byte_perm(v2, v3, sel);
+            mma_f16_16816(o[4 * G + beta], r01 & 0x000F000Fu, r01 & 0x00F000F0u, r23 & 0x000F000Fu,
+                          r23 & 0x00F000F0u, bl, bh);
+          }
+        }
       }
     }
     __syncwarp();
@@ -650,15 +677,24 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   float* wo = wres + 16;
 #pragma unroll
   for (int mt_i = 0; mt_i < MT; ++mt_i) {
-    // tile 4G + j: row g is dim 64G + 4g + j, row g + 8 is dim 64G + 32 + 4g + j; odd j
-    // took the high nibble (code * 2^-20), even j the low one (code * 2^-24)
     const int G = mt_i / 4, j = mt_i % 4;
-    const int d = 64 * G + 4 * g + j;
-    const float sc = (j & 1) ? 1048576.0f : 16777216.0f;
-    wo[(2 * t) * OS + d] = fmaf(o[mt_i][0], sc, vbias[0][G]);
-    wo[(2 * t + 1) * OS + d] = fmaf(o[mt_i][1], sc, vbias[1][G]);
-    wo[(2 * t) * OS + d + 32] = fmaf(o[mt_i][2], sc, vbias[0][G]);
-    wo[(2 * t + 1) * OS + d + 32] = fmaf(o[mt_i][3], sc, vbias[1][G]);
+    if constexpr (V_LDSM) {
+      // tile 4G + j: row g is dim 64G + 4g + j, row g + 8 is dim 64G + 32 + 4g + j; odd j
+      // took the high nibble (code * 2^-20), even j the low one (code * 2^-24)
+      const int d = 64 * G + 4 * g + j;
+      const float sc = (j & 1) ? 1048576.0f : 16777216.0f;
+      wo[(2 * t) * OS + d] = fmaf(o[mt_i][0], sc, vbias[0][G]);
+      wo[(2 * t + 1) * OS + d] = fmaf(o[mt_i][1], sc, vbias[1][G]);
+      wo[(2 * t) * OS + d + 32] = fmaf(o[mt_i][2], sc, vbias[0][G]);
+      wo[(2 * t + 1) * OS + d + 32] = fmaf(o[mt_i][3], sc, vbias[1][G]);
+    } else {
+      // tile 4G + j: rows g / g + 8 are dims 64G + 8g + 2j / +1 (low / high nibble)
+      const int d = 64 * G + 8 * g + 2 * j;
+      wo[(2 * t) * OS + d] = fmaf(o[mt_i][0], 16777216.0f, vbias[0][G]);
+      wo[(2 * t + 1) * OS + d] = fmaf(o[mt_i][1], 16777216.0f, vbias[1][G]);
+      wo[(2 * t) * OS + d + 1] = fmaf(o[mt_i][2], 1048576.0f, vbias[0][G]);
+      wo[(2 * t + 1) * OS + d + 1] = fmaf(o[mt_i][3], 1048576.0f, vbias[1][G]);
+    }
   }
   __syncthreads();
 
