@@ -136,7 +136,7 @@ static int check_args(const am_q4_cache* c, const am_attn_args* a, const char* f
 // and the KV split.  The span of a windowed call is the window plus the query rows, plus
 // up to one stage of keys from rounding the first key down to a stage boundary.
 static int decode_geometry(const am_q4_cache* c, const am_attn_args* a, int* row_groups,
-                           int* chunk, int* n_chunks) {
+                           int* chunk, int* n_chunks, int* cluster) {
   const int n_rep = a->n_q_heads / c->n_kv_heads;
   const int rows = n_rep * a->q_len;
   *row_groups = (rows + 7) / 8;
@@ -146,7 +146,7 @@ static int decode_geometry(const am_q4_cache* c, const am_attn_args* a, int* row
     if (w < span) span = static_cast<int>(w);
   }
   decode_plan(a->batch, c->n_kv_heads, *row_groups, span, decode_ctas_per_sm(c->k_dim, c->v_dim),
-              chunk, n_chunks);
+              c->k_dim, c->v_dim, chunk, n_chunks, cluster);
   return rows;
 }
 
@@ -303,9 +303,9 @@ int am_q4_append(const am_q4_cache* cache, const void* k, const void* v, int32_t
 size_t am_q4_attention_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args) {
   if (cache == nullptr || args == nullptr || cache->n_kv_heads <= 0 || args->n_q_heads <= 0)
     return 0;
-  int row_groups, chunk, n_chunks;
-  decode_geometry(cache, args, &row_groups, &chunk, &n_chunks);
-  if (n_chunks <= 1) return 0;
+  int row_groups, chunk, n_chunks, cluster;
+  decode_geometry(cache, args, &row_groups, &chunk, &n_chunks, &cluster);
+  if (n_chunks <= 1 || cluster) return 0;
   const size_t rows_total = static_cast<size_t>(args->n_q_heads) * args->q_len;
   return static_cast<size_t>(args->batch) * rows_total * n_chunks * (cache->v_dim + kPartialHead) *
          sizeof(float);
@@ -340,8 +340,8 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
     return AM_ERR_UNSUPPORTED;
   }
   if (a->batch == 0 || a->q_len == 0) return AM_OK;
-  int row_groups, chunk, n_chunks;
-  decode_geometry(cache, a, &row_groups, &chunk, &n_chunks);
+  int row_groups, chunk, n_chunks, cluster;
+  decode_geometry(cache, a, &row_groups, &chunk, &n_chunks, &cluster);
   const size_t need = am_q4_attention_workspace_bytes(cache, a);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))) {
     set_error("am_q4_decode: workspace of %zu bytes required (got %zu)", need, workspace_bytes);
@@ -353,6 +353,7 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
   p.max_chunks = n_chunks;
   p.stage_tokens = decode_stage_tokens(cache->k_dim, cache->v_dim);
   p.ws = static_cast<float*>(workspace);
+  p.cluster = cluster;
   return cuda_status(launch_decode(p, a->batch, row_groups, cache->layout == AM_LAYOUT_PAGED,
                                    cache->scale_dtype == AM_DTYPE_BF16,
                                    static_cast<cudaStream_t>(stream)),

@@ -195,6 +195,24 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
+// Thread-block cluster primitives: a full cluster barrier (every thread of every CTA of the
+// cluster; writes before it are visible to reads after it across the cluster), the
+// distributed-shared-memory address of a peer CTA's copy of a local shared address, and
+// a 32-bit load through that address.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // Final softmax normalisation of one query row from its running max m and sum l (log2
 // units), with an optional attention sink s2 (log2 units): returns the factor that turns
 // the unnormalised output O into O * w / den, i.e. w / den, so that
@@ -307,6 +325,8 @@ struct DecodeParams {
   int32_t max_chunks;  // grid.x
   float* ws;           // partials [batch][hq*q_len][max_chunks][kPartialHead + v_dim]
   const float* sinks;  // [hq] sink logits (scaled-score units) or nullptr
+  int32_t cluster;     // 1: the max_chunks CTAs of a column are one thread-block cluster and
+                       // merge their partials through distributed shared memory (no ws)
 };
 
 // Visible key range of a sequence for the structured mask: keys outside [lo, hi) are

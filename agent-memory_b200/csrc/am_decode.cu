@@ -28,6 +28,7 @@
 // softmax, P.V; GQA head h -> KV head h / n_rep) and the Metal decode kernel's online
 // softmax (mlx_fused_attention.py:320-361).  Accumulation is fp32 throughout.
 #include <cfloat>
+#include <cstdlib>
 
 #include "am_common.cuh"
 #include "am_internal.h"
@@ -36,6 +37,7 @@ namespace am {
 
 constexpr int kWarps = 4;
 constexpr int kMaxChunk = 2048;            // tokens per CTA chunk (decode_plan never exceeds it)
+constexpr int kMaxCluster = 16;            // chunks merged inside one thread-block cluster
 constexpr int kMaxBlk = kMaxChunk / 32 + 2;  // block ids a chunk can touch (block_tokens >= 32)
 constexpr float kMaskedFinite = -1.0e30f;  // boolean-mask fill (finite: keeps uniform rows)
 
@@ -133,10 +135,14 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   if (n_chunks_need > p.max_chunks && chunk == 0 && blockIdx.y == 0 && threadIdx.x == 0)
     flag_status(p.status, AM_STATUS_BAD_POSITION);  // kv_len beyond the planned max_kv_len
   const int n_chunks_b = min(n_chunks_need, p.max_chunks);
-  if (chunk >= n_chunks_b) return;
+  // A chunk past this sequence's span has no keys.  In cluster mode its CTA still runs to
+  // the end (with no stages): every CTA of a cluster takes part in the cluster barriers
+  // and in the merge.
+  const bool idle = chunk >= n_chunks_b;
+  if (idle && !p.cluster) return;
   const int c_lo = lo + chunk * p.chunk;
   const int c_hi = min(c_lo + p.chunk, hi);
-  const int n_stages = c_hi > c_lo ? (c_hi - c_lo + TS - 1) / TS : 0;
+  const int n_stages = (!idle && c_hi > c_lo) ? (c_hi - c_lo + TS - 1) / TS : 0;
   const int my_stages = n_stages > warp ? (n_stages - warp + kWarps - 1) / kWarps : 0;
 
   uint8_t* ring = smem + warp * LY::RING;
@@ -360,7 +366,6 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   for (int c = 0; c < 2; ++c) {
     const int col = 2 * t + c;
     fac[c] = 16777216.0f / col_pw[col] * p.scale_log2;  // 2^24 undoes the subnormal code encoding
-#pragma unroll
     hq_c[c] = col_i[col * 4 + 0];
     l_c[c] = col_i[col * 4 + 1];
     pos_c[c] = col_i[col * 4 + 2];
@@ -723,6 +728,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
         softmax_out_factor(M, L, sink, sink ? p.sinks[col_i[tid * 4 + 0]] * 1.4426950408889634f : 0.0f);
   }
   __syncthreads();
+  float* wres0 = reinterpret_cast<float*>(smem);  // warp 0's result
   for (int i = tid; i < 8 * DV; i += 128) {
     const int c = i / DV, d = i % DV;
     if (!col_i[c * 4 + 3]) continue;
@@ -730,7 +736,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
 #pragma unroll
     for (int w = 0; w < kWarps; ++w)
       O = fmaf(reinterpret_cast<const float*>(smem + w * LY::RING)[16 + c * OS + d], cf[w * 8 + c], O);
-    if (n_chunks_b == 1) {
+    if (p.cluster) {
+      wres0[16 + c * OS + d] = O;  // in place: only this thread reads or writes element (c, d)
+    } else if (n_chunks_b == 1) {
       store_out(p.out, col_oo[c] + d, O * cf[kWarps * 8 + 16 + c], p.out_dtype);
     } else {
       float* slot = p.ws + col_wo[c];
@@ -741,6 +749,62 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       }
     }
   }
+  if (!p.cluster) return;
+
+  // ------------------------------------------------------------------ cluster merge
+  // The max_chunks CTAs of this column group form one cluster; each holds its chunk's
+  // (M, L) in cf and its O in warp 0's result area.  Threads 0..7 turn the cluster's (M, L)
+  // of one column into per-chunk weights and the output factor; then the cluster's CTAs
+  // each write an interleaved share of the output elements, reading the chunks' O through
+  // distributed shared memory.  The second barrier keeps every CTA (and its shared memory)
+  // alive until all peers are done reading it.
+  cluster_sync_all();
+  const int nc = p.max_chunks;
+  float* cw = reinterpret_cast<float*>(smem + LY::RING);  // warp 1's ring: [8][kMaxCluster] weights, [8] factors
+  if (tid < 8) {
+    const int c = tid;
+    const uint32_t m_loc = smem_u32(cf + kWarps * 8 + c), l_loc = smem_u32(cf + kWarps * 8 + 8 + c);
+    float mj[kMaxCluster], lj[kMaxCluster];
+#pragma unroll
+    for (int j = 0; j < kMaxCluster; ++j) {
+      mj[j] = j < nc ? ld_dsmem_f32(dsmem_addr(m_loc, j)) : -INFINITY;
+      lj[j] = j < nc ? ld_dsmem_f32(dsmem_addr(l_loc, j)) : 0.0f;
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kMaxCluster; ++j) M = fmaxf(M, mj[j]);
+    float L = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxCluster; ++j) {
+      const float w = mj[j] == -INFINITY ? 0.0f : ex2(mj[j] - M);
+      cw[c * kMaxCluster + j] = w;
+      L = fmaf(lj[j], w, L);
+    }
+    const bool sink = p.sinks != nullptr;
+    cw[8 * kMaxCluster + c] =
+        softmax_out_factor(M, L, sink, sink ? p.sinks[col_i[c * 4 + 0]] * 1.4426950408889634f : 0.0f);
+  }
+  __syncthreads();
+  const int cols = min(8, rph - rg * 8);  // valid columns are 0 .. cols-1
+  const uint32_t o_loc = smem_u32(wres0 + 16);
+  for (int i = chunk * 128 + tid; i < cols * DV; i += nc * 128) {
+    const int c = i / DV, d = i % DV;
+    const uint32_t a = o_loc + (c * OS + d) * 4;
+    const float* wc = cw + c * kMaxCluster;
+    float O = 0.0f;
+#pragma unroll
+    for (int j0 = 0; j0 < kMaxCluster; j0 += 8) {
+      if (j0 >= nc) break;
+      float x[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        x[j] = (j0 + j < nc && wc[j0 + j] != 0.0f) ? ld_dsmem_f32(dsmem_addr(a, j0 + j)) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) O = fmaf(x[j], wc[j0 + j], O);
+    }
+    store_out(p.out, col_oo[c] + d, O * cw[8 * kMaxCluster + c], p.out_dtype);
+  }
+  cluster_sync_all();
 }
 
 // Merge the per-chunk partials of sequences split into more than one chunk.  One warp per
@@ -788,11 +852,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
       m = mn;
     }
   }
-  const int hq = row / p.q_len, lq = row % p.q_len;
   const float M = m;
-  const bool sink = p.sinks != nullptr;
-  const float inv_l = softmax_out_factor(m, l, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
-
   float4 acc[PER];
 #pragma unroll
   for (int k = 0; k < PER; ++k) acc[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -801,23 +861,34 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
     const float mc = c0 == 0 ? m_first : (c < nc ? base[(int64_t)c * PF] : -INFINITY);
     const float w = (c < nc && mc != -INFINITY) ? ex2(mc - M) : 0.0f;
     const int cnt = min(32, nc - c0);
-#pragma unroll 8
-    for (int j = 0; j < cnt; ++j) {
-      const float wj = __shfl_sync(0xffffffffu, w, j);
-      const float4* src = reinterpret_cast<const float4*>(base + (int64_t)(c0 + j) * PF + kPartialHead);
+    // eight chunks' slices are loaded before any is used, so their latencies overlap
+    for (int j0 = 0; j0 < cnt; j0 += 8) {
+      float4 x[8][PER];
 #pragma unroll
-      for (int k = 0; k < PER; ++k) {
-        const int v = lane + 32 * k;
-        if (V4 % 32 == 0 || v < V4) {
-          const float4 x = src[v];
-          acc[k].x = fmaf(x.x, wj, acc[k].x);
-          acc[k].y = fmaf(x.y, wj, acc[k].y);
-          acc[k].z = fmaf(x.z, wj, acc[k].z);
-          acc[k].w = fmaf(x.w, wj, acc[k].w);
+      for (int u = 0; u < 8; ++u) {
+        const float4* src = reinterpret_cast<const float4*>(base + (int64_t)(c0 + j0 + u) * PF + kPartialHead);
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+          const int v = lane + 32 * k;
+          x[u][k] = (j0 + u < cnt && (V4 % 32 == 0 || v < V4)) ? src[v] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float wj = __shfl_sync(0xffffffffu, w, (j0 + u) & 31);
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+          acc[k].x = fmaf(x[u][k].x, wj, acc[k].x);
+          acc[k].y = fmaf(x[u][k].y, wj, acc[k].y);
+          acc[k].z = fmaf(x[u][k].z, wj, acc[k].z);
+          acc[k].w = fmaf(x[u][k].w, wj, acc[k].w);
         }
       }
     }
   }
+  const int hq = row / p.q_len, lq = row % p.q_len;
+  const bool sink = p.sinks != nullptr;
+  const float inv_l = softmax_out_factor(m, l, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
   const int64_t o0 = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)lq * p.osl;
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
@@ -842,10 +913,17 @@ bool decode_supported(int k_dim, int v_dim) {
 // Split size (tokens per CTA chunk) for a decode call.  With fewer (sequence, KV head, row
 // group) pairs than CTA slots on the device, each pair is split into chunks; the split is
 // chosen by a small cost model: waves of CTAs x (fixed per-CTA cost + chunk tokens), where
-// the fixed cost (prologue, pipeline fill, CTA merge) is worth ~256 streamed tokens.  With
-// at least a full wave of pairs, chunks are as long as allowed (fewer partials to merge).
-void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_per_sm, int* chunk,
-                 int* n_chunks) {
+// the fixed cost (prologue, pipeline fill, CTA merge) is worth ~256 streamed tokens, plus
+// the merge of split chunks.  With at least a full wave of pairs, chunks are as long as
+// allowed (fewer partials to merge).
+//
+// Split chunks merge either through the workspace and a second launch (combine_kernel,
+// ~320 tokens' worth of latency) or, when every column's chunks form one thread-block
+// cluster and all clusters are resident at once, inside the cluster (*cluster = 1: ~64
+// tokens' worth, no workspace).  Cluster CTAs are held until the whole cluster is done,
+// so a grid of several waves keeps the workspace merge.
+void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_per_sm, int k_dim,
+                 int v_dim, int* chunk, int* n_chunks, int* cluster) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
@@ -860,47 +938,73 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_p
     c = (c + 63) / 64 * 64;
     return c < 128 ? (int64_t)128 : (c > kMaxChunk ? (int64_t)kMaxChunk : c);
   };
+  constexpr int64_t kFixed = 256, kCombine = 320, kClusterMerge = 64;
+  const int max_cluster = pairs < slots ? decode_max_cluster(k_dim, v_dim) : 0;
+  // cluster merge possible for nch chunks per column: all pairs' clusters resident at once
+  auto cluster_ok = [&](int64_t nch) {
+    return nch >= 2 && nch <= max_cluster && pairs <= decode_active_clusters(k_dim, v_dim, (int)nch);
+  };
   int64_t best_c = chunk_for(1);
+  bool best_cluster = false;
   if (pairs < slots) {
-    constexpr int64_t kFixed = 256;
     int64_t best_cost = -1;
     const int64_t max_split = (4 * slots + pairs - 1) / pairs;
     for (int64_t n = 1; n <= max_split; ++n) {
       const int64_t c = chunk_for(n);
-      const int64_t ctas = pairs * ((sp + c - 1) / c);
-      const int64_t cost = ((ctas + slots - 1) / slots) * (kFixed + c);
+      const int64_t nch = (sp + c - 1) / c;
+      const int64_t ctas = pairs * nch;
+      int64_t cost = ((ctas + slots - 1) / slots) * (kFixed + c) + (nch > 1 ? kCombine : 0);
+      bool cl = false;
+      if (cluster_ok(nch) && kFixed + c + kClusterMerge < cost) {
+        cost = kFixed + c + kClusterMerge;
+        cl = true;
+      }
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
         best_c = c;
+        best_cluster = cl;
       }
     }
   }
   *chunk = static_cast<int>(best_c);
   *n_chunks = static_cast<int>((sp + best_c - 1) / best_c);
   if (*n_chunks < 1) *n_chunks = 1;
+  *cluster = (best_cluster && *n_chunks >= 2) ? 1 : 0;
 }
 
 // Launch with programmatic stream serialization: the grid may become resident while the
 // previous kernel in the stream finishes (it waits in griddep_wait() before touching
 // memory).  Streams or drivers that refuse the attribute get a plain launch.
+// cluster_x > 1 launches thread-block clusters of (cluster_x, 1, 1) CTAs.
 template <typename... Args>
 static cudaError_t launch_pdl(void (*kfn)(Args...), dim3 grid, dim3 block, size_t smem,
-                              cudaStream_t stream, const DecodeParams& p) {
+                              cudaStream_t stream, const DecodeParams& p, int cluster_x = 1) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x > 1 ? cluster_x : 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  const bool clustered = cluster_x > 1;
+  cfg.attrs = clustered ? attr : attr + 1;
+  cfg.numAttrs = clustered ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, p);
   if (e == cudaErrorNotSupported || e == cudaErrorInvalidValue) {
     (void)cudaGetLastError();
-    kfn<<<grid, block, smem, stream>>>(p);
-    e = cudaGetLastError();
+    if (clustered) {
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      e = cudaLaunchKernelEx(&cfg, kfn, p);
+    } else {
+      kfn<<<grid, block, smem, stream>>>(p);
+      e = cudaGetLastError();
+    }
   }
   return e;
 }
@@ -929,16 +1033,36 @@ struct DecodeCfg {
   using LY = DecodeLayout<DK, DV, NS, TS>;
 };
 
+// Clusters of more than 8 CTAs are opt-in per kernel (and per device).
+template <typename F>
+static cudaError_t allow_large_clusters_once(F kfn, unsigned long long* done_mask) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit != 0 && (__atomic_load_n(done_mask, __ATOMIC_ACQUIRE) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess && bit != 0) __atomic_fetch_or(done_mask, bit, __ATOMIC_RELEASE);
+  return e;
+}
+
 template <int DK, int DV, bool SBF16, bool PAGED>
 static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_groups,
                                    cudaStream_t stream) {
   using CF = DecodeCfg<DK, DV>;
   using LY = typename CF::LY;
   auto kfn = decode_kernel<DK, DV, SBF16, PAGED, CF::NS, CF::TS>;
-  static unsigned long long smem_done = 0;
+  static unsigned long long smem_done = 0, cluster_done = 0;
   cudaError_t e = set_smem_once(kfn, LY::SMEM, &smem_done);
   if (e != cudaSuccess) return e;
   dim3 grid(p.max_chunks, p.hkv * row_groups, batch);
+  if (p.cluster) {
+    if (p.max_chunks > 8) {
+      e = allow_large_clusters_once(kfn, &cluster_done);
+      if (e != cudaSuccess) return e;
+    }
+    return launch_pdl(kfn, grid, dim3(128), LY::SMEM, stream, p, p.max_chunks);
+  }
   e = launch_pdl(kfn, grid, dim3(128), LY::SMEM, stream, p);
   if (e != cudaSuccess) return e;
   if (p.max_chunks > 1) {
@@ -986,6 +1110,75 @@ int decode_ctas_per_sm(int k_dim, int v_dim) {
 }
 
 int decode_stage_tokens(int k_dim, int v_dim) { return k_dim + v_dim <= 256 ? 64 : 32; }
+
+// Resident clusters of `size` decode CTAs (2 .. kMaxCluster) for a head-dim pair on the
+// current device, cached per device and size; 0 when such a cluster cannot be scheduled.
+template <int DK, int DV>
+static int active_clusters_t(int size) {
+  using CF = DecodeCfg<DK, DV>;
+  static int cache[64][kMaxCluster + 1] = {};  // 0: not queried, -1: none
+  if (size < 2 || size > kMaxCluster) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  if (dev >= 0 && dev < 64) {
+    const int v = __atomic_load_n(&cache[dev][size], __ATOMIC_ACQUIRE);
+    if (v != 0) return v > 0 ? v : 0;
+  }
+  auto kfn = decode_kernel<DK, DV, false, true, CF::NS, CF::TS>;
+  static unsigned long long smem_done = 0, cluster_done = 0;
+  int n = 0;
+  bool ok = set_smem_once(kfn, CF::LY::SMEM, &smem_done) == cudaSuccess &&
+            (size <= 8 || allow_large_clusters_once(kfn, &cluster_done) == cudaSuccess);
+  if (ok) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(size, 1, 1);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = CF::LY::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ok = cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) == cudaSuccess;
+  }
+  (void)cudaGetLastError();
+  if (!ok || n < 1) n = -1;
+  if (dev >= 0 && dev < 64) __atomic_store_n(&cache[dev][size], n, __ATOMIC_RELEASE);
+  return n > 0 ? n : 0;
+}
+
+int decode_active_clusters(int k_dim, int v_dim, int size) {
+  if (k_dim == 64 && v_dim == 64) return active_clusters_t<64, 64>(size);
+  if (k_dim == 128 && v_dim == 128) return active_clusters_t<128, 128>(size);
+  if (k_dim == 128 && v_dim == 64) return active_clusters_t<128, 64>(size);
+  if (k_dim == 192 && v_dim == 128) return active_clusters_t<192, 128>(size);
+  if (k_dim == 256 && v_dim == 256) return active_clusters_t<256, 256>(size);
+  return 0;
+}
+
+// Largest cluster of decode CTAs (up to kMaxCluster) that the device can schedule for a
+// head-dim pair; 0 when clusters are unavailable.  AM_Q4_DECODE_MAX_CLUSTER (read on every
+// call) lowers the cap: 0 or 1 turns cluster merging off, so split chunks go through the
+// workspace and combine_kernel.
+int decode_max_cluster(int k_dim, int v_dim) {
+  int m = 0;
+  for (int size : {kMaxCluster, 8, 4, 2}) {
+    if (decode_active_clusters(k_dim, v_dim, size) > 0) {
+      m = size;
+      break;
+    }
+  }
+  if (const char* env = getenv("AM_Q4_DECODE_MAX_CLUSTER")) {
+    const int cap = atoi(env);
+    if (cap < m) m = cap < 2 ? 0 : cap;
+  }
+  return m;
+}
 
 template <int DK, int DV>
 static cudaError_t launch_decode_d(const DecodeParams& p, int batch, int row_groups, bool paged,

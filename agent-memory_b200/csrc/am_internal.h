@@ -32,9 +32,15 @@ bool prefill_supported(int k_dim, int v_dim);
 cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16,
                            cudaStream_t stream);
 
-// Split size (tokens per CTA chunk) and number of chunks for a decode call.
-void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_per_sm, int* chunk,
-                 int* n_chunks);
+// Split size (tokens per CTA chunk), number of chunks and merge mode (1: in-cluster merge)
+// for a decode call.
+void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_per_sm, int k_dim,
+                 int v_dim, int* chunk, int* n_chunks, int* cluster);
+// Largest decode cluster (chunks merged in one thread-block cluster) for a head-dim pair
+// on the current device; 0 when cluster merging is unavailable or turned off.
+int decode_max_cluster(int k_dim, int v_dim);
+// Clusters of `size` decode CTAs that can be resident at once (0: not schedulable).
+int decode_active_clusters(int k_dim, int v_dim, int size);
 // Resident decode CTAs per SM on the current device for a (k_dim, v_dim) pair.
 int decode_ctas_per_sm(int k_dim, int v_dim);
 

@@ -294,6 +294,19 @@ def _mask_args(args: AttnArgs, mask: torch.Tensor | None, keep: list) -> None:
     (args.mask_stride_b, args.mask_stride_h, args.mask_stride_l, args.mask_stride_n) = strides
 
 
+def decode_workspace_bytes(view: CacheView, batch: int, n_q_heads: int, q_len: int,
+                           max_kv_len: int, *, window: int = 0) -> int:
+    """Workspace bytes a decode call of this shape needs for split-KV partials: 0 when it
+    runs as one launch (a single chunk per sequence, or chunks merged inside a thread-block
+    cluster), else the partials that the second launch (the combine kernel) merges."""
+    a = AttnArgs()
+    a.batch, a.n_q_heads, a.q_len = int(batch), int(n_q_heads), int(q_len)
+    a.max_kv_len = int(max_kv_len)
+    a.window = int(window or 0)
+    a.scale = 1.0
+    return int(_lib.load().am_q4_attention_workspace_bytes(ctypes.byref(view.desc), ctypes.byref(a)))
+
+
 def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torch.Tensor,
               max_kv_len: int, *, kv_start: torch.Tensor | None = None, causal: bool = False,
               window: int = 0, mask: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,

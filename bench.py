@@ -304,7 +304,9 @@ def run_ours(args, rank, world, local_rank):
     tokens_per_step = args.agents if world > 1 or A == args.agents else A
     value = tokens_per_step / (ms_per_step / 1e3)
 
-    # roofline of the decode attention launch (split-KV kernel + its combine)
+    # roofline of the decode attention call (split-KV kernel, plus the combine kernel when
+    # split chunks are merged through the workspace instead of inside a cluster)
+    combine = am.kernels.decode_workspace_bytes(views[0], A, hq, 1, max_len) > 0
     per_tok = q4_bytes_per_token(hkv, dk, dv)
     launch_bytes = sum(n + 1 for n in lens) * per_tok + A * hq * (dk + dv) * 2
     avg_launch_s = float(np.mean(attn_ms)) / 1e3
@@ -373,7 +375,8 @@ def run_ours(args, rank, world, local_rank):
                        "step": "per layer: append 1 token/agent + split-KV decode",
                        "l2": "inputs larger than L2 (Q4 cache %.1f GB/rank)" % (pool.nbytes / 1e9),
                        "fill_s": round(t_fill, 1)},
-            "roofline": {"kernel": "am_q4_decode (decode_kernel + combine_kernel)",
+            "roofline": {"kernel": "am_q4_decode (decode_kernel%s)" % (
+                             " + combine_kernel" if combine else ", chunks merged in-cluster"),
                          "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "bytes_per_launch": int(launch_bytes),
@@ -383,7 +386,7 @@ def run_ours(args, rank, world, local_rank):
                                            "decode launch of the 32-agent case (664.7 MB for 655.4 MB "
                                            "algorithmic), scaled by the bytes this launch processes"},
             "e2e": e2e,
-            "gpu_launches": args.steps * layers * 3,
+            "gpu_launches": args.steps * layers * (3 if combine else 2),
             "clocks": clk,
             "cpu_baseline": cpu,
         }
@@ -464,6 +467,14 @@ def run_single_workload(args, am, dev, rank, world):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
     launch_ms = step_ms / inst  # graph nodes run back to back: mean time per attention call
+    # kernel launches per step: one per call, plus a combine launch for split decode calls
+    # whose chunks merge through the workspace
+    launches_per_step = 0
+    for i in range(inst):
+        launches_per_step += 1
+        if L == 1:
+            wl = 0 if (w != "gemma" or is_global[i % layers]) else window
+            launches_per_step += am.kernels.decode_workspace_bytes(views[i], B, hq, L, N, window=wl) > 0
     hbm, tf_burst, tf_sus, kind = peaks()
     per_tok = q4_bytes_per_token(hkv, dk, dv)
     if L == 1:
@@ -498,7 +509,7 @@ def run_single_workload(args, am, dev, rank, world):
                        "window": window, "parallelism": f"replicas x{world}",
                        "l2": f"{reps} rotating instances" if reps > 1 else "inputs larger than L2",
                        "timing": "whole step in one CUDA graph; per-call time = step / calls"},
-            "roofline": roof, "gpu_launches": args.steps * inst * (1 if L > 1 else 2),
+            "roofline": roof, "gpu_launches": args.steps * launches_per_step,
             "clocks": clk}))
 
 

@@ -47,6 +47,19 @@ def cuda():
     return torch.device("cuda:0")
 
 
+@pytest.fixture(params=["cluster", "workspace"])
+def merge_mode(request, monkeypatch):
+    """Split-KV decode merges the partials of a column's chunks either inside one
+    thread-block cluster (the default where the chunks fit one cluster) or through the
+    workspace and combine_kernel (AM_Q4_DECODE_MAX_CLUSTER=0); a test using this fixture
+    runs once with each."""
+    if request.param == "workspace":
+        monkeypatch.setenv("AM_Q4_DECODE_MAX_CLUSTER", "0")
+    else:
+        monkeypatch.delenv("AM_Q4_DECODE_MAX_CLUSTER", raising=False)
+    return request.param
+
+
 def assert_close(got, want, atol=2e-3, rtol=1e-3, what=""):
     """The attention tolerance: |got - want| <= atol + rtol * |want| elementwise."""
     got = np.asarray(got, dtype=np.float64)

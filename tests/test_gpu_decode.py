@@ -7,13 +7,16 @@ K192/V128 (n_rep 1), asymmetric K128/V64, D64; masks (none, causal string, boole
 additive, structured left padding / window), bf16, paged vs contiguous, B=1 vs B=2.
 """
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
 
 from conftest import assert_close, pkg
 
-pytestmark = pytest.mark.gpu
+# every case runs with both merges of split chunks (conftest.merge_mode)
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("merge_mode")]
 
 F16, BF16 = 0, 1
 
@@ -47,6 +50,7 @@ GEOMS = [
     (2, 8, 4, 333, 128, 64),      # asymmetric K/V
     (1, 4, 1, 100, 64, 64),       # small head dim, n_rep 4
     (2, 12, 4, 5, 128, 128),      # N < one tile
+    (1, 4, 1, 40000, 64, 64),     # more than 16 chunks of 2048: always workspace + combine
 ]
 
 
@@ -214,3 +218,19 @@ def test_unsupported_dims_raise(cuda):
     q, kq, vq = make_case(1, 2, 1, 20, 320, 320, cuda=cuda)
     with pytest.raises(pkg.Q4KernelError):
         pkg.quantized_scaled_dot_product_attention(q.to(cuda), kq, vq, 0.1, None)
+
+
+def test_cluster_merge_needs_no_workspace(cuda, merge_mode):
+    """Split chunks that fit one cluster merge there (no workspace); with cluster merging
+    turned off the same call needs a workspace for its partials."""
+    L_ = pkg._lib.load()
+    q, kq, vq = make_case(2, 32, 8, 2048, 128, 128, cuda=cuda, seed=1)
+    view, _ = pkg.kernels.contiguous_view(kq, vq)
+    a = pkg._lib.AttnArgs()
+    a.batch, a.n_q_heads, a.q_len, a.max_kv_len = 2, 32, 1, 2048
+    a.scale = 128 ** -0.5
+    ws = L_.am_q4_attention_workspace_bytes(ctypes.byref(view.desc), ctypes.byref(a))
+    if merge_mode == "cluster":
+        assert ws == 0
+    else:
+        assert ws > 0

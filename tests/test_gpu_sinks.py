@@ -16,7 +16,7 @@ import torch
 
 from conftest import assert_close, pkg
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("merge_mode")]
 
 GOLDEN = Path(__file__).parent / "golden"
 F16 = 0
