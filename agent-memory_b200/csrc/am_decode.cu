@@ -3,10 +3,11 @@
 // One CTA = (KV split "chunk", KV head, row group, sequence).  A row group is up to 8
 // query rows of one KV head (the n_rep GQA heads times the query positions), so every
 // Q4 byte of the chunk is read once for all of them.  4 warps per CTA; each warp streams
-// 16-token tiles (tiles w, w+4, ...) through a private cp.async ring of NS stages and
-// keeps its own online-softmax state; the 4 warp states are merged through shared
-// memory and either written as the final output (single chunk) or as a partial
-// (m, l, O) that combine_kernel merges across chunks.
+// stages of TS tokens (stages w, w+4, ...) through a private ring of NS stages filled by
+// 1-D bulk copies, and keeps its own online-softmax state; the 4 warp states are merged
+// through shared memory and written as the final output (single chunk), merged with the
+// other chunks of the column inside a thread-block cluster through distributed shared
+// memory, or written as a partial (m, l, O) that combine_kernel merges across chunks.
 //
 // Tensor-core use (mma.sync m16n8k16, fp16 in / fp32 accumulate), HBM-bound design:
 //  * S = K . Q^T with K as the A operand (16 tokens x 16 dims) and the 8 query rows as N.

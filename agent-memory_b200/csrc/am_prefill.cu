@@ -2,22 +2,24 @@
 //
 // One CTA = 128 query rows of one KV head of one sequence.  Rows are (token, GQA head)
 // pairs, token-major: 128 / n_rep query tokens times the n_rep heads that share the KV
-// head, so each dequantized K/V tile feeds all of them.  256 threads, warp-specialised:
-//   * producer warps 4-7 dequantize the Q4 K and V rows of 128-key tile j (one token per
-//     thread, raw rows prefetched one tile ahead; fp16 FMA dequantisation) into fp16
-//     operand tiles in shared memory (128-byte swizzle; K K-major, V MN-major; two
+// head, so each dequantized K/V tile feeds all of them.  384 threads, warp-specialised:
+//   * producer warps 8-11 dequantize the Q4 K and V rows of 128-key tile j (one token per
+//     thread, raw rows prefetched one tile ahead; fp16 magic-number dequantisation) into
+//     fp16 operand tiles in shared memory (128-byte swizzle; K K-major, V MN-major; two
 //     buffers), then one producer thread issues S_j = Q . K_j^T (tcgen05.mma kind::f16,
 //     M=128, N=128, K=16 steps) into TMEM S[j%2];
-//   * softmax warps 0-3 own TMEM lanes 0-127 (one query row per thread): tcgen05.ld of
-//     their S row, fp32 online softmax, P (fp16, K-major) into shared memory, the previous
-//     tile's O row folded into fp32 registers with the running-max correction; then one
-//     softmax thread issues O_j = P_j . V_j into TMEM O[j%2].
-// mbarriers (MMA commits and 128-thread arrivals) chain the stages so the dequantisation
-// of tile j+1, the MMAs of tile j and the softmax of tile j overlap.  TMEM: S x2 + O x2
-// (512 columns, one CTA per SM).  Operands are fp16 for every query dtype: bf16 queries
-// are rescaled per row by a power of two so the conversion is exact.  Every mbarrier
-// wait is bounded (2 s of %globaltimer); on timeout the kernel flags AM_STATUS_TIMEOUT,
-// stops issuing work, frees its TMEM and returns.
+//   * softmax warps 0-7: warp w owns TMEM lanes 32(w%4) .. +31 (one query row per thread)
+//     and key columns 64(w/4) .. +63 of each tile; tcgen05.ld of its half row, row maxima
+//     exchanged with the partner warp through shared memory, fp32 online softmax, P (fp16,
+//     K-major) into shared memory; O rows rescaled in TMEM only when the running max moves
+//     by more than 2^8.  Once all 256 softmax threads have written P (an mbarrier), lane 0
+//     of warp 0 issues O += P_j . V_j into TMEM O (accumulating after the first tile).
+// mbarriers (MMA commits and thread arrivals) chain the stages so the dequantisation of
+// tile j+1, the MMAs of tile j and the softmax of tile j overlap.  TMEM: S x2 + O (512
+// columns, one CTA per SM).  Operands are fp16 for every query dtype: bf16 queries are
+// rescaled per row by a power of two so the conversion is exact.  Every mbarrier wait is
+// bounded (2 s of %globaltimer); on timeout the kernel flags AM_STATUS_TIMEOUT, stops
+// issuing work, frees its TMEM and returns.
 //
 // Reference semantics: the compiled quantized SDPA (mlx_fused_attention.py:69-139) as
 // used by chunked prefill (batch_engine.py:339-456): the chunk's own K/V are already in
