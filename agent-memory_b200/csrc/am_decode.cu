@@ -37,7 +37,8 @@
 namespace am {
 
 constexpr int kWarps = 4;
-constexpr int kMaxChunk = 2048;            // tokens per CTA chunk (decode_plan never exceeds it)
+constexpr int kMaxChunk = 8192;            // tokens per CTA chunk (decode_plan never exceeds it)
+constexpr int kMaxSplitChunk = 4096;       // chunk cap when the planner splits for parallelism
 constexpr int kMaxCluster = 16;            // chunks merged inside one thread-block cluster
 constexpr int kMaxBlk = kMaxChunk / 32 + 2;  // block ids a chunk can touch (block_tokens >= 32)
 constexpr float kMaskedFinite = -1.0e30f;  // boolean-mask fill (finite: keeps uniform rows)
@@ -915,8 +916,9 @@ bool decode_supported(int k_dim, int v_dim) {
 // group) pairs than CTA slots on the device, each pair is split into chunks; the split is
 // chosen by a small cost model: waves of CTAs x (fixed per-CTA cost + chunk tokens), where
 // the fixed cost (prologue, pipeline fill, CTA merge) is worth ~256 streamed tokens, plus
-// the merge of split chunks.  With at least a full wave of pairs, chunks are as long as
-// allowed (fewer partials to merge).
+// the merge of split chunks, with chunks of at most 4096 tokens.  With at least a full
+// wave of pairs, chunks are as long as allowed (8192 tokens: fewer CTA prologues and
+// partials to merge; measured 8% faster than 2048-token chunks on 256 agents).
 //
 // Split chunks merge either through the workspace and a second launch (combine_kernel,
 // ~320 tokens' worth of latency) or, when every column's chunks form one thread-block
@@ -934,10 +936,10 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_p
   const int64_t pairs = (int64_t)batch * n_kv_heads * row_groups;
   const int64_t slots = (int64_t)sms * (ctas_per_sm > 0 ? ctas_per_sm : 1);
   const int64_t sp = span > 0 ? span : 1;
-  auto chunk_for = [&](int64_t n_split) {
+  auto chunk_for = [&](int64_t n_split, int64_t cap) {
     int64_t c = (sp + n_split - 1) / n_split;
     c = (c + 63) / 64 * 64;
-    return c < 128 ? (int64_t)128 : (c > kMaxChunk ? (int64_t)kMaxChunk : c);
+    return c < 128 ? (int64_t)128 : (c > cap ? cap : c);
   };
   constexpr int64_t kFixed = 256, kCombine = 320, kClusterMerge = 64;
   const int max_cluster = pairs < slots ? decode_max_cluster(k_dim, v_dim) : 0;
@@ -945,13 +947,13 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_p
   auto cluster_ok = [&](int64_t nch) {
     return nch >= 2 && nch <= max_cluster && pairs <= decode_active_clusters(k_dim, v_dim, (int)nch);
   };
-  int64_t best_c = chunk_for(1);
+  int64_t best_c = chunk_for(1, kMaxChunk);
   bool best_cluster = false;
   if (pairs < slots) {
     int64_t best_cost = -1;
     const int64_t max_split = (4 * slots + pairs - 1) / pairs;
     for (int64_t n = 1; n <= max_split; ++n) {
-      const int64_t c = chunk_for(n);
+      const int64_t c = chunk_for(n, kMaxSplitChunk);
       const int64_t nch = (sp + c - 1) / c;
       const int64_t ctas = pairs * nch;
       int64_t cost = ((ctas + slots - 1) / slots) * (kFixed + c) + (nch > 1 ? kCombine : 0);

@@ -50,7 +50,7 @@ GEOMS = [
     (2, 8, 4, 333, 128, 64),      # asymmetric K/V
     (1, 4, 1, 100, 64, 64),       # small head dim, n_rep 4
     (2, 12, 4, 5, 128, 128),      # N < one tile
-    (1, 4, 1, 40000, 64, 64),     # more than 16 chunks of 2048: always workspace + combine
+    (1, 4, 1, 40000, 64, 64),     # more chunks than one cluster holds: workspace + combine
 ]
 
 
