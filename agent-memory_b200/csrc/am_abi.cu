@@ -8,6 +8,10 @@
 #include <cstdio>
 #include <cstring>
 
+#include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
+
+#include <mutex>
+
 #include "am_common.cuh"
 #include "am_internal.h"
 
@@ -148,6 +152,49 @@ static int decode_geometry(const am_q4_cache* c, const am_attn_args* a, int* row
   decode_plan(a->batch, c->n_kv_heads, *row_groups, span, decode_ctas_per_sm(c->k_dim, c->v_dim),
               c->k_dim, c->v_dim, chunk, n_chunks, cluster);
   return rows;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against the
+// driver library); null when the driver does not provide it.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    } else {
+      (void)cudaGetLastError();
+    }
+  });
+  return fn;
+}
+
+// A 2-D map over a codes array seen as [rows, row_bytes] bytes, box = box_rows rows, swizzled
+// by the row size (32, 64 or 128 bytes), rows past the array read as zeros.
+static bool encode_codes_map(CUtensorMap* m, const void* base, int64_t rows, int row_bytes,
+                             int box_rows) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (enc == nullptr) return false;
+  const CUtensorMapSwizzle sw = row_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_32B;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(row_bytes), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t elem[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Decode kernels with 32-, 64- or 128-byte code rows (k_dim, v_dim in {64, 128, 256}) read
+// K and V codes through swizzled tensor maps.
+static bool decode_uses_tensor_maps(int k_dim, int v_dim) {
+  auto ok = [](int d) { return d == 64 || d == 128 || d == 256; };
+  return ok(k_dim) && ok(v_dim);
 }
 
 static void fill_params(DecodeParams& p, const am_q4_cache* cache, const am_attn_args* a) {
@@ -354,6 +401,23 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
   p.stage_tokens = decode_stage_tokens(cache->k_dim, cache->v_dim);
   p.ws = static_cast<float*>(workspace);
   p.cluster = cluster;
+  if (decode_uses_tensor_maps(cache->k_dim, cache->v_dim)) {
+    const int64_t rows = cache->layout == AM_LAYOUT_PAGED
+                             ? cache->capacity * cache->n_kv_heads * cache->block_tokens
+                             : static_cast<int64_t>(cache->batch) * cache->n_kv_heads * cache->capacity;
+    if (rows <= 0 || rows > INT_MAX) {
+      set_error("am_q4_decode: %lld code rows (sequences x KV heads x tokens) outside (0, 2^31)",
+                static_cast<long long>(rows));
+      return AM_ERR_UNSUPPORTED;
+    }
+    if (!aligned(cache->k_codes, 16) || !aligned(cache->v_codes, 16) ||
+        !encode_codes_map(&p.tmap_kc, cache->k_codes, rows, cache->k_dim / 2, stage) ||
+        !encode_codes_map(&p.tmap_vc, cache->v_codes, rows, cache->v_dim / 2, stage)) {
+      set_error("am_q4_decode: cannot describe the K/V codes as tensor maps (16-byte aligned "
+                "code arrays and a driver with cuTensorMapEncodeTiled are required)");
+      return AM_ERR_CUDA;
+    }
+  }
   return cuda_status(launch_decode(p, a->batch, row_groups, cache->layout == AM_LAYOUT_PAGED,
                                    cache->scale_dtype == AM_DTYPE_BF16,
                                    static_cast<cudaStream_t>(stream)),

@@ -3,6 +3,7 @@
 // ex2.approx, and in the prefill kernel tcgen05.* / mbarrier.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the type only; maps are encoded through the runtime's driver entry point)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -146,6 +147,31 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
           smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
+}
+
+// 2-D tiled TMA load (no multicast) of the box at (x, y) of `map` into shared memory,
+// completing on mbarrier `bar`.  `map` must live in parameter, constant or global memory.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory address of byte `byte` of row `row` in a tile of ROWB-byte rows written by a
+// TMA load with the matching swizzle (ROWB = 32, 64, 128 <-> CU_TENSOR_MAP_SWIZZLE_32B, 64B,
+// 128B): the 16-byte chunk index is XORed with address bits 7.. of the row start, so rows
+// that share a chunk column land in different banks.  `base` is aligned to the pattern
+// period (256, 512 or 1024 bytes).
+template <int ROWB>
+__device__ __forceinline__ uint32_t swz_addr(uint32_t base, int row, int byte) {
+  static_assert(ROWB == 32 || ROWB == 64 || ROWB == 128, "swizzled rows are 32, 64 or 128 bytes");
+  constexpr int SH = ROWB == 128 ? 0 : (ROWB == 64 ? 1 : 2);  // rows per 128-byte line: 1, 2, 4
+  constexpr int MASK = ROWB == 128 ? 7 : (ROWB == 64 ? 3 : 1);
+  const int chunk = (byte >> 4) ^ ((row >> SH) & MASK);
+  return base + row * ROWB + (chunk << 4) + (byte & 15);
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -327,6 +353,10 @@ struct DecodeParams {
   const float* sinks;  // [hq] sink logits (scaled-score units) or nullptr
   int32_t cluster;     // 1: the max_chunks CTAs of a column are one thread-block cluster and
                        // merge their partials through distributed shared memory (no ws)
+  // Decode kernels whose code rows are 32, 64 or 128 bytes load K and V codes through these
+  // 2-D tensor maps ([rows, row bytes], box = one stage, swizzled to the row size).
+  alignas(64) CUtensorMap tmap_kc;
+  alignas(64) CUtensorMap tmap_vc;
 };
 
 // Visible key range of a sequence for the structured mask: keys outside [lo, hi) are

@@ -54,7 +54,14 @@ struct DecodeLayout {
   static constexpr int OFF_KB = OFF_KS + TS * NGK * 2;
   static constexpr int OFF_VS = OFF_KB + TS * NGK * 2;
   static constexpr int OFF_VB = OFF_VS + TS * NGV * 2;
-  static constexpr int STAGE = (OFF_VB + TS * NGV * 2 + 127) / 128 * 128;
+  // K and V code rows of 32, 64 or 128 bytes arrive by swizzled 2-D tensor loads; their
+  // tiles then start on 1024-byte boundaries (stages are multiples of 1024 bytes and the
+  // V tile offset TS * KROW is one too)
+  static constexpr bool SWZ = (KROW == 32 || KROW == 64 || KROW == 128) &&
+                              (VROW == 32 || VROW == 64 || VROW == 128);
+  static constexpr int STAGE_ALIGN = SWZ ? 1024 : 128;
+  static constexpr int STAGE = (OFF_VB + TS * NGV * 2 + STAGE_ALIGN - 1) / STAGE_ALIGN * STAGE_ALIGN;
+  static_assert(!SWZ || OFF_V % 1024 == 0, "swizzled V tiles start on a 1024-byte boundary");
   static constexpr int RING = NS * STAGE;
   static constexpr int OFF_BAR = kWarps * RING;
   static constexpr int OFF_OK = OFF_BAR + kWarps * NS * 8;
@@ -103,7 +110,7 @@ __device__ __forceinline__ float load_mask(const DecodeParams& p, int b, int hq,
 constexpr float kRescaleSlack = 3.0f;
 
 template <int DK, int DV, bool SBF16, bool PAGED, int NS, int TS>
-__global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ DecodeParams p) {
   using LY = DecodeLayout<DK, DV, NS, TS>;
   constexpr int NH = TS / 16;  // 16-token MMA tiles per stage
   constexpr int NGK = LY::NGK, NGV = LY::NGV;
@@ -112,10 +119,20 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
   constexpr int MT = DV / 16;
   constexpr bool V_LDSM = VROW <= 64;  // ldmatrix V tiles unless the rows are 128 bytes
 
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem[];
 
   griddep_launch_dependents();
   griddep_wait();  // everything this kernel reads or writes is ordered after the previous grid
+
+  if constexpr (LY::SWZ) {
+    // swizzled tensor loads need 1024-byte aligned tiles: refuse (every CTA alike, so no
+    // cluster peer is left waiting) rather than read a shifted pattern
+    if (smem_u32(smem) & 1023u) {
+      if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+        flag_status(p.status, AM_STATUS_BAD_POSITION);
+      return;
+    }
+  }
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -205,10 +222,17 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       mbar_arrive(bar);
       return;
     }
-    mbar_arrive_expect_tx(bar, nrows * (KROW + VROW + 4 * NGK + 4 * NGV));
     uint8_t* stg = ring + s * LY::STAGE;
-    bulk_g2s(stg, p.kc + row0 * LY::KW, nrows * KROW, bar);
-    bulk_g2s(stg + LY::OFF_V, p.vc + row0 * LY::VW, nrows * VROW, bar);
+    if constexpr (LY::SWZ) {
+      // codes: one swizzled box of TS rows each (rows past the array read as zeros)
+      mbar_arrive_expect_tx(bar, TS * (KROW + VROW) + nrows * (4 * NGK + 4 * NGV));
+      tma_load_2d(smem_u32(stg), &p.tmap_kc, 0, static_cast<int>(row0), bar);
+      tma_load_2d(smem_u32(stg + LY::OFF_V), &p.tmap_vc, 0, static_cast<int>(row0), bar);
+    } else {
+      mbar_arrive_expect_tx(bar, nrows * (KROW + VROW + 4 * NGK + 4 * NGV));
+      bulk_g2s(stg, p.kc + row0 * LY::KW, nrows * KROW, bar);
+      bulk_g2s(stg + LY::OFF_V, p.vc + row0 * LY::VW, nrows * VROW, bar);
+    }
     bulk_g2s(stg + LY::OFF_KS, p.ks + row0 * NGK, nrows * NGK * 2, bar);
     bulk_g2s(stg + LY::OFF_KB, p.kb + row0 * NGK, nrows * NGK * 2, bar);
     bulk_g2s(stg + LY::OFF_VS, p.vs + row0 * NGV, nrows * NGV * 2, bar);
@@ -415,8 +439,13 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
       uint2 wa[NH], wb[NH];
 #pragma unroll
       for (int hh = 0; hh < NH; ++hh) {
-        wa[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g) * KROW + G * 32 + t * 8);
-        wb[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g + 8) * KROW + G * 32 + t * 8);
+        if constexpr (LY::SWZ) {
+          wa[hh] = *reinterpret_cast<const uint2*>(stg + swz_addr<LY::SWZ ? KROW : 32>(0, hh * 16 + g, G * 32 + t * 8));
+          wb[hh] = *reinterpret_cast<const uint2*>(stg + swz_addr<LY::SWZ ? KROW : 32>(0, hh * 16 + g + 8, G * 32 + t * 8));
+        } else {
+          wa[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g) * KROW + G * 32 + t * 8);
+          wb[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g + 8) * KROW + G * 32 + t * 8);
+        }
       }
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -601,8 +630,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
         // V^T tiles by ldmatrix.trans: matrices (tokens 0-7 | 8-15) x (dims 0-31 | 32-63 of
         // group G); lane (g, t) gets the 4 codes of dims 4g..4g+3 of tokens 2t and 2t+1 in
         // one register, and nibble j of each half is MMA row g's operand for MMA j
-        const uint32_t vrow_addr = smem_u32(stg + LY::OFF_V) +
-                                   (hh * 16 + ((lane >> 4) << 3) + (lane & 7)) * VROW + ((lane >> 3) & 1) * 16;
+        const uint32_t vtile = smem_u32(stg + LY::OFF_V);
+        const int vrow = hh * 16 + ((lane >> 4) << 3) + (lane & 7);
+        const int vseg = ((lane >> 3) & 1) * 16;
 #pragma unroll
         for (int G = 0; G < NGV; ++G) {
           vbias[0][G] = fmaf(pr[0], bvc[0][0][G], fmaf(pr[2], bvc[1][0][G], vbias[0][G]));
@@ -610,7 +640,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
           const uint32_t bl = movmatrix_trans(bpk[0][G]);
           const uint32_t bh = movmatrix_trans(bpk[1][G]);
           uint32_t m0, m1, m2, m3;  // (tok 0-7, seg 0) (tok 0-7, seg 1) (tok 8-15, seg 0) (tok 8-15, seg 1)
-          ldsm_x4_trans(vrow_addr + G * 32, m0, m1, m2, m3);
+          const uint32_t va = LY::SWZ ? swz_addr<LY::SWZ ? VROW : 32>(vtile, vrow, G * 32 + vseg)
+                                      : vtile + vrow * VROW + G * 32 + vseg;
+          ldsm_x4_trans(va, m0, m1, m2, m3);
           const uint32_t h0 = m0 >> 8, h1 = m1 >> 8, h2 = m2 >> 8, h3 = m3 >> 8;
           mma_f16_16816(o[4 * G + 0], m0 & 0x000F000Fu, m1 & 0x000F000Fu, m2 & 0x000F000Fu,
                         m3 & 0x000F000Fu, bl, bh);
@@ -632,10 +664,20 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeParams p) {
           const uint32_t bl = movmatrix_trans(bpk[0][G]);
           const uint32_t bh = movmatrix_trans(bpk[1][G]);
           const int woff = (8 * G + g) * 4;
-          const uint32_t v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * VROW + woff);
-          const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * VROW + woff);
-          const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * VROW + woff);
-          const uint32_t v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * VROW + woff);
+          uint32_t v0, v1, v2, v3;
+          if constexpr (LY::SWZ) {
+            const uint8_t* vt = stg + LY::OFF_V;
+            constexpr int VR = LY::SWZ ? VROW : 32;
+            v0 = *reinterpret_cast<const uint32_t*>(vt + swz_addr<VR>(0, hh * 16 + 2 * t, woff));
+            v1 = *reinterpret_cast<const uint32_t*>(vt + swz_addr<VR>(0, hh * 16 + 2 * t + 1, woff));
+            v2 = *reinterpret_cast<const uint32_t*>(vt + swz_addr<VR>(0, hh * 16 + 2 * t + 8, woff));
+            v3 = *reinterpret_cast<const uint32_t*>(vt + swz_addr<VR>(0, hh * 16 + 2 * t + 9, woff));
+          } else {
+            v0 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t) * VROW + woff);
+            v1 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 1) * VROW + woff);
+            v2 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 8) * VROW + woff);
+            v3 = *reinterpret_cast<const uint32_t*>(vbase + (2 * t + 9) * VROW + woff);
+          }
 #pragma unroll
           for (int beta = 0; beta < 4; ++beta) {
             const uint32_t sel = beta | ((4 + beta) << 8);
