@@ -117,7 +117,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   constexpr int KROW = LY::KROW, VROW = LY::VROW;
   constexpr int KSTEPS = DK / 16;
   constexpr int MT = DV / 16;
-  constexpr bool V_LDSM = VROW <= 64;  // ldmatrix V tiles unless the rows are 128 bytes
+  // ldmatrix V tiles, except 128-byte rows without the swizzle (8 rows of a tile would share
+  // one bank group)
+  constexpr bool V_LDSM = VROW <= 64 || LY::SWZ;
 
   extern __shared__ __align__(1024) uint8_t smem[];
 
