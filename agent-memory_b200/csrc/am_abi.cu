@@ -172,29 +172,29 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// A 2-D map over a codes array seen as [rows, row_bytes] bytes, box = box_rows rows, swizzled
-// by the row size (32, 64 or 128 bytes), rows past the array read as zeros.
+// A 2-D map over a codes array seen as [rows, row_bytes] bytes; a box is box_bytes (32, 64
+// or 128) of box_rows rows, swizzled by the box width; rows past the array read as zeros.
 static bool encode_codes_map(CUtensorMap* m, const void* base, int64_t rows, int row_bytes,
-                             int box_rows) {
+                             int box_bytes, int box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (enc == nullptr) return false;
-  const CUtensorMapSwizzle sw = row_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
-                                : row_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+  const CUtensorMapSwizzle sw = box_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                                   : CU_TENSOR_MAP_SWIZZLE_32B;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(row_bytes), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t elem[2] = {1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
              CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Decode kernels with 32-, 64- or 128-byte code rows (k_dim, v_dim in {64, 128, 256}) read
-// K and V codes through swizzled tensor maps.
+// Decode kernels with 32-, 64- or 128-byte code rows (head dims 64, 128, 256; Dk = 192 as a
+// 64-byte plus a 32-byte box) read K and V codes through swizzled tensor maps.
 static bool decode_uses_tensor_maps(int k_dim, int v_dim) {
   auto ok = [](int d) { return d == 64 || d == 128 || d == 256; };
-  return ok(k_dim) && ok(v_dim);
+  return (ok(k_dim) || k_dim == 192) && ok(v_dim);
 }
 
 static void fill_params(DecodeParams& p, const am_q4_cache* cache, const am_attn_args* a) {
@@ -410,9 +410,12 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
                 static_cast<long long>(rows));
       return AM_ERR_UNSUPPORTED;
     }
+    const int krow = cache->k_dim / 2, vrow = cache->v_dim / 2;
+    const bool ksplit = krow == 96;
     if (!aligned(cache->k_codes, 16) || !aligned(cache->v_codes, 16) ||
-        !encode_codes_map(&p.tmap_kc, cache->k_codes, rows, cache->k_dim / 2, stage) ||
-        !encode_codes_map(&p.tmap_vc, cache->v_codes, rows, cache->v_dim / 2, stage)) {
+        !encode_codes_map(&p.tmap_kc, cache->k_codes, rows, krow, ksplit ? 64 : krow, stage) ||
+        (ksplit && !encode_codes_map(&p.tmap_kc2, cache->k_codes, rows, krow, 32, stage)) ||
+        !encode_codes_map(&p.tmap_vc, cache->v_codes, rows, vrow, vrow, stage)) {
       set_error("am_q4_decode: cannot describe the K/V codes as tensor maps (16-byte aligned "
                 "code arrays and a driver with cuTensorMapEncodeTiled are required)");
       return AM_ERR_CUDA;

@@ -355,8 +355,10 @@ struct DecodeParams {
                        // merge their partials through distributed shared memory (no ws)
   // Decode kernels whose code rows are 32, 64 or 128 bytes load K and V codes through these
   // 2-D tensor maps ([rows, row bytes], box = one stage, swizzled to the row size).
+  // (Dk = 192: tmap_kc holds bytes 0..63 of each 96-byte K row, tmap_kc2 bytes 64..95)
   alignas(64) CUtensorMap tmap_kc;
   alignas(64) CUtensorMap tmap_vc;
+  alignas(64) CUtensorMap tmap_kc2;
 };
 
 // Visible key range of a sequence for the structured mask: keys outside [lo, hi) are

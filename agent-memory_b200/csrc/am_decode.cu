@@ -57,8 +57,11 @@ struct DecodeLayout {
   // K and V code rows of 32, 64 or 128 bytes arrive by swizzled 2-D tensor loads; their
   // tiles then start on 1024-byte boundaries (stages are multiples of 1024 bytes and the
   // V tile offset TS * KROW is one too)
-  static constexpr bool SWZ = (KROW == 32 || KROW == 64 || KROW == 128) &&
+  // (96-byte K rows, Dk = 192, arrive as a 64-byte tile then a 32-byte tile of the same rows)
+  static constexpr bool KSPLIT = KROW == 96;
+  static constexpr bool SWZ = (KROW == 32 || KROW == 64 || KROW == 128 || KSPLIT) &&
                               (VROW == 32 || VROW == 64 || VROW == 128);
+  static constexpr int OFF_K2 = TS * 64;  // KSPLIT: the 32-byte tile of K bytes 64..95
   static constexpr int STAGE_ALIGN = SWZ ? 1024 : 128;
   static constexpr int STAGE = (OFF_VB + TS * NGV * 2 + STAGE_ALIGN - 1) / STAGE_ALIGN * STAGE_ALIGN;
   static_assert(!SWZ || OFF_V % 1024 == 0, "swizzled V tiles start on a 1024-byte boundary");
@@ -229,6 +232,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
       // codes: one swizzled box of TS rows each (rows past the array read as zeros)
       mbar_arrive_expect_tx(bar, TS * (KROW + VROW) + nrows * (4 * NGK + 4 * NGV));
       tma_load_2d(smem_u32(stg), &p.tmap_kc, 0, static_cast<int>(row0), bar);
+      if constexpr (LY::KSPLIT)
+        tma_load_2d(smem_u32(stg + LY::OFF_K2), &p.tmap_kc2, 64, static_cast<int>(row0), bar);
       tma_load_2d(smem_u32(stg + LY::OFF_V), &p.tmap_vc, 0, static_cast<int>(row0), bar);
     } else {
       mbar_arrive_expect_tx(bar, nrows * (KROW + VROW + 4 * NGK + 4 * NGV));
@@ -441,9 +446,18 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
       uint2 wa[NH], wb[NH];
 #pragma unroll
       for (int hh = 0; hh < NH; ++hh) {
-        if constexpr (LY::SWZ) {
-          wa[hh] = *reinterpret_cast<const uint2*>(stg + swz_addr<LY::SWZ ? KROW : 32>(0, hh * 16 + g, G * 32 + t * 8));
-          wb[hh] = *reinterpret_cast<const uint2*>(stg + swz_addr<LY::SWZ ? KROW : 32>(0, hh * 16 + g + 8, G * 32 + t * 8));
+        if constexpr (LY::KSPLIT) {
+          // bytes 0..63 in the 64-byte tile, 64..95 (group 2) in the 32-byte tile
+          if (G < 2) {
+            wa[hh] = *reinterpret_cast<const uint2*>(stg + swz_addr<64>(0, hh * 16 + g, G * 32 + t * 8));
+            wb[hh] = *reinterpret_cast<const uint2*>(stg + swz_addr<64>(0, hh * 16 + g + 8, G * 32 + t * 8));
+          } else {
+            wa[hh] = *reinterpret_cast<const uint2*>(stg + LY::OFF_K2 + swz_addr<32>(0, hh * 16 + g, t * 8));
+            wb[hh] = *reinterpret_cast<const uint2*>(stg + LY::OFF_K2 + swz_addr<32>(0, hh * 16 + g + 8, t * 8));
+          }
+        } else if constexpr (LY::SWZ) {
+          wa[hh] = *reinterpret_cast<const uint2*>(stg + swz_addr<(LY::SWZ && !LY::KSPLIT) ? KROW : 32>(0, hh * 16 + g, G * 32 + t * 8));
+          wb[hh] = *reinterpret_cast<const uint2*>(stg + swz_addr<(LY::SWZ && !LY::KSPLIT) ? KROW : 32>(0, hh * 16 + g + 8, G * 32 + t * 8));
         } else {
           wa[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g) * KROW + G * 32 + t * 8);
           wb[hh] = *reinterpret_cast<const uint2*>(stg + (hh * 16 + g + 8) * KROW + G * 32 + t * 8);
