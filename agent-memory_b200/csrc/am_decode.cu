@@ -355,9 +355,12 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   }
   __syncthreads();
 
-  // B fragments of Q for S = K . Q^T.  k-step s = 4G + 2j + e covers words 8G + 2t + j of
-  // column g's slots; nibbles (2e, 2e+4) feed k-slots 2t, 2t+1 and nibbles (2e+1, 2e+5)
-  // feed 2t+8, 2t+9 (pre-divided by 16).
+  // B fragments of Q for S = K . Q^T.  k-step s = 4G + 2j covers words 8G + 2t + j of
+  // column g's slots: nibbles (0, 4) feed k-slots 2t, 2t+1 and nibbles (1, 5) feed 2t+8,
+  // 2t+9 (pre-divided by 16).  k-step s + 1 takes bytes 1 and 3 of the words whole: slots
+  // 2t, 2t+1 see n2 + 16 n3 (and n6 + 16 n7) with q3 / 16 (q7 / 16), slots 2t+8, 2t+9 see
+  // n2 (n6) with q2 - q3 / 16 (q6 - q7 / 16), which sums to n2 q2 + n3 q3 and saves the
+  // shift and one mask per operand pair.
   uint32_t qf[KSTEPS][2];
   {
     const float pw = col_pw[g];
@@ -368,9 +371,15 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int s = 4 * G + 2 * j + e;
-          const int d8 = 8 * (8 * G + 2 * t + j) + 2 * e;
-          qf[s][0] = pack_half2(qget(g, d8) * pw, qget(g, d8 + 4) * pw);
-          qf[s][1] = pack_half2(qget(g, d8 + 1) * pw * 0.0625f, qget(g, d8 + 5) * pw * 0.0625f);
+          const int d8 = 8 * (8 * G + 2 * t + j);
+          if (e == 0) {
+            qf[s][0] = pack_half2(qget(g, d8) * pw, qget(g, d8 + 4) * pw);
+            qf[s][1] = pack_half2(qget(g, d8 + 1) * pw * 0.0625f, qget(g, d8 + 5) * pw * 0.0625f);
+          } else {
+            const float q3 = qget(g, d8 + 3) * pw * 0.0625f, q7 = qget(g, d8 + 7) * pw * 0.0625f;
+            qf[s][0] = pack_half2(q3, q7);
+            qf[s][1] = pack_half2(fmaf(qget(g, d8 + 2), pw, -q3), fmaf(qget(g, d8 + 6), pw, -q7));
+          }
         }
       }
     }
@@ -475,10 +484,11 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
         }
 #pragma unroll
         for (int hh = 0; hh < NH; ++hh) {
-          const uint32_t xa = (j ? wa[hh].y : wa[hh].x) >> 8;
-          const uint32_t xb = (j ? wb[hh].y : wb[hh].x) >> 8;
-          mma_f16_16816(acc[hh][G], xa & 0x000F000Fu, xb & 0x000F000Fu, xa & 0x00F000F0u,
-                        xb & 0x00F000F0u, qf[s0 + 1][0], qf[s0 + 1][1]);
+          // bytes 1 and 3 into the low bytes of the two halves: n2 + 16 n3, n6 + 16 n7
+          const uint32_t xa = __byte_perm(j ? wa[hh].y : wa[hh].x, 0u, 0x4341);
+          const uint32_t xb = __byte_perm(j ? wb[hh].y : wb[hh].x, 0u, 0x4341);
+          mma_f16_16816(acc[hh][G], xa, xb, xa & 0x000F000Fu, xb & 0x000F000Fu, qf[s0 + 1][0],
+                        qf[s0 + 1][1]);
         }
       }
     }
@@ -659,13 +669,16 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
           const uint32_t va = LY::SWZ ? swz_addr<LY::SWZ ? VROW : 32>(vtile, vrow, G * 32 + vseg)
                                       : vtile + vrow * VROW + G * 32 + vseg;
           ldsm_x4_trans(va, m0, m1, m2, m3);
-          const uint32_t h0 = m0 >> 8, h1 = m1 >> 8, h2 = m2 >> 8, h3 = m3 >> 8;
-          mma_f16_16816(o[4 * G + 0], m0 & 0x000F000Fu, m1 & 0x000F000Fu, m2 & 0x000F000Fu,
-                        m3 & 0x000F000Fu, bl, bh);
+          // MMA 0 takes byte 0 of each half whole (n0 + 16 n1), MMA 1 its high nibble (16 n1),
+          // MMA 2 byte 1 whole (n2 + 16 n3, moved down by a byte permute), MMA 3 its high
+          // nibble; the epilogue subtracts the odd accumulators from the even ones
+          const uint32_t h0 = __byte_perm(m0, 0u, 0x4341), h1 = __byte_perm(m1, 0u, 0x4341);
+          const uint32_t h2 = __byte_perm(m2, 0u, 0x4341), h3 = __byte_perm(m3, 0u, 0x4341);
+          mma_f16_16816(o[4 * G + 0], m0 & 0x00FF00FFu, m1 & 0x00FF00FFu, m2 & 0x00FF00FFu,
+                        m3 & 0x00FF00FFu, bl, bh);
           mma_f16_16816(o[4 * G + 1], m0 & 0x00F000F0u, m1 & 0x00F000F0u, m2 & 0x00F000F0u,
                         m3 & 0x00F000F0u, bl, bh);
-          mma_f16_16816(o[4 * G + 2], h0 & 0x000F000Fu, h1 & 0x000F000Fu, h2 & 0x000F000Fu,
-                        h3 & 0x000F000Fu, bl, bh);
+          mma_f16_16816(o[4 * G + 2], h0, h1, h2, h3, bl, bh);
           mma_f16_16816(o[4 * G + 3], h0 & 0x00F000F0u, h1 & 0x00F000F0u, h2 & 0x00F000F0u,
                         h3 & 0x00F000F0u, bl, bh);
         }
@@ -745,13 +758,17 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
     const int G = mt_i / 4, j = mt_i % 4;
     if constexpr (V_LDSM) {
       // tile 4G + j: row g is dim 64G + 4g + j, row g + 8 is dim 64G + 32 + 4g + j; odd j
-      // took the high nibble (code * 2^-20), even j the low one (code * 2^-24)
+      // hold the high nibble (code * 2^-20), even j the whole byte (low + 16 * high, so the
+      // odd neighbour is subtracted) in units of 2^-24
       const int d = 64 * G + 4 * g + j;
-      const float sc = (j & 1) ? 1048576.0f : 16777216.0f;
-      wo[(2 * t) * OS + d] = fmaf(o[mt_i][0], sc, vbias[0][G]);
-      wo[(2 * t + 1) * OS + d] = fmaf(o[mt_i][1], sc, vbias[1][G]);
-      wo[(2 * t) * OS + d + 32] = fmaf(o[mt_i][2], sc, vbias[0][G]);
-      wo[(2 * t + 1) * OS + d + 32] = fmaf(o[mt_i][3], sc, vbias[1][G]);
+      float ov[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        ov[e] = (j & 1) ? o[mt_i][e] * 1048576.0f : (o[mt_i][e] - o[mt_i + 1][e]) * 16777216.0f;
+      wo[(2 * t) * OS + d] = ov[0] + vbias[0][G];
+      wo[(2 * t + 1) * OS + d] = ov[1] + vbias[1][G];
+      wo[(2 * t) * OS + d + 32] = ov[2] + vbias[0][G];
+      wo[(2 * t + 1) * OS + d + 32] = ov[3] + vbias[1][G];
     } else {
       // tile 4G + j: rows g / g + 8 are dims 64G + 8g + 2j / +1 (low / high nibble)
       const int d = 64 * G + 8 * g + 2 * j;

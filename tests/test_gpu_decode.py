@@ -234,3 +234,22 @@ def test_cluster_merge_needs_no_workspace(cuda, merge_mode):
         assert ws == 0
     else:
         assert ws > 0
+
+
+def test_decode_full_chunks_accuracy(cuda, orc, merge_mode):
+    """Enough (sequence, KV head) pairs to fill the device, so every CTA streams a whole
+    8192-token chunk: the longest fp32 accumulation of the kernel (the V accumulators hold
+    whole code bytes and are separated by a subtraction at the end) stays within tolerance."""
+    B, Hq, Hkv, N, D = 64, 32, 8, 8192, 128
+    g = torch.Generator(device=cuda).manual_seed(11)
+    k = torch.randn(B, Hkv, N, D, generator=g, device=cuda, dtype=torch.float16)
+    v = torch.randn(B, Hkv, N, D, generator=g, device=cuda, dtype=torch.float16)
+    q = torch.randn(B, Hq, 1, D, generator=g, device=cuda, dtype=torch.float16)
+    kq, vq = pkg.quantize(k), pkg.quantize(v)
+    del k, v
+    got = pkg.quantized_scaled_dot_product_attention(q, kq, vq, D ** -0.5, None)
+    want = oracle(orc, q.cpu(), tuple(t.cpu() for t in kq), tuple(t.cpu() for t in vq), D ** -0.5,
+                  causal=False)
+    g32 = got.float().cpu().numpy()
+    print(f"8192-token chunks ({merge_mode}): max abs err {np.abs(g32 - want).max():.2e}")
+    assert_close(g32, want, what="8192-token chunks")
