@@ -253,3 +253,19 @@ def test_decode_full_chunks_accuracy(cuda, orc, merge_mode):
     g32 = got.float().cpu().numpy()
     print(f"8192-token chunks ({merge_mode}): max abs err {np.abs(g32 - want).max():.2e}")
     assert_close(g32, want, what="8192-token chunks")
+
+
+def test_pool_beyond_tensor_map_rows_is_refused(cuda):
+    """A pool descriptor claiming more than 2^31 code rows is refused before any launch (the
+    TMA coordinates of a row are 32-bit); nothing is read or written."""
+    pool = pkg.PagedQ4Pool(2, 128, 128, 4, 256, torch.float16, cuda)
+    table = torch.tensor([[0, 1]], dtype=torch.int32, device=cuda)
+    view = pool.view(table)
+    view.desc.capacity = (1 << 31) // (2 * 256) + 1  # num_blocks x heads x tokens > 2^31
+    q = torch.randn(1, 4, 1, 128, dtype=torch.float16, device=cuda)
+    out = torch.full((1, 4, 1, 128), 7.0, dtype=torch.float16, device=cuda)
+    with pytest.raises(pkg.Q4KernelError, match="code rows"):
+        pkg.kernels.attention(view, q, 0.1, torch.tensor([300], dtype=torch.int32, device=cuda), 300,
+                              out=out, mode="decode")
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all())
