@@ -15,7 +15,9 @@ function agent-memory installs into ``mlx_lm.models.base``
 
 All batch entries run in one launch (the reference splits the batch into B=1 calls,
 :185-207).  L <= 64 / n_rep goes to the split-KV decode kernel; longer query blocks go to
-the tcgen05 prefill kernel.  Accumulation is fp32.  group_size/bits other than 64/4 have
+the tcgen05 prefill kernel (head dims 64 and 128), or for head dims without a prefill
+instantiation (Gemma-3 D256, MLA K192/V128) to the decode kernel in slices of 64 / n_rep
+query positions.  Accumulation is fp32.  group_size/bits other than 64/4 have
 no kernel and raise (the reference would call the original MLX op, :164-173).
 """
 

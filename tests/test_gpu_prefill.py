@@ -98,3 +98,38 @@ def test_chunked_prefill_paged(cuda, orc):
                          tuple(_bits(t) for t in pool.v), D ** -0.5, sdtype=1, n_kv_heads=Hkv,
                          layout=1, block_table=table, kv_len=np.array(layer.lengths), causal=True)
     assert_close(got.float().cpu().numpy(), want, atol=4e-3, rtol=4e-3, what="paged chunked prefill")
+
+
+@pytest.mark.parametrize("geom", [(2, 16, 8, 256, 256, 100), (1, 16, 16, 192, 128, 80)],
+                         ids=["gemma_d256", "mla_k192_v128"])
+@pytest.mark.parametrize("window", [0, 96])
+def test_query_blocks_without_prefill_kernel(cuda, orc, geom, window):
+    """Query blocks of head dims without a tcgen05 prefill instantiation (Gemma-3 D256, MLA
+    K192/V128) run through the decode kernel in slices of 64 / n_rep positions, each at its
+    own cache positions (causal, sliding window, left padding)."""
+    B, Hq, Hkv, dk, dv, L = geom
+    P = 150
+    N = P + L
+    q, kq, vq = make_case(B, Hq, Hkv, N, dk, dv, L=L, cuda=cuda, seed=dk + L + window)
+    lp = torch.tensor([0, 7][:B])
+    view, _ = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q.to(cuda), dk ** -0.5, kv_len, N, causal=True, window=window,
+                                kv_start=lp.to(cuda), out_dtype=torch.float32)
+    want = oracle(orc, q, kq, vq, dk ** -0.5, causal=True, window=window, kv_start=lp.numpy())
+    assert_close(got.cpu().numpy(), want, what=f"decode slices {geom} window={window}")
+
+
+def test_query_blocks_without_prefill_kernel_dense_mask(cuda, orc):
+    """Non-causal query block with a boolean mask on a D256 cache: every slice sees all keys
+    and its own rows of the mask."""
+    B, Hq, Hkv, D, L, N = 1, 8, 4, 256, 70, 200
+    q, kq, vq = make_case(B, Hq, Hkv, N, D, D, L=L, cuda=cuda, seed=77)
+    g = torch.Generator().manual_seed(1)
+    keep = torch.rand(B, 1, L, N, generator=g) > 0.3
+    view, _ = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q.to(cuda), 0.06, kv_len, N, mask=keep.to(cuda),
+                                out_dtype=torch.float32)
+    want = oracle(orc, q, kq, vq, 0.06, causal=False, mask=keep.numpy(), mask_kind=1)
+    assert_close(got.cpu().numpy(), want, what="decode slices, dense mask")
