@@ -995,10 +995,11 @@ bool decode_supported(int k_dim, int v_dim) {
 // wave of pairs, chunks are as long as allowed (8192 tokens: fewer CTA prologues and
 // partials to merge; measured 8% faster than 2048-token chunks on 256 agents).
 //
-// Split chunks merge either through the workspace and a second launch (combine_kernel,
-// ~320 tokens' worth of latency) or, when every column's chunks form one thread-block
-// cluster and all clusters are resident at once, inside the cluster (*cluster = 1: ~64
-// tokens' worth, no workspace).  Cluster CTAs are held until the whole cluster is done,
+// A chunk is costed between its tokens and whole rounds of 4 stages (the CTA's warps
+// stream stages in parallel).  Split chunks merge either through the workspace and a
+// second launch (combine_kernel, ~320 tokens' worth of latency) or, when every column's
+// chunks form one thread-block cluster and all clusters are resident at once, inside the
+// cluster (*cluster = 1: ~64 tokens' worth plus 12 per chunk read, no workspace).  Cluster CTAs are held until the whole cluster is done,
 // so a grid of several waves keeps the workspace merge.
 void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_per_sm, int k_dim,
                  int v_dim, int* chunk, int* n_chunks, int* cluster) {
@@ -1016,7 +1017,14 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_p
     c = (c + 63) / 64 * 64;
     return c < 128 ? (int64_t)128 : (c > cap ? cap : c);
   };
-  constexpr int64_t kFixed = 256, kCombine = 320, kClusterMerge = 64;
+  constexpr int64_t kFixed = 256, kCombine = 320, kClusterMerge = 64, kClusterPerChunk = 12;
+  // the 4 warps of a CTA stream stages in parallel, so a partial round of 4 stages costs
+  // about half a round more than its tokens (measured: 2-stage chunks take most of a
+  // 4-stage chunk's time)
+  const int64_t round_tokens = (int64_t)kWarps * decode_stage_tokens(k_dim, v_dim);
+  auto chunk_cost = [&](int64_t c) {
+    return kFixed + (c + (c + round_tokens - 1) / round_tokens * round_tokens) / 2;
+  };
   const int max_cluster = pairs < slots ? decode_max_cluster(k_dim, v_dim) : 0;
   // cluster merge possible for nch chunks per column: all pairs' clusters resident at once
   auto cluster_ok = [&](int64_t nch) {
@@ -1031,10 +1039,12 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_p
       const int64_t c = chunk_for(n, kMaxSplitChunk);
       const int64_t nch = (sp + c - 1) / c;
       const int64_t ctas = pairs * nch;
-      int64_t cost = ((ctas + slots - 1) / slots) * (kFixed + c) + (nch > 1 ? kCombine : 0);
+      int64_t cost = ((ctas + slots - 1) / slots) * chunk_cost(c) + (nch > 1 ? kCombine : 0);
       bool cl = false;
-      if (cluster_ok(nch) && kFixed + c + kClusterMerge < cost) {
-        cost = kFixed + c + kClusterMerge;
+      // the in-cluster merge reads every chunk's partial: its cost grows with the cluster
+      const int64_t cl_cost = chunk_cost(c) + kClusterMerge + kClusterPerChunk * nch;
+      if (cluster_ok(nch) && cl_cost < cost) {
+        cost = cl_cost;
         cl = true;
       }
       if (best_cost < 0 || cost < best_cost) {
