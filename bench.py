@@ -535,11 +535,19 @@ def run_single_workload(args, am, dev, rank, world):
 # ------------------------------------------------------------------------------- CPU arm
 
 
-def cpu_baseline_multi_agent(args, lengths_all, layers, geo, budget_s=12.0, threads=None):
+def cpu_baseline_multi_agent(args, lengths_all, layers, geo, budget_s=12.0, threads=None,
+                             sampler=None):
     """Time the C oracle (OpenMP over agents x KV heads, all host threads) on a bounded
     sample of the workload: one layer of decode for a sample of agents held in a paged Q4
     pool (256-token blocks, random block order), repeated until the time budget is spent;
-    the rate is extrapolated by Q4 bytes to the full step (all agents, all layers)."""
+    the rate is extrapolated by Q4 bytes to the full step (all agents, all layers).
+    `sampler` (from cpu_sampler) reuses an already built sample."""
+    run = sampler or cpu_sampler(lengths_all, layers, geo, threads)
+    return run(budget_s)
+
+
+def cpu_sampler(lengths_all, layers, geo, threads=None):
+    """Build the CPU baseline's sample once; returns budget_s -> result dict."""
     from oracle import q4_oracle as orc
 
     orc.build()
@@ -567,22 +575,26 @@ def cpu_baseline_multi_agent(args, lengths_all, layers, geo, budget_s=12.0, thre
     del v
     q = rng.standard_normal((len(sample), hq, 1, dk), dtype=np.float32)
     kv_len = np.array(sample, np.int32)
-    done_s, reps = 0.0, 0
-    while done_s < budget_s or reps == 0:
-        t = time.perf_counter()
-        orc.attention(q, kq, vq, dk ** -0.5, n_kv_heads=hkv, layout=1, block_table=table,
-                      kv_len=kv_len, causal=False)
-        done_s += time.perf_counter() - t
-        reps += 1
-    done_bytes = sum(sample) * per_tok * reps
-    full_bytes = sum(n + 1 for n in lengths_all) * per_tok * layers
-    step_s = done_s * full_bytes / done_bytes
-    return {"value": round(len(lengths_all) / step_s, 3), "unit": "tokens/s",
-            "cores": min(nthr, len(sample) * hkv), "kind": "port",
-            "sample": f"{len(sample)} agents x 1 layer decode over a paged Q4 pool, {reps} reps "
-                      f"({done_bytes / 1e9:.2f} GB of Q4 K/V in {done_s:.1f} s), extrapolated by "
-                      f"Q4 bytes to {len(lengths_all)} agents x {layers} layers",
-            "achieved_gbs": round(done_bytes / done_s / 1e9, 2)}
+
+    def run(budget_s):
+        done_s, reps = 0.0, 0
+        while done_s < budget_s or reps == 0:
+            t = time.perf_counter()
+            orc.attention(q, kq, vq, dk ** -0.5, n_kv_heads=hkv, layout=1, block_table=table,
+                          kv_len=kv_len, causal=False)
+            done_s += time.perf_counter() - t
+            reps += 1
+        done_bytes = sum(sample) * per_tok * reps
+        full_bytes = sum(n + 1 for n in lengths_all) * per_tok * layers
+        step_s = done_s * full_bytes / done_bytes
+        return {"value": round(len(lengths_all) / step_s, 3), "unit": "tokens/s",
+                "cores": min(nthr, len(sample) * hkv), "kind": "port",
+                "sample": f"{len(sample)} agents x 1 layer decode over a paged Q4 pool, {reps} reps "
+                          f"({done_bytes / 1e9:.2f} GB of Q4 K/V in {done_s:.1f} s), extrapolated "
+                          f"by Q4 bytes to {len(lengths_all)} agents x {layers} layers",
+                "achieved_gbs": round(done_bytes / done_s / 1e9, 2)}
+
+    return run
 
 
 def run_reference(args, rank, world):
@@ -592,13 +604,13 @@ def run_reference(args, rank, world):
     layers = args.layers or geo["layers"]
     lengths_all = agent_lengths(args.agents, args.min_len, args.max_len, args.seed)
     vals = []
+    sampler = cpu_sampler(lengths_all, layers, geo)  # the sample is built once, then timed
     for _ in range(args.warmup):
-        cpu_baseline_multi_agent(args, lengths_all, layers, geo, budget_s=1.0)
+        sampler(1.0)
     t0 = time.time()
     last = None
     for _ in range(args.steps):
-        last = cpu_baseline_multi_agent(args, lengths_all, layers, geo,
-                                        budget_s=max(1.0, args.cpu_seconds / max(1, args.steps)))
+        last = sampler(max(1.0, args.cpu_seconds / max(1, args.steps)))
         vals.append(last["value"])
     value = float(np.mean(vals))
     ms = len(lengths_all) / value * 1e3
