@@ -56,6 +56,16 @@ __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t a, uint64_t b, uin
       "l"(a), "l"(b), "r"(id), "r"(accum));
 }
 
+// D (TMEM) [+]= A (TMEM: M rows in lanes, K fp16 elements packed two per 32-bit column)
+// x B (shared-memory descriptor).
+__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t id,
+                                       uint32_t accum) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(id), "r"(accum));
+}
+
 __device__ __forceinline__ void commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
       bar)
@@ -142,6 +152,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]),
       "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
       "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
+// Warp stores 32 lanes x 32 consecutive 32-bit columns of TMEM (thread i -> lane base+i).
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+      "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
@@ -285,8 +308,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
   if (tid == 0) {
     mbar_init(bar(B_SFULL), 1);
     mbar_init(bar(B_SFULL + 1), 1);
-    mbar_init(bar(B_SFREE), kSoftmaxThreads);
-    mbar_init(bar(B_SFREE + 1), kSoftmaxThreads);
+    mbar_init(bar(B_SFREE), 1);  // P . V of the tile done: S (which then holds P) is free
+    mbar_init(bar(B_SFREE + 1), 1);
     mbar_init(bar(B_OFULL), 1);
     mbar_init(bar(B_PFULL), kSoftmaxThreads);
     mbar_init(bar(B_KVFREE), 1);
@@ -554,27 +577,21 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
       float lp[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) lp[k] = 0.0f;
+      // P (fp16 pairs) replaces this warp's own S columns: keys half * 64 + 2c, +1 in
+      // column half * 64 + c of the tile's S buffer, the A operand of P . V
+      uint32_t pk[32];
 #pragma unroll
-      for (int key0 = 0; key0 < 64; key0 += 8) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2(fmaf(v[key0 + 2 * e], fac, -m_safe));
-          const float p1 = ex2(fmaf(v[key0 + 2 * e + 1], fac, -m_safe));
-          lp[(2 * e) & 7] += p0;
-          lp[(2 * e + 1) & 7] += p1;
-          pk[e] = pack_half2(p0, p1);
-        }
-        const int key = half * 64 + key0;
-        const uint32_t off = (key / 64) * (128 * 128) + r * 128 + ((key % 64) / 8) * 16;
-        *reinterpret_cast<uint4*>(smem + LY::OFF_P + tc::swz(off)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = ex2(fmaf(v[2 * c], fac, -m_safe));
+        const float p1 = ex2(fmaf(v[2 * c + 1], fac, -m_safe));
+        lp[(2 * c) & 7] += p0;
+        lp[(2 * c + 1) & 7] += p1;
+        pk[c] = pack_half2(p0, p1);
       }
+      tc::tmem_st32u(tmem + buf * 128 + half * 64 + lane_base, pk);
 #pragma unroll
       for (int k = 0; k < 8; ++k) l_run += lp[k];
-      tc::fence_proxy_async();
       tc::fence_before();
-      mbar_arrive(bar(B_SFREE + buf));
       mbar_arrive(bar(B_PFULL));
       if (warp == 0) {
         // a failed wait only raises the flag: warp 0 must not leave its pair (warp 4)
@@ -586,12 +603,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
           const uint32_t vb_addr = sV + buf * LY::TILE;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
-            const uint32_t poff = (ks / 4) * (128 * 128) + (ks % 4) * 32;
-            tc::mma(tmem + 256, tc::sdesc(sP + poff, 16, 1024),
-                    tc::sdesc(vb_addr + ks * 2048, 128 * 128, 1024), ID_O, (i > 0 || ks > 0) ? 1u : 0u);
+            // 16 keys per step: columns (ks / 4) * 64 + (ks % 4) * 8 of the S buffer
+            tc::mma_ts(tmem + 256, tmem + buf * 128 + (ks / 4) * 64 + (ks % 4) * 8,
+                       tc::sdesc(vb_addr + ks * 2048, 128 * 128, 1024), ID_O, (i > 0 || ks > 0) ? 1u : 0u);
           }
           tc::commit(bar(B_OFULL));
           tc::commit(bar(B_KVFREE + buf));
+          tc::commit(bar(B_SFREE + buf));
         }
         __syncwarp();
       }
