@@ -177,17 +177,17 @@ __device__ __forceinline__ uint32_t swz(uint32_t off) { return off ^ (((off >> 7
 template <int D>
 struct PrefillLayout {
   static constexpr int TILE = 128 * 128 * 2;  // 128 rows x up to 128 fp16 (Q, K, V tiles)
-  static constexpr int P_BYTES = 128 * 128 * 2;  // P: 128 rows x 128 keys fp16
+  static constexpr int NKV = 3;                // K/V tile buffers (P lives in TMEM)
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + TILE;   // two K buffers
-  static constexpr int OFF_V = OFF_K + 2 * TILE;  // two V buffers
-  static constexpr int OFF_P = OFF_V + 2 * TILE;
-  static constexpr int OFF_QF = OFF_P + P_BYTES;  // per-row query factor (128 floats)
+  static constexpr int OFF_K = OFF_Q + TILE;        // NKV K buffers
+  static constexpr int OFF_V = OFF_K + NKV * TILE;  // NKV V buffers
+  static constexpr int OFF_QF = OFF_V + NKV * TILE;  // per-row query factor (128 floats)
   static constexpr int OFF_RX = OFF_QF + 128 * 4;   // per-row exchange between column halves [2][128]
   static constexpr int OFF_BAR = OFF_RX + 2 * 128 * 4;
   static constexpr int SMEM = OFF_BAR + 128 + 1024;  // barriers + slack for 1024-byte alignment
   static constexpr uint32_t TMEM_COLS = 512;     // S x2 (256) + O (D, accumulated over tiles)
   static_assert(D <= 128, "tiles sized for D <= 128");
+  static_assert(SMEM <= 232448, "dynamic shared memory of one CTA");
 };
 
 // Multiply this thread's TMEM row of the O accumulator (D columns at taddr) by f.
@@ -246,7 +246,7 @@ constexpr int kPrefillThreads = 384;
 constexpr int kSoftmaxThreads = 256;
 
 // mbarrier slots (8 bytes each) inside OFF_BAR
-enum { B_SFULL = 0, B_SFREE = 2, B_OFULL = 4, B_KVFREE = 5, B_PFULL = 7, B_COUNT = 8 };
+enum { B_SFULL = 0, B_SFREE = 2, B_OFULL = 4, B_KVFREE = 5, B_PFULL = 8, B_COUNT = 9 };
 
 // Named barrier over one 128-thread warp group that also ORs a flag across it: every
 // thread gets the same answer, so a group leaves its loop together even if the shared
@@ -276,8 +276,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
   const uint32_t s_base = raw_addr + pad;
-  const uint32_t sQ = s_base + LY::OFF_Q, sK = s_base + LY::OFF_K, sV = s_base + LY::OFF_V,
-                 sP = s_base + LY::OFF_P;
+  const uint32_t sQ = s_base + LY::OFF_Q, sK = s_base + LY::OFF_K, sV = s_base + LY::OFF_V;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::OFF_BAR + B_COUNT * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::OFF_BAR + B_COUNT * 8 + 4);
@@ -312,8 +311,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
     mbar_init(bar(B_SFREE + 1), 1);
     mbar_init(bar(B_OFULL), 1);
     mbar_init(bar(B_PFULL), kSoftmaxThreads);
-    mbar_init(bar(B_KVFREE), 1);
-    mbar_init(bar(B_KVFREE + 1), 1);
+    for (int b2 = 0; b2 < LY::NKV; ++b2) mbar_init(bar(B_KVFREE + b2), 1);
     fence_mbar_init();
     *abort_flag = 0;
   }
@@ -426,16 +424,17 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
     RawRow cur;
     if (n_tiles > 0) load_raw(0, cur);
     for (int j = 0; j < n_tiles; ++j) {
-      const int buf = j & 1;
-      if (j >= 2 && !*abort_flag) {
-        if (!mbar_wait_bounded(bar(B_KVFREE + buf), ((j - 2) >> 1) & 1)) *abort_flag = 1;
+      const int buf = j & 1;         // TMEM S buffer
+      const int kvb = j % LY::NKV;   // shared-memory K/V buffer, free once P . V(j - NKV) is done
+      if (j >= LY::NKV && !*abort_flag) {
+        if (!mbar_wait_bounded(bar(B_KVFREE + kvb), ((j - LY::NKV) / LY::NKV) & 1)) *abort_flag = 1;
       }
       // the producers decide together (no thread may be left waiting in barrier 1)
       if (group_bar_any(1, *abort_flag != 0)) break;
       RawRow nxt;
       if (j + 1 < n_tiles) load_raw(j + 1, nxt);
-      uint8_t* kdst = smem + LY::OFF_K + buf * LY::TILE;
-      uint8_t* vdst = smem + LY::OFF_V + buf * LY::TILE;
+      uint8_t* kdst = smem + LY::OFF_K + kvb * LY::TILE;
+      uint8_t* vdst = smem + LY::OFF_V + kvb * LY::TILE;
 #pragma unroll
       for (int G = 0; G < NG; ++G) {
         const __half2 ks2 = scale_h2<SBF16>(cur.ks[G]), kb2 = scale_h2<SBF16>(cur.kb[G]);
@@ -463,7 +462,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
         bool ok = true;
         if (j >= 2) ok = mbar_wait_bounded(bar(B_SFREE + buf), ((j - 2) >> 1) & 1);
         if (ok) {
-          const uint32_t kb_addr = sK + buf * LY::TILE;
+          const uint32_t kb_addr = sK + kvb * LY::TILE;
 #pragma unroll
           for (int ks = 0; ks < KSTEPS; ++ks) {
             const uint32_t off = (ks / 4) * (128 * 128) + (ks % 4) * 32;
@@ -529,6 +528,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
     // an OR barrier, so both halves of a row leave together.
     for (int i = 0; i < n_tiles; ++i) {
       const int buf = i & 1;
+      const int kvb = i % LY::NKV;
       const int t0 = lo + i * 128 + half * 64;  // first key of this warp's columns
       bool ok = !*abort_flag && mbar_wait_bounded(bar(B_SFULL + buf), (i >> 1) & 1);
       if (group_bar_any(pair_bar, !ok, 64)) {
@@ -555,20 +555,24 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
       for (int k = 1; k < 8; ++k) mp[0] = take_max ? fmaxf(mp[0], mp[k]) : fminf(mp[0], mp[k]);
       const float my_max = need_mask ? mp[0] : mp[0] * q_fac;
       rx[half * 128 + r] = my_max;
-      // P . V of the previous tile must be done before P is rewritten (single P buffer)
-      // and before O is rescaled
-      ok = i == 0 || mbar_wait_bounded(bar(B_OFULL), (i - 1) & 1);
-      if (group_bar_any(pair_bar, !ok, 64)) {  // also publishes rx between the pair
+      if (group_bar_any(pair_bar, false, 64)) {  // publishes rx between the pair
         *abort_flag = 1;
         break;
       }
-      tc::fence_after();
       const float tile_max = fmaxf(my_max, rx[(half ^ 1) * 128 + r]);
       const bool raise = tile_max > m_run + kPrefillRescaleSlack;
       if (__any_sync(0xffffffffu, raise)) {  // the same rows, so the same answer in both halves
         const float m_new = raise ? tile_max : m_run;
         const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
-        if (i >= 1) rescale_o<DH>(o_row + half * DH, alpha);
+        if (i >= 1) {
+          // O is rescaled in TMEM only after P . V of the previous tile has landed in it
+          if (__all_sync(0xffffffffu, mbar_wait_bounded(bar(B_OFULL), (i - 1) & 1))) {
+            tc::fence_after();
+            rescale_o<DH>(o_row + half * DH, alpha);
+          } else {
+            *abort_flag = 1;
+          }
+        }
         l_run *= alpha;
         m_run = m_new;
       }
@@ -598,9 +602,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
         // waiting in their barrier, so both see the flag at the next pair barrier
         ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar(B_PFULL), i & 1));
         if (!ok) *abort_flag = 1;
-        if (ok && lane_id == 0) {
+        if (ok && !*abort_flag && lane_id == 0) {
           tc::fence_after();
-          const uint32_t vb_addr = sV + buf * LY::TILE;
+          const uint32_t vb_addr = sV + kvb * LY::TILE;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             // 16 keys per step: columns (ks / 4) * 64 + (ks % 4) * 8 of the S buffer
@@ -608,7 +612,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
                        tc::sdesc(vb_addr + ks * 2048, 128 * 128, 1024), ID_O, (i > 0 || ks > 0) ? 1u : 0u);
           }
           tc::commit(bar(B_OFULL));
-          tc::commit(bar(B_KVFREE + buf));
+          tc::commit(bar(B_KVFREE + kvb));
           tc::commit(bar(B_SFREE + buf));
         }
         __syncwarp();
