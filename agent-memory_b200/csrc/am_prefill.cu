@@ -5,15 +5,16 @@
 // head, so each dequantized K/V tile feeds all of them.  384 threads, warp-specialised:
 //   * producer warps 8-11 dequantize the Q4 K and V rows of 128-key tile j (one token per
 //     thread, raw rows prefetched one tile ahead; fp16 magic-number dequantisation) into
-//     fp16 operand tiles in shared memory (128-byte swizzle; K K-major, V MN-major; two
+//     fp16 operand tiles in shared memory (128-byte swizzle; K K-major, V MN-major; three
 //     buffers), then one producer thread issues S_j = Q . K_j^T (tcgen05.mma kind::f16,
 //     M=128, N=128, K=16 steps) into TMEM S[j%2];
 //   * softmax warps 0-7: warp w owns TMEM lanes 32(w%4) .. +31 (one query row per thread)
 //     and key columns 64(w/4) .. +63 of each tile; tcgen05.ld of its half row, row maxima
-//     exchanged with the partner warp through shared memory, fp32 online softmax, P (fp16,
-//     K-major) into shared memory; O rows rescaled in TMEM only when the running max moves
-//     by more than 2^8.  Once all 256 softmax threads have written P (an mbarrier), lane 0
-//     of warp 0 issues O += P_j . V_j into TMEM O (accumulating after the first tile).
+//     exchanged with the partner warp through shared memory, fp32 online softmax, P as
+//     fp16 pairs stored back over the warp's own S columns (tcgen05.st); O rows rescaled in
+//     TMEM only when the running max moves by more than 2^8.  Once all 256 softmax threads
+//     have written P (an mbarrier), lane 0 of warp 0 issues O += P_j . V_j with A = P read
+//     from TMEM (accumulating after the first tile); its commit frees the S buffer.
 // mbarriers (MMA commits and thread arrivals) chain the stages so the dequantisation of
 // tile j+1, the MMAs of tile j and the softmax of tile j overlap.  TMEM: S x2 + O (512
 // columns, one CTA per SM).  Operands are fp16 for every query dtype: bf16 queries are
