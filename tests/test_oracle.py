@@ -1,6 +1,6 @@
 """CPU checks of the oracle itself, against what the reference's own tests pin.
 
-The reference's tests pin (SURVEY of tests/): the Q4 dtype rule (bf16 input -> bf16
+The reference's tests pin: the Q4 dtype rule (bf16 input -> bf16
 scales/biases, uint32 codes: tests/mlx/test_real_cache_round_trip.py:329-337), shapes
 [..., D/8] / [..., D/64] (tests/mlx/test_fused_attention_gpu.py:36-49), the Q4 byte
 formula (tests/unit/test_analytical_estimates.py:92-190), persistence bit-identity
