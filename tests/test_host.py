@@ -129,3 +129,36 @@ def test_patch_installer_idempotent_and_env_flag(monkeypatch):
 def test_group_size_other_than_64_raises():
     with pytest.raises(NotImplementedError):
         pkg.quantized_scaled_dot_product_attention(None, None, None, 1.0, None, group_size=32)
+
+
+def test_decode_slices_for_query_blocks_without_prefill_kernel(monkeypatch):
+    """Query blocks on head dims without a prefill instantiation are cut into slices of
+    64 / n_rep positions; under the causal mask a slice ending `gap` positions early sees
+    kv_len - gap keys (its queries at their own positions), without it every slice sees all
+    keys; dense masks are sliced along the query axis."""
+    K = pkg.kernels
+    calls = []
+
+    def fake_attention(view, q, scale, kv_len, max_kv_len, **kw):
+        calls.append((q.shape[2], kv_len.tolist(), max_kv_len, kw["out"].shape[2],
+                       None if kw["mask"] is None else kw["mask"].shape[-2], kw["mode"]))
+        return kw["out"]
+
+    monkeypatch.setattr(K, "attention", fake_attention)
+    view = type("V", (), {"n_kv_heads": 8, "k_dim": 256, "v_dim": 256})()
+    B, Hq, L = 2, 16, 100  # n_rep 2 -> slices of 32 positions
+    q = torch.zeros(B, Hq, L, 256)
+    out = torch.zeros(B, Hq, L, 256)
+    kv_len = torch.tensor([400, 300], dtype=torch.int32)
+    assert not K._prefill_kernel_covers(256, 256) and K._prefill_kernel_covers(128, 128)
+    K._attention_in_decode_slices(view, q, 0.1, kv_len, 400, None, True, 0, None, out, None, None)
+    assert [c[0] for c in calls] == [32, 32, 32, 4]
+    assert [c[1] for c in calls] == [[332, 232], [364, 264], [396, 296], [400, 300]]
+    assert [c[2] for c in calls] == [332, 364, 396, 400]
+    assert all(c[3] == c[0] and c[5] == "decode" for c in calls)
+    calls.clear()
+    mask = torch.ones(B, 1, L, 400, dtype=torch.bool)
+    K._attention_in_decode_slices(view, q, 0.1, kv_len, 400, None, False, 0, mask, out, None, None)
+    assert [c[1] for c in calls] == [[400, 300]] * 4 and [c[4] for c in calls] == [32, 32, 32, 4]
+    with pytest.raises(ValueError, match="sliding window without the causal mask"):
+        K._attention_in_decode_slices(view, q, 0.1, kv_len, 400, None, False, 64, None, out, None, None)
