@@ -142,12 +142,17 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int b = blockIdx.z;
-  const int row_groups = gridDim.y / p.hkv;
-  const int h0 = blockIdx.y / row_groups;
-  const int rg = blockIdx.y % row_groups;
-  const int chunk = blockIdx.x;
+  // Grid: clusters are (chunk, head x row group, sequence) with the chunks of a column
+  // along x; otherwise (head x row group, sequence, chunk), so CTAs are dispatched chunk
+  // by chunk and the last to run are the highest chunks, each a sequence's shorter tail
+  // (long work first, short work last).
   const int rph = p.rows_per_head;
+  const int row_groups = (rph + 7) / 8;
+  const int hrg = p.cluster ? blockIdx.y : blockIdx.x;
+  const int b = p.cluster ? blockIdx.z : blockIdx.y;
+  const int chunk = p.cluster ? blockIdx.x : blockIdx.z;
+  const int h0 = hrg / row_groups;
+  const int rg = hrg % row_groups;
 
   const int n = p.kv_len[b];
   const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
@@ -156,7 +161,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   visible_range(n, st, p.q_len, p.window, dense_mask, TS, lo, hi);
   const int span = max(0, hi - lo);
   const int n_chunks_need = max(1, (span + p.chunk - 1) / p.chunk);
-  if (n_chunks_need > p.max_chunks && chunk == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+  if (n_chunks_need > p.max_chunks && chunk == 0 && hrg == 0 && threadIdx.x == 0)
     flag_status(p.status, AM_STATUS_BAD_POSITION);  // kv_len beyond the planned max_kv_len
   const int n_chunks_b = min(n_chunks_need, p.max_chunks);
   // A chunk past this sequence's span has no keys.  In cluster mode its CTA still runs to
@@ -1143,15 +1148,15 @@ static cudaError_t launch_decode_t(const DecodeParams& p, int batch, int row_gro
   static unsigned long long smem_done = 0, cluster_done = 0;
   cudaError_t e = set_smem_once(kfn, LY::SMEM, &smem_done);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.max_chunks, p.hkv * row_groups, batch);
   if (p.cluster) {
+    const dim3 grid(p.max_chunks, p.hkv * row_groups, batch);
     if (p.max_chunks > 8) {
       e = allow_large_clusters_once(kfn, &cluster_done);
       if (e != cudaSuccess) return e;
     }
     return launch_pdl(kfn, grid, dim3(128), LY::SMEM, stream, p, p.max_chunks);
   }
-  e = launch_pdl(kfn, grid, dim3(128), LY::SMEM, stream, p);
+  e = launch_pdl(kfn, dim3(p.hkv * row_groups, batch, p.max_chunks), dim3(128), LY::SMEM, stream, p);
   if (e != cudaSuccess) return e;
   if (p.max_chunks > 1) {
     const int rows_total = p.hq * p.q_len;
