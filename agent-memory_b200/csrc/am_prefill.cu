@@ -287,10 +287,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const Decod
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const bool producer = warp >= 8;
-  const int b = blockIdx.z, h = blockIdx.y;
+  // Grid (KV head, sequence, query tile) with the query tile slowest and reversed: under
+  // the causal mask later query tiles see more keys, so the heaviest CTAs are dispatched
+  // first and the lightest fill the last wave.
+  const int h = blockIdx.x, b = blockIdx.y;
   const int n_rep = p.n_rep;
   const int tok_per_cta = 128 / n_rep;
-  const int l0 = blockIdx.x * tok_per_cta;
+  const int l0 = (gridDim.z - 1 - blockIdx.z) * tok_per_cta;
   const int l_last = min(l0 + tok_per_cta, p.q_len) - 1;
 
   const int n = p.kv_len[b];
@@ -713,7 +716,7 @@ static cudaError_t launch_prefill_t(const DecodeParams& p, int batch, cudaStream
     attr_done = true;
   }
   const int tok_per_cta = 128 / p.n_rep;
-  dim3 grid((p.q_len + tok_per_cta - 1) / tok_per_cta, p.hkv, batch);
+  dim3 grid(p.hkv, batch, (p.q_len + tok_per_cta - 1) / tok_per_cta);
   kfn<<<grid, kPrefillThreads, LY::SMEM, stream>>>(p);
   return cudaGetLastError();
 }
