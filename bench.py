@@ -62,7 +62,7 @@ def parse():
 
 # DRAM bytes (read + write) per algorithmic byte of one decode launch, from the ncu capture
 # of the 32-agent x 2-layer case of this workload (traffic grows with the Q4 bytes read).
-DECODE_TRAFFIC_RATIO = 663.9 / 655.0
+DECODE_TRAFFIC_RATIO = 662.3 / 655.0
 
 
 def peaks():
@@ -402,7 +402,7 @@ def run_ours(args, rank, world, local_rank):
                          "avg_launch_ms": round(avg_launch_s * 1e3, 4),
                          "traffic": round(launch_bytes * DECODE_TRAFFIC_RATIO),
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
-                                           "decode launch of the 32-agent case (663.9 MB for 655.0 MB "
+                                           "decode launch of the 32-agent case (662.3 MB for 655.0 MB "
                                            "algorithmic), scaled by the bytes this launch processes"},
             "e2e": e2e,
             "gpu_launches": args.steps * layers * (3 if combine else 2),
