@@ -9,6 +9,7 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG_DIR = Path(__file__).resolve().parent
@@ -44,11 +45,27 @@ def needs_build() -> bool:
 
 
 def build_library(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every source to an object file in parallel (one nvcc per file), then link the
+    shared library.  Objects go to a build folder next to the sources."""
     if not force and not needs_build():
         return OUT
+    objdir = PKG_DIR / "_build"
+    objdir.mkdir(exist_ok=True)
+    flags = [f for f in NVCC_FLAGS if f != "-shared"]
+
+    def compile_one(src: str) -> Path:
+        obj = objdir / (Path(src).stem + ".o")
+        cmd = [nvcc(), *flags, f"-I{INCLUDE}", f"-I{CSRC}", "-c", "-o", str(obj), str(CSRC / src)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+        objs = list(ex.map(compile_one, SOURCES))
     tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc(), *NVCC_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-o", str(tmp),
-           *[str(CSRC / s) for s in SOURCES]]
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(tmp),
+           *[str(o) for o in objs]]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)

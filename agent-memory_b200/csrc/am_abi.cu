@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include <cudaTypedefs.h>  // PFN_cuTensorMapEncodeTiled
@@ -197,8 +198,21 @@ static bool decode_uses_tensor_maps(int k_dim, int v_dim) {
   return (ok(k_dim) || k_dim == 192) && ok(v_dim);
 }
 
+// Limit of the kernels' bounded waits.  AM_Q4_TEST_WAIT_LIMIT_NS (read on every call) lowers
+// it for tests that drive the timeout path; 0 makes every pipeline wait give up at once (the
+// kernels still let their copies in flight land before they return).  Unset, the limit is
+// kWaitLimitNs.
+static uint64_t wait_limit_ns() {
+  const char* env = getenv("AM_Q4_TEST_WAIT_LIMIT_NS");
+  if (env == nullptr || *env == '\0') return kWaitLimitNs;
+  char* end = nullptr;
+  const unsigned long long v = strtoull(env, &end, 10);
+  return (end != env && v < kWaitLimitNs) ? static_cast<uint64_t>(v) : kWaitLimitNs;
+}
+
 static void fill_params(DecodeParams& p, const am_q4_cache* cache, const am_attn_args* a) {
   const int n_rep = a->n_q_heads / cache->n_kv_heads;
+  p.wait_ns = wait_limit_ns();
   p.kc = cache->k_codes;
   p.ks = static_cast<const uint16_t*>(cache->k_scales);
   p.kb = static_cast<const uint16_t*>(cache->k_biases);

@@ -184,12 +184,19 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Default limit of a kernel's bounded waits (DecodeParams::wait_ns): 2 s.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
 // Wait for phase `parity` of an mbarrier; gives up after `limit_ns` (returns false).  Each
 // try_wait may suspend the warp for up to 0.5 ms (woken early when the phase completes), so
-// a waiting warp yields its issue slots instead of spinning.
+// a waiting warp yields its issue slots instead of spinning.  limit_ns == 0 gives up at once,
+// as a wait whose phase never completes would after its limit: tests use it to drive a
+// kernel's timeout path (flag, drain the copies in flight, release, return) without
+// waiting for anything.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
-                                                  uint64_t limit_ns = 2000000000ull) {
+                                                  uint64_t limit_ns = kWaitLimitNs) {
   constexpr uint32_t kSuspendNs = 500000;
+  if (limit_ns == 0) return false;
   uint64_t t0 = 0;
   for (uint32_t it = 0;; ++it) {
     uint32_t done;
@@ -351,6 +358,7 @@ struct DecodeParams {
   int32_t max_chunks;  // grid.x
   float* ws;           // partials [batch][hq*q_len][max_chunks][kPartialHead + v_dim]
   const float* sinks;  // [hq] sink logits (scaled-score units) or nullptr
+  uint64_t wait_ns;    // limit of the kernels' bounded waits (kWaitLimitNs unless a test lowers it)
   int32_t cluster;     // 1: the max_chunks CTAs of a column are one thread-block cluster and
                        // merge their partials through distributed shared memory (no ws)
   // Decode kernels whose code rows are 32, 64 or 128 bytes load K and V codes through these

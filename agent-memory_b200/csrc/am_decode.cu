@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
       fence_proxy_async_smem();  // earlier reads of the stage being refilled come first
       issue(k + NS - 1);
     }
-    const bool ready = mbar_wait_bounded(smem_u32(&bars[s]), (k / NS) & 1);
+    const bool ready = mbar_wait_bounded(smem_u32(&bars[s]), (k / NS) & 1, p.wait_ns);
     if (!__all_sync(0xffffffffu, ready)) {
       aborted = true;
       break;

@@ -20,6 +20,10 @@
 // The device address of the array is looked up once per device with cudaGetSymbolAddress
 // (the array's host-side name is only a stand-in, not a device address) on the first call
 // made with that device current; make that first call before any stream capture begins.
+// The cached address belongs to the device's current context: after cudaDeviceReset (or
+// any teardown of the primary context) it is stale.  A call that ends in a CUDA error
+// drops the cached address so the next call looks it up again; callers that reset a
+// device should expect the first call afterwards to repeat the lookup.
 #include <mutex>
 
 #include "am_common.cuh"
@@ -60,6 +64,18 @@ static int static_scratch(void** out) {
   return AM_OK;
 }
 
+// Drop the current device's cached address (after a CUDA error it may belong to a context
+// that no longer exists); the next call repeats the lookup.
+static void forget_static_scratch() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    (void)cudaGetLastError();
+    return;
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  g_scratch_ptr[dev] = nullptr;
+}
+
 }  // namespace am
 
 extern "C" int am_q4_decode_noalloc(const am_q4_cache* cache, const am_attn_args* args,
@@ -69,6 +85,12 @@ extern "C" int am_q4_decode_noalloc(const am_q4_cache* cache, const am_attn_args
   if (cache == nullptr || args == nullptr) {
     set_error("am_q4_decode_noalloc: cache and args are required");
     return AM_ERR_INVALID;
+  }
+  // Sizes that cannot describe a call are reported by am_q4_decode's own argument checks
+  // (AM_ERR_INVALID) before the scratch size is computed from them; nothing is launched.
+  if (args->batch < 0 || args->q_len < 0 || args->max_kv_len < 0 || args->n_q_heads <= 0 ||
+      cache->n_kv_heads <= 0 || args->n_q_heads % cache->n_kv_heads != 0) {
+    return am_q4_decode(cache, args, nullptr, 0, stream);
   }
   const size_t need = am_q4_attention_workspace_bytes(cache, args);
   if (need > kStaticDecodeScratchBytes) {
@@ -80,5 +102,7 @@ extern "C" int am_q4_decode_noalloc(const am_q4_cache* cache, const am_attn_args
   void* scratch = nullptr;
   int rc = static_scratch(&scratch);
   if (rc != AM_OK) return rc;
-  return am_q4_decode(cache, args, scratch, kStaticDecodeScratchBytes, stream);
+  rc = am_q4_decode(cache, args, scratch, kStaticDecodeScratchBytes, stream);
+  if (rc == AM_ERR_CUDA) forget_static_scratch();
+  return rc;
 }

@@ -4,9 +4,11 @@
  * Plain C: pointers, sizes and small POD structs, no C++ or torch types.  Every
  * pointer named *device* is a CUDA device address on the current device; `stream`
  * is a cudaStream_t passed as void* (NULL = legacy default stream).  The library
- * allocates no device memory: the caller owns the cache, the queries, the outputs and
- * the workspace.  Calls are stream-ordered and never synchronise the device.  Every
- * function returns AM_OK or a negative AM_ERR_* code; am_last_error() describes the
+ * allocates no device memory at run time: the caller owns the cache, the queries, the
+ * outputs and the workspace.  The only device memory the library itself holds is one
+ * fixed array of AM_STATIC_DECODE_SCRATCH_BYTES per device that loads it (the scratch of
+ * am_q4_decode_noalloc), reserved when the library's module is loaded on that device.
+ * Calls are stream-ordered and never synchronise the device.  Every function returns AM_OK or a negative AM_ERR_* code; am_last_error() describes the
  * last failure on the calling thread.  There is no CPU fallback: an unsupported
  * shape returns AM_ERR_UNSUPPORTED.
  *

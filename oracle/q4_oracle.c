@@ -20,6 +20,17 @@
  *        code = clamp(rint((w - bias) / scale), 0, 15)
  *    scale and bias are then rounded to the input dtype (fp16 or bf16,
  *    tests/mlx/test_real_cache_round_trip.py:329-337 pins that rule).
+ *    In the mlx sources the rule lives in mlx/backend/cpu/quantized.cpp
+ *    (CPU backend) and in the Metal kernels' affine_quantize
+ *    (mlx/backend/metal/kernels/quantized.h).  Details this restatement
+ *    fixes and the tests pin against the GPU kernel bit-for-bit: ties of
+ *    (w - bias) / scale round to the even code (rint), divisions are IEEE
+ *    round-to-nearest, codes come from the fp32 scale and bias before they
+ *    are rounded to the storage dtype, all-zero groups keep bias 0 and the
+ *    scale floor (stored in fp16 as the subnormal 1.19e-7), subnormal inputs
+ *    are not flushed.  Groups whose fp32 range or edge / 1e-7 overflows
+ *    (bf16 values beyond ~1.7e38, or bf16 constants beyond ~3.4e31) have no
+ *    defined codes, in mlx as here.
  *    Codes are packed 8 per uint32, element d in word d/8 at bits 4*(d%8)
  *    (mlx_fused_attention.py:274-288 reads them that way).
  *

@@ -14,8 +14,11 @@ Two independent restatements live here:
 Sources restated (reference paths are relative to the agent-memory repository):
 
 * affine Q4 quantization, group 64: mlx 0.30.3 ``mx.quantize`` (third-party,
-  pyproject.toml:33, not vendored), called at
-  src/agent_memory/adapters/outbound/mlx_quantized_extensions.py:273-274;
+  pyproject.toml:33, not vendored; in the mlx sources mlx/backend/cpu/quantized.cpp and
+  the Metal kernels' affine_quantize), called at
+  src/agent_memory/adapters/outbound/mlx_quantized_extensions.py:273-274.  Ties round to
+  the even code (rint); codes come from the fp32 scale/bias before their rounding to the
+  storage dtype (the corner cases are listed in q4_oracle.c's header);
 * dequantization ``code * scale + bias``: mlx_fused_attention.py:274-288;
 * attention op order (scale q, q.k^T, bool mask -> dtype min / additive mask
   added, softmax in fp32, P.V) and GQA reshape: mlx_fused_attention.py:69-139;

@@ -72,3 +72,17 @@ def assert_close(got, want, atol=2e-3, rtol=1e-3, what=""):
         i = np.unravel_index(np.argmax(err - bound), err.shape)
         raise AssertionError(f"{what}: {bad.sum()} of {err.size} elements out of tolerance; "
                              f"max err {err.max():.3e} at {i}: got {got[i]} want {want[i]}")
+
+
+# Largest relative rounding error of storing a value in a 16-bit output dtype (half an ulp):
+# fp16 keeps 11 significant bits, bf16 8.
+OUT_ROUNDING = {"float16": 2.0 ** -11, "bfloat16": 2.0 ** -8, "float32": 0.0}
+
+
+def assert_close_out(got, want, out_dtype, what=""):
+    """The attention tolerance for outputs stored in a 16-bit dtype: the fp32 bound
+    2e-3 + 1e-3 * |want| plus the dtype's own rounding of the result (half an ulp,
+    OUT_ROUNDING relative).  Cases that check the kernel's arithmetic alone use fp32 outputs
+    and assert_close."""
+    name = str(out_dtype).replace("torch.", "")
+    assert_close(got, want, atol=2e-3, rtol=1e-3 + OUT_ROUNDING[name], what=what)

@@ -211,7 +211,8 @@ def block_pool_ops(services, vo):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the agent-memory repository whose src/ is imported")
     args = ap.parse_args()
     quantize_fixtures()
     import mlx_standin

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import assert_close, pkg
+from conftest import assert_close, assert_close_out, pkg
 from test_gpu_decode import _bits, make_case, oracle
 
 pytestmark = pytest.mark.gpu
@@ -30,11 +30,19 @@ def test_prefill_llama_gqa(cuda, orc, qdtype):
 
 
 def test_prefill_through_dropin_op(cuda, orc):
-    """The drop-in op routes L=64 with the causal string to the prefill kernel."""
+    """The drop-in op routes L=64 with the causal string to the prefill kernel; its fp16
+    output is held to the attention bound plus fp16's own rounding, and the same call with
+    fp32 output to the attention bound alone."""
     q, kq, vq = make_case(1, 8, 8, 300, 128, 128, L=64, cuda=cuda, seed=3)
     got = pkg.quantized_scaled_dot_product_attention(q.to(cuda), kq, vq, 0.08, "causal")
     want = oracle(orc, q, kq, vq, 0.08, causal=True)
-    assert_close(got.float().cpu().numpy(), want, atol=3e-3, rtol=2e-3, what="drop-in prefill")
+    assert got.dtype == torch.float16
+    assert_close_out(got.float().cpu().numpy(), want, got.dtype, what="drop-in prefill")
+    view, N = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((1,), N, dtype=torch.int32, device=cuda)
+    got32 = pkg.kernels.attention(view, q.to(cuda), 0.08, kv_len, N, causal=True,
+                                  out_dtype=torch.float32)
+    assert_close(got32.cpu().numpy(), want, what="drop-in prefill, fp32 out")
 
 
 def test_prefill_d64_mha_window_leftpad(cuda, orc):
@@ -97,7 +105,11 @@ def test_chunked_prefill_paged(cuda, orc):
     want = orc.attention(q.float().numpy(), tuple(_bits(t) for t in pool.k),
                          tuple(_bits(t) for t in pool.v), D ** -0.5, sdtype=1, n_kv_heads=Hkv,
                          layout=1, block_table=table, kv_len=np.array(layer.lengths), causal=True)
-    assert_close(got.float().cpu().numpy(), want, atol=4e-3, rtol=4e-3, what="paged chunked prefill")
+    assert got.dtype == torch.bfloat16
+    assert_close_out(got.float().cpu().numpy(), want, got.dtype, what="paged chunked prefill")
+    out32 = torch.empty(A, Hq, L, D, dtype=torch.float32, device=cuda)
+    layer.attention(q.to(cuda), D ** -0.5, out=out32, mode="prefill")
+    assert_close(out32.cpu().numpy(), want, what="paged chunked prefill, fp32 out")
 
 
 @pytest.mark.parametrize("geom", [(2, 16, 8, 256, 256, 100), (1, 16, 16, 192, 128, 80)],

@@ -141,3 +141,77 @@ def test_append_flags_bad_block(cuda):
     assert int(status.item()) & 1  # AM_STATUS_BAD_BLOCK
     # the valid block was still written
     assert _bits(pool.k[0][0]).any()
+
+
+def _edge_rows(dtype):
+    """Groups at the corners of the affine rule (mlx 0.30.3 affine quantizer: in the mlx
+    sources mlx/backend/cpu/quantized.cpp and the Metal kernel's affine_quantize): exact
+    round-half ties of (w - bias) / scale, groups whose q0 = rint(edge / scale) is 0, constant
+    groups, the dtype's largest finite values, and subnormal inputs."""
+    f32 = torch.float32
+    rows = []
+    # ties: min -15, max 0 -> scale 1, bias -15, (w - bias) / scale = k + 0.5 exactly
+    t = torch.tensor([-15.0 + (k % 15) + 0.5 for k in range(64)], dtype=f32)
+    t[0], t[1] = -15.0, 0.0
+    rows.append(t)
+    # the same with a power-of-two step: min -7.5, max 0 -> scale 0.5, ties at j * 0.5 + 0.25
+    t = torch.tensor([-7.5 + (k % 15) * 0.5 + 0.25 for k in range(64)], dtype=f32)
+    t[0], t[1] = -7.5, 0.0
+    rows.append(t)
+    # ties on the max side (scale negative): max 15, min 0
+    t = torch.tensor([(k % 15) + 0.5 for k in range(64)], dtype=f32)
+    t[0], t[1] = 0.0, 15.0
+    rows.append(t)
+    # q0 = 0: an all-zero group, a group of negative zeros, and (bf16) values far below the
+    # 1e-7 scale floor, whose edge / scale rounds to 0 so the bias is 0
+    rows.append(torch.zeros(64, dtype=f32))
+    rows.append(-torch.zeros(64, dtype=f32))
+    if dtype == torch.bfloat16:
+        rows.append(torch.linspace(-3e-8, 4e-8, 64, dtype=f32))
+        rows.append(torch.full((64,), 2e-8, dtype=f32))
+    # constants of both signs and sizes
+    for c in (1.0, -1.0, 0.3333, -1234.5, 7.0e-5):
+        rows.append(torch.full((64,), c, dtype=f32))
+    # the largest finite values of the dtype (fp16 +-65504); for bf16 the largest values whose
+    # range max - min stays finite in the rule's fp32 arithmetic (+-1.6e38: a group spanning
+    # +-3.39e38 overflows to an infinite scale, in mlx as here, and has no defined codes).
+    # fp16 groups of zeros get the fp16 subnormal scale -1.19e-7 (the 1e-7 floor, rounded).
+    big = 65504.0 if dtype == torch.float16 else 1.6e38
+    t = torch.linspace(-1, 1, 64, dtype=f32) * 1000.0
+    t[3], t[40] = big, -big
+    rows.append(t)
+    t = torch.full((64,), big, dtype=f32)
+    t[9] = -big
+    rows.append(t)
+    # a constant group divides its value by the 1e-7 scale floor: bf16 constants above
+    # ~3.4e31 overflow that quotient (undefined codes, in mlx as here), so bf16 uses 1e30
+    rows.append(torch.full((64,), -(big if dtype == torch.float16 else 1e30), dtype=f32))
+    # subnormal inputs (fp16 subnormals below 6.1e-5; bf16 ones below 1.2e-38)
+    tiny = 6.0e-8 if dtype == torch.float16 else 1.0e-39
+    rows.append(torch.arange(64, dtype=f32) * tiny)
+    rows.append((torch.arange(64, dtype=f32) - 32) * tiny)
+    return torch.stack(rows).to(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_quantize_pinned_edge_cases(cuda, orc, dtype):
+    """Bit-exact GPU vs both CPU restatements on the rule's corner cases, and ties round to
+    the even code (rint), the rounding the restatement follows."""
+    x = _edge_rows(dtype)
+    dt = BF16 if dtype == torch.bfloat16 else F16
+    got = [_bits(t) for t in pkg.quantize(x.to(cuda))]
+    want_c = _oracle_q(x, orc)
+    want_np = orc.quantize_np(x.view(torch.int16).numpy().view(np.uint16), dt)
+    for g, wc, wn, name in zip(got, want_c, want_np, ("codes", "scales", "biases")):
+        kind = np.uint32 if name == "codes" else np.uint16
+        np.testing.assert_array_equal(g, wc.view(kind), err_msg=f"{name} vs C oracle")
+        np.testing.assert_array_equal(g, np.asarray(wn).view(kind), err_msg=f"{name} vs NumPy oracle")
+    codes = got[0].reshape(x.shape[0], -1)
+    nib = (codes[:, :, None] >> (np.arange(8, dtype=np.uint32) * 4)) & 0xF
+    nib = nib.reshape(x.shape[0], 64)
+    # row 0: (w + 15) = k + 0.5 -> even neighbour of k + 0.5 (k + 1 when k is odd, k when even)
+    k = np.arange(64) % 15
+    expect = np.where(k % 2 == 0, k, k + 1)
+    np.testing.assert_array_equal(nib[0, 2:], expect[2:])
+    # all-zero groups: bias 0, codes 0
+    assert not nib[3].any() and not nib[4].any()

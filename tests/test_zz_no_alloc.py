@@ -81,3 +81,57 @@ def test_noalloc_rejects_requests_beyond_the_static_scratch(cuda):
     rc = lib.am_q4_decode_noalloc(ctypes.byref(view.desc), ctypes.byref(a), None)
     assert rc == pkg._lib.AM_ERR_WORKSPACE
     assert b"static scratch" in lib.am_last_error()
+
+
+def test_noalloc_paged_bf16_through_static_scratch(cuda, monkeypatch):
+    """Paged layout with bf16 scales, split chunks merged through the scratch (cluster merging
+    off): two calls in a row agree with am_q4_decode given a caller workspace."""
+    monkeypatch.setenv("AM_Q4_DECODE_MAX_CLUSTER", "0")
+    lib = pkg._lib.load()
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    Hq, Hkv, D, bt = 16, 4, 128, 256
+    lens = [3000, 700, 5000]
+    nb = sum(-(-n // bt) for n in lens)
+    pool = pkg.PagedQ4Pool(Hkv, D, D, nb, bt, torch.bfloat16, cuda)
+    g = torch.Generator().manual_seed(9)
+    perm = torch.randperm(nb, generator=g)
+    table = torch.full((len(lens), max(-(-n // bt) for n in lens)), -1, dtype=torch.int32)
+    used = 0
+    for a, n in enumerate(lens):
+        k = -(-n // bt)
+        table[a, :k] = perm[used:used + k]
+        used += k
+    tab = table.to(cuda)
+    for a, n in enumerate(lens):
+        kk = torch.randn(1, Hkv, n, D, generator=g).bfloat16().to(cuda)
+        vv = torch.randn(1, Hkv, n, D, generator=g).bfloat16().to(cuda)
+        pkg.kernels.append(pool.view(tab[a:a + 1].contiguous()), kk, vv,
+                           torch.zeros(1, dtype=torch.int32, device=cuda))
+    view = pool.view(tab)
+    kv_len = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    for call in range(2):
+        q = torch.randn(len(lens), Hq, 1, D, generator=g).half().to(cuda)
+        ref = torch.empty(len(lens), Hq, 1, D, dtype=torch.float32, device=cuda)
+        got = torch.empty_like(ref)
+        a_ref = _args(view, q, ref, kv_len, max(lens), D ** -0.5)
+        need = lib.am_q4_attention_workspace_bytes(ctypes.byref(view.desc), ctypes.byref(a_ref))
+        assert 0 < need <= pkg._lib.STATIC_DECODE_SCRATCH_BYTES
+        ws = torch.empty(need, dtype=torch.uint8, device=cuda)
+        rc = lib.am_q4_decode(ctypes.byref(view.desc), ctypes.byref(a_ref), ws.data_ptr(), need, stream)
+        assert rc == 0, lib.am_last_error()
+        a_got = _args(view, q, got, kv_len, max(lens), D ** -0.5)
+        rc = lib.am_q4_decode_noalloc(ctypes.byref(view.desc), ctypes.byref(a_got), stream)
+        assert rc == 0, lib.am_last_error()
+        torch.cuda.synchronize(cuda)
+        assert_close(got.cpu().numpy(), ref.cpu().numpy(), what=f"paged bf16 noalloc call {call}")
+
+
+def test_noalloc_reports_bad_sizes_as_invalid(cuda):
+    """Negative sizes are argument errors (AM_ERR_INVALID), not scratch-size errors."""
+    lib = pkg._lib.load()
+    view, q, kv_len, n = _case(cuda, 4, B=1, N=64)
+    out = torch.empty(1, 32, 1, 128, dtype=torch.float32, device=cuda)
+    a = _args(view, q, out, kv_len, n, 0.1)
+    a.max_kv_len = -5
+    assert lib.am_q4_decode_noalloc(ctypes.byref(view.desc), ctypes.byref(a), None) == pkg._lib.AM_ERR_INVALID
+    assert b"max_kv_len" in lib.am_last_error()
