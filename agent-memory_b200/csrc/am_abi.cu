@@ -1,6 +1,7 @@
 // C ABI of libamq4.so: argument validation, dispatch to the kernel launchers, and
 // per-thread error reporting.  The library allocates no device memory and keeps no
 // pointer after a call returns.
+#include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstdint>
@@ -258,6 +259,36 @@ static void fill_params(DecodeParams& p, const am_q4_cache* cache, const am_attn
   p.status = a->status;
 }
 
+// Workspace planes of a prefill call: nw rows per (sequence, KV head) hold the keys the query
+// block can see, [lo, kv_len) -- the window plus the block when a sliding window applies
+// (and no dense mask), else up to max_kv_len keys; K rows first, V rows 256-byte aligned
+// after them.
+struct PrefillPlanes {
+  int nw;
+  int64_t rows;
+  size_t k_bytes, v_bytes;
+};
+
+static PrefillPlanes prefill_planes(const am_q4_cache* c, const am_attn_args* a) {
+  int64_t span = a->max_kv_len;
+  if (a->mask_kind == AM_MASK_NONE && a->window > 0)
+    span = std::min<int64_t>(span, static_cast<int64_t>(a->window) + a->q_len - 1);
+  PrefillPlanes pl;
+  pl.nw = static_cast<int>(std::max<int64_t>(8, (span + 7) / 8 * 8));
+  pl.rows = static_cast<int64_t>(a->batch) * c->n_kv_heads * pl.nw;
+  pl.k_bytes = (static_cast<size_t>(pl.rows) * c->k_dim * 2 + 255) / 256 * 256;
+  pl.v_bytes = static_cast<size_t>(pl.rows) * c->v_dim * 2;
+  return pl;
+}
+
+// am_q4_attention's dispatch: query blocks of more than 64 rows per KV head (n_rep * q_len),
+// or of at least 16 positions, take the tcgen05 prefill kernel; shorter ones split-KV decode.
+static bool routes_to_prefill(const am_q4_cache* c, const am_attn_args* a) {
+  if (c == nullptr || a == nullptr || c->n_kv_heads <= 0 || a->n_q_heads <= 0) return false;
+  const int n_rep = a->n_q_heads / c->n_kv_heads;
+  return n_rep * a->q_len > 64 || (a->q_len >= 16 && prefill_supported(c->k_dim, c->v_dim));
+}
+
 }  // namespace am
 
 using namespace am;
@@ -361,8 +392,9 @@ int am_q4_append(const am_q4_cache* cache, const void* k, const void* v, int32_t
                      "am_q4_append");
 }
 
-size_t am_q4_attention_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args) {
-  if (cache == nullptr || args == nullptr || cache->n_kv_heads <= 0 || args->n_q_heads <= 0)
+size_t am_q4_decode_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args) {
+  if (cache == nullptr || args == nullptr || cache->n_kv_heads <= 0 || args->n_q_heads <= 0 ||
+      args->batch < 0 || args->q_len < 0 || args->max_kv_len < 0)
     return 0;
   int row_groups, chunk, n_chunks, cluster;
   decode_geometry(cache, args, &row_groups, &chunk, &n_chunks, &cluster);
@@ -370,6 +402,19 @@ size_t am_q4_attention_workspace_bytes(const am_q4_cache* cache, const am_attn_a
   const size_t rows_total = static_cast<size_t>(args->n_q_heads) * args->q_len;
   return static_cast<size_t>(args->batch) * rows_total * n_chunks * (cache->v_dim + kPartialHead) *
          sizeof(float);
+}
+
+size_t am_q4_prefill_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args) {
+  if (cache == nullptr || args == nullptr || cache->n_kv_heads <= 0 || args->batch <= 0 ||
+      args->q_len <= 0 || args->max_kv_len < 0 || cache->k_dim <= 0 || cache->v_dim <= 0)
+    return 0;
+  const PrefillPlanes pl = prefill_planes(cache, args);
+  return pl.k_bytes + pl.v_bytes;
+}
+
+size_t am_q4_attention_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args) {
+  return routes_to_prefill(cache, args) ? am_q4_prefill_workspace_bytes(cache, args)
+                                        : am_q4_decode_workspace_bytes(cache, args);
 }
 
 int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
@@ -403,7 +448,7 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
   if (a->batch == 0 || a->q_len == 0) return AM_OK;
   int row_groups, chunk, n_chunks, cluster;
   decode_geometry(cache, a, &row_groups, &chunk, &n_chunks, &cluster);
-  const size_t need = am_q4_attention_workspace_bytes(cache, a);
+  const size_t need = am_q4_decode_workspace_bytes(cache, a);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))) {
     set_error("am_q4_decode: workspace of %zu bytes required (got %zu)", need, workspace_bytes);
     return AM_ERR_WORKSPACE;
@@ -441,7 +486,8 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
                      "am_q4_decode");
 }
 
-int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* stream) {
+int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
+                  size_t workspace_bytes, void* stream) {
   clear_error();
   int rc = check_cache(cache, "am_q4_prefill");
   if (rc) return rc;
@@ -452,8 +498,30 @@ int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* stream)
     return AM_ERR_UNSUPPORTED;
   }
   if (a->batch == 0 || a->q_len == 0) return AM_OK;
+  const PrefillPlanes pl = prefill_planes(cache, a);
+  const size_t need = pl.k_bytes + pl.v_bytes;
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)) {
+    set_error("am_q4_prefill: a 256-byte aligned workspace of %zu bytes is required (got %zu)", need,
+              workspace_bytes);
+    return AM_ERR_WORKSPACE;
+  }
+  if (pl.rows <= 0 || pl.rows > INT_MAX) {
+    set_error("am_q4_prefill: %lld workspace rows (sequences x KV heads x keys) outside (0, 2^31)",
+              static_cast<long long>(pl.rows));
+    return AM_ERR_UNSUPPORTED;
+  }
   DecodeParams p{};
   fill_params(p, cache, a);
+  p.kd = static_cast<uint16_t*>(workspace);
+  p.vd = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + pl.k_bytes);
+  p.nw = pl.nw;
+  const int bn = prefill_key_tile(cache->k_dim, cache->v_dim);
+  if (!encode_codes_map(&p.tmap_kd, p.kd, pl.rows, cache->k_dim * 2, 128, bn) ||
+      !encode_codes_map(&p.tmap_vd, p.vd, pl.rows, cache->v_dim * 2, 128, bn)) {
+    set_error("am_q4_prefill: cannot describe the workspace as tensor maps (a driver with "
+              "cuTensorMapEncodeTiled is required)");
+    return AM_ERR_CUDA;
+  }
   return cuda_status(launch_prefill(p, a->batch, cache->layout == AM_LAYOUT_PAGED,
                                     cache->scale_dtype == AM_DTYPE_BF16,
                                     static_cast<cudaStream_t>(stream)),
@@ -462,12 +530,7 @@ int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* stream)
 
 int am_q4_attention(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
                     size_t workspace_bytes, void* stream) {
-  if (cache != nullptr && a != nullptr && cache->n_kv_heads > 0 && a->n_q_heads > 0) {
-    const int n_rep = a->n_q_heads / cache->n_kv_heads;
-    if (n_rep * a->q_len > 64 || (a->q_len >= 16 && prefill_supported(cache->k_dim, cache->v_dim))) {
-      return am_q4_prefill(cache, a, stream);
-    }
-  }
+  if (routes_to_prefill(cache, a)) return am_q4_prefill(cache, a, workspace, workspace_bytes, stream);
   return am_q4_decode(cache, a, workspace, workspace_bytes, stream);
 }
 

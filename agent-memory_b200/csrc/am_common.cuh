@@ -367,6 +367,15 @@ struct DecodeParams {
   alignas(64) CUtensorMap tmap_kc;
   alignas(64) CUtensorMap tmap_vc;
   alignas(64) CUtensorMap tmap_kc2;
+  // Prefill: fp16 rows of the keys and values the query block can see, dequantized by the
+  // stage kernel into the caller's workspace ([batch][hkv][nw][k_dim] and [..][v_dim]), and
+  // the 2-D tensor maps the attention kernel loads them through ([rows, row bytes], box =
+  // 128 bytes x one key tile, 128-byte swizzle).
+  uint16_t* kd;
+  uint16_t* vd;
+  int32_t nw;  // rows per (sequence, KV head) plane
+  alignas(64) CUtensorMap tmap_kd;
+  alignas(64) CUtensorMap tmap_vd;
 };
 
 // Visible key range of a sequence for the structured mask: keys outside [lo, hi) are

@@ -92,7 +92,7 @@ extern "C" int am_q4_decode_noalloc(const am_q4_cache* cache, const am_attn_args
       cache->n_kv_heads <= 0 || args->n_q_heads % cache->n_kv_heads != 0) {
     return am_q4_decode(cache, args, nullptr, 0, stream);
   }
-  const size_t need = am_q4_attention_workspace_bytes(cache, args);
+  const size_t need = am_q4_decode_workspace_bytes(cache, args);
   if (need > kStaticDecodeScratchBytes) {
     set_error("am_q4_decode_noalloc: this call needs %zu bytes of scratch but the static scratch "
               "holds %zu bytes; use am_q4_decode with a caller-provided workspace",

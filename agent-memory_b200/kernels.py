@@ -307,35 +307,6 @@ def decode_workspace_bytes(view: CacheView, batch: int, n_q_heads: int, q_len: i
     return int(_lib.load().am_q4_attention_workspace_bytes(ctypes.byref(view.desc), ctypes.byref(a)))
 
 
-def _prefill_kernel_covers(k_dim: int, v_dim: int) -> bool:
-    """Head dims with a tcgen05 prefill instantiation (prefill_supported in am_prefill.cu)."""
-    return k_dim == v_dim and k_dim in (64, 128)
-
-
-def _attention_in_decode_slices(view, q, scale, kv_len, max_kv_len, kv_start, causal, window,
-                                mask, out, status, sinks):
-    """Query blocks of head dims the prefill kernel has no instantiation for (Dk = 192 or
-    256: MLA, Gemma-3) run through the split-KV decode kernel in slices of 64 / n_rep query
-    positions.  A slice ending `gap` positions before the last query sees the cache as
-    kv_len - gap keys long, which puts its queries at their own positions; under the causal
-    mask no query sees the keys past that point anyway.  Without the causal mask every
-    query sees all keys and positions do not matter."""
-    B, Hq, L, _ = q.shape
-    n_rep = Hq // view.n_kv_heads
-    if window and not causal:
-        raise ValueError("a sliding window without the causal mask has no kernel for "
-                         f"k_dim={view.k_dim}, v_dim={view.v_dim} query blocks")
-    step = max(1, 64 // n_rep)
-    for l0 in range(0, L, step):
-        l1 = min(L, l0 + step)
-        gap = L - l1 if causal else 0
-        m = mask[..., l0:l1, :] if (mask is not None and mask.shape[-2] == L) else mask
-        attention(view, q[:, :, l0:l1], scale, kv_len - gap if gap else kv_len, max_kv_len - gap,
-                  kv_start=kv_start, causal=causal, window=window, mask=m,
-                  out=out[:, :, l0:l1], status=status, mode="decode", sinks=sinks)
-    return out
-
-
 def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torch.Tensor,
               max_kv_len: int, *, kv_start: torch.Tensor | None = None, causal: bool = False,
               window: int = 0, mask: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
@@ -345,7 +316,9 @@ def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torc
 
     kv_len/kv_start: int32 device tensors [B].  mode: "auto" (library dispatch), "decode"
     (split-KV kernel) or "prefill" (tcgen05 kernel).  sinks: optional [Hq] attention-sink
-    logits (scaled-score units).
+    logits (scaled-score units).  The workspace the chosen kernel needs (split-KV partials,
+    or the prefill kernel's fp16 rows of the visible keys and values) is allocated here from
+    the caching allocator, on the call's stream.
     """
     dev = _require_cuda(queries, kv_len)
     B, Hq, L, Dk = queries.shape
@@ -358,13 +331,6 @@ def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torc
         out = torch.empty(B, Hq, L, view.v_dim, dtype=odt, device=dev)
     elif out.shape != (B, Hq, L, view.v_dim) or out.stride(-1) != 1:
         raise ValueError("out must be [B, Hq, L, Dv] with a contiguous last dim")
-    if (mode == "auto" and (Hq // max(view.n_kv_heads, 1)) * L > 64
-            and not _prefill_kernel_covers(view.k_dim, view.v_dim)):
-        kv_len = kv_len.to(device=dev, dtype=torch.int32)
-        if kv_start is not None:
-            kv_start = kv_start.to(device=dev, dtype=torch.int32)
-        return _attention_in_decode_slices(view, q, scale, kv_len, max_kv_len, kv_start, causal,
-                                           window, mask, out, status, sinks)
     keep = [q, out]
     kv_len = kv_len.to(device=dev, dtype=torch.int32).contiguous()
     keep.append(kv_len)
@@ -398,19 +364,16 @@ def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torc
     else:
         a.sinks = None
     L_ = _lib.load()
-    ws_bytes = L_.am_q4_attention_workspace_bytes(ctypes.byref(view.desc), ctypes.byref(a))
-    ws = torch.empty(max(int(ws_bytes), 16), dtype=torch.uint8, device=dev) if ws_bytes else None
+    fn = {"decode": "am_q4_decode", "prefill": "am_q4_prefill"}.get(mode, "am_q4_attention")
+    sizing = {"am_q4_decode": L_.am_q4_decode_workspace_bytes,
+              "am_q4_prefill": L_.am_q4_prefill_workspace_bytes,
+              "am_q4_attention": L_.am_q4_attention_workspace_bytes}[fn]
+    ws_bytes = int(sizing(ctypes.byref(view.desc), ctypes.byref(a)))
+    # the caching allocator's blocks are 512-byte aligned (the prefill workspace needs 256)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev) if ws_bytes else None
     ws_ptr = ws.data_ptr() if ws is not None else None
-    s = _stream(dev)
-    if mode == "decode":
-        rc = L_.am_q4_decode(ctypes.byref(view.desc), ctypes.byref(a), ws_ptr, ws_bytes, s)
-        check("am_q4_decode", rc)
-    elif mode == "prefill":
-        rc = L_.am_q4_prefill(ctypes.byref(view.desc), ctypes.byref(a), s)
-        check("am_q4_prefill", rc)
-    else:
-        rc = L_.am_q4_attention(ctypes.byref(view.desc), ctypes.byref(a), ws_ptr, ws_bytes, s)
-        check("am_q4_attention", rc)
+    rc = getattr(L_, fn)(ctypes.byref(view.desc), ctypes.byref(a), ws_ptr, ws_bytes, _stream(dev))
+    check(fn, rc)
     return out
 
 

@@ -8,9 +8,10 @@
  * outputs and the workspace.  The only device memory the library itself holds is one
  * fixed array of AM_STATIC_DECODE_SCRATCH_BYTES per device that loads it (the scratch of
  * am_q4_decode_noalloc), reserved when the library's module is loaded on that device.
- * Calls are stream-ordered and never synchronise the device.  Every function returns AM_OK or a negative AM_ERR_* code; am_last_error() describes the
- * last failure on the calling thread.  There is no CPU fallback: an unsupported
- * shape returns AM_ERR_UNSUPPORTED.
+ * Calls are stream-ordered and never synchronise the device.  Every function returns
+ * AM_OK or a negative AM_ERR_* code; am_last_error() describes the last failure on the
+ * calling thread.  There is no CPU fallback: an unsupported shape returns
+ * AM_ERR_UNSUPPORTED.
  *
  * Each entry point names the reference interface it replaces (paths relative to the
  * agent-memory repository).
@@ -25,13 +26,13 @@
 extern "C" {
 #endif
 
-#define AM_ABI_VERSION 2
+#define AM_ABI_VERSION 3
 
 enum {
   AM_OK = 0,
   AM_ERR_INVALID = -1,     /* null pointer, bad shape, misaligned buffer, bad enum */
   AM_ERR_UNSUPPORTED = -2, /* no kernel for this head-dim / dtype combination */
-  AM_ERR_WORKSPACE = -3,   /* workspace smaller than am_q4_attention_workspace_bytes() */
+  AM_ERR_WORKSPACE = -3,   /* workspace smaller than the call's *_workspace_bytes() */
   AM_ERR_CUDA = -4         /* a CUDA launch failed; see am_last_error() */
 };
 
@@ -155,7 +156,17 @@ int am_q4_append(const am_q4_cache* cache, const void* k, const void* v, int32_t
                  int64_t k_stride_l, int64_t v_stride_b, int64_t v_stride_h,
                  int64_t v_stride_l, const int32_t* positions, int32_t* status, void* stream);
 
-/* Bytes of workspace am_q4_attention / am_q4_decode need for these arguments (0 allowed). */
+/*
+ * Workspace sizing (bytes; 0 = none needed).  am_q4_decode_workspace_bytes: the split-KV
+ * partials of am_q4_decode.  am_q4_prefill_workspace_bytes: the fp16 rows of the keys and
+ * values a prefill call can see (batch x n_kv_heads x span x (k_dim + v_dim) x 2 bytes, the
+ * span being max_kv_len, or window + q_len - 1 with a sliding window).
+ * am_q4_attention_workspace_bytes: what am_q4_attention needs for the kernel it dispatches
+ * to.  The reference's compiled path allocates its intermediates inside mlx
+ * (mlx_fused_attention.py:86-109); here the caller owns that memory.
+ */
+size_t am_q4_decode_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args);
+size_t am_q4_prefill_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args);
 size_t am_q4_attention_workspace_bytes(const am_q4_cache* cache, const am_attn_args* args);
 
 /*
@@ -182,9 +193,14 @@ int am_q4_decode_noalloc(const am_q4_cache* cache, const am_attn_args* args, voi
 /*
  * Chunked prefill attention on tcgen05 tensor cores (replaces the L>1 compiled path of
  * _fused_q4_sdpa, mlx_fused_attention.py:144-207, as driven by chunked prefill,
- * batch_engine.py:339-456).  Requires k_dim == v_dim in {64, 128}.
+ * batch_engine.py:339-456).  Head dims (k_dim, v_dim): (64, 64), (128, 128), (128, 64),
+ * (192, 128), (256, 256).  Two launches on `stream`: the keys and values the query block
+ * can see are dequantized once into fp16 rows of `workspace` (256-byte aligned, at least
+ * am_q4_prefill_workspace_bytes), then the attention kernel streams them to the tensor
+ * cores.  Dequantized values beyond fp16's range saturate at +-65504.
  */
-int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* args, void* stream);
+int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* args, void* workspace,
+                  size_t workspace_bytes, void* stream);
 
 /*
  * quantized_scaled_dot_product_attention (mlx_fused_attention.py:462-484): dispatches to

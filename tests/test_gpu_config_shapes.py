@@ -10,6 +10,7 @@ shape of a benchmark configuration, fp32 outputs and the attention tolerance
 * chunked prefill, Llama-3.1-8B heads (32 / 8, head dim 128): batch 2, a 512-token bf16
   chunk appended into 256-token pool blocks after a 4096-token prefix, causal attention of
   the chunk over prefix + chunk;
+* 512-token chunks on the Gemma-3 (global and window-1024 layers) and MLA shapes;
 * multi-agent block-pool decode, Llama-3.1-8B heads: a sample of agents whose contexts span
   the workload's range (1024 to 32768 tokens), blocks at shuffled pool offsets.
 
@@ -114,3 +115,32 @@ def test_multi_agent_decode_sample(cuda, orc):
                          n_kv_heads=Hkv, layout=1, block_table=layer._table_host.numpy(),
                          kv_len=np.array(layer.lengths), causal=False)
     assert_close(out.cpu().numpy(), want, what="multi-agent decode sample")
+
+
+@pytest.mark.parametrize("window", [0, 1024], ids=["global", "window1024"])
+def test_gemma3_prefill_chunk(cuda, orc, window):
+    B, Hq, Hkv, D, N, L = 8, 16, 8, 256, 4096, 512
+    kq = pkg.quantize(_randn((B, Hkv, N, D), 21, cuda))
+    vq = pkg.quantize(_randn((B, Hkv, N, D), 22, cuda))
+    q = _randn((B, Hq, L, D), 23, cuda)
+    view, n = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q, D ** -0.5, kv_len, N, causal=True, window=window,
+                                out_dtype=torch.float32, mode="prefill")
+    want = orc.attention(q.float().cpu().numpy(), _q4_bits(kq), _q4_bits(vq), D ** -0.5,
+                         causal=True, window=window)
+    assert_close(got.cpu().numpy(), want, what=f"gemma3 prefill window={window}")
+
+
+def test_mla_prefill_chunk(cuda, orc):
+    B, H, Dk, Dv, N, L = 16, 16, 192, 128, 8192, 512
+    kq = pkg.quantize(_randn((B, H, N, Dk), 24, cuda))
+    vq = pkg.quantize(_randn((B, H, N, Dv), 25, cuda))
+    q = _randn((B, H, L, Dk), 26, cuda)
+    view, n = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q, Dk ** -0.5, kv_len, N, causal=True,
+                                out_dtype=torch.float32, mode="prefill")
+    want = orc.attention(q.float().cpu().numpy(), _q4_bits(kq), _q4_bits(vq), Dk ** -0.5,
+                         causal=True)
+    assert_close(got.cpu().numpy(), want, what="mla prefill")

@@ -112,13 +112,13 @@ def test_chunked_prefill_paged(cuda, orc):
     assert_close(out32.cpu().numpy(), want, what="paged chunked prefill, fp32 out")
 
 
-@pytest.mark.parametrize("geom", [(2, 16, 8, 256, 256, 100), (1, 16, 16, 192, 128, 80)],
-                         ids=["gemma_d256", "mla_k192_v128"])
+@pytest.mark.parametrize("geom", [(2, 16, 8, 256, 256, 100), (1, 16, 16, 192, 128, 80),
+                                  (2, 8, 4, 128, 64, 90)],
+                         ids=["gemma_d256", "mla_k192_v128", "k128_v64"])
 @pytest.mark.parametrize("window", [0, 96])
-def test_query_blocks_without_prefill_kernel(cuda, orc, geom, window):
-    """Query blocks of head dims without a tcgen05 prefill instantiation (Gemma-3 D256, MLA
-    K192/V128) run through the decode kernel in slices of 64 / n_rep positions, each at its
-    own cache positions (causal, sliding window, left padding)."""
+def test_prefill_gemma_mla_geometries(cuda, orc, geom, window):
+    """Query blocks on the Gemma-3 (D256, 64-key tiles), MLA (K192 / V128) and asymmetric
+    geometries: causal, sliding window, left padding."""
     B, Hq, Hkv, dk, dv, L = geom
     P = 150
     N = P + L
@@ -127,14 +127,13 @@ def test_query_blocks_without_prefill_kernel(cuda, orc, geom, window):
     view, _ = pkg.kernels.contiguous_view(kq, vq)
     kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
     got = pkg.kernels.attention(view, q.to(cuda), dk ** -0.5, kv_len, N, causal=True, window=window,
-                                kv_start=lp.to(cuda), out_dtype=torch.float32)
+                                kv_start=lp.to(cuda), out_dtype=torch.float32, mode="prefill")
     want = oracle(orc, q, kq, vq, dk ** -0.5, causal=True, window=window, kv_start=lp.numpy())
-    assert_close(got.cpu().numpy(), want, what=f"decode slices {geom} window={window}")
+    assert_close(got.cpu().numpy(), want, what=f"prefill {geom} window={window}")
 
 
-def test_query_blocks_without_prefill_kernel_dense_mask(cuda, orc):
-    """Non-causal query block with a boolean mask on a D256 cache: every slice sees all keys
-    and its own rows of the mask."""
+def test_prefill_d256_dense_mask(cuda, orc):
+    """Non-causal query block with a boolean mask on a D256 cache."""
     B, Hq, Hkv, D, L, N = 1, 8, 4, 256, 70, 200
     q, kq, vq = make_case(B, Hq, Hkv, N, D, D, L=L, cuda=cuda, seed=77)
     g = torch.Generator().manual_seed(1)
@@ -142,6 +141,37 @@ def test_query_blocks_without_prefill_kernel_dense_mask(cuda, orc):
     view, _ = pkg.kernels.contiguous_view(kq, vq)
     kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
     got = pkg.kernels.attention(view, q.to(cuda), 0.06, kv_len, N, mask=keep.to(cuda),
-                                out_dtype=torch.float32)
+                                out_dtype=torch.float32, mode="prefill")
     want = oracle(orc, q, kq, vq, 0.06, causal=False, mask=keep.numpy(), mask_kind=1)
-    assert_close(got.cpu().numpy(), want, what="decode slices, dense mask")
+    assert_close(got.cpu().numpy(), want, what="prefill d256 dense mask")
+
+
+@pytest.mark.parametrize("geom", [(2, 16, 8, 256, 256), (1, 16, 16, 192, 128)], ids=["gemma", "mla"])
+def test_prefill_reference_short_blocks(cuda, orc, geom):
+    """The reference's own tests drive Gemma-like and DeepSeek-like query blocks of L = 2
+    (tests/mlx/test_fused_attention_gpu.py:648-674): the drop-in op takes them through the
+    decode kernel; forcing the prefill kernel gives the same answer."""
+    B, Hq, Hkv, dk, dv = geom
+    q, kq, vq = make_case(B, Hq, Hkv, 300, dk, dv, L=2, cuda=cuda, seed=5)
+    want = oracle(orc, q, kq, vq, dk ** -0.5, causal=True)
+    got = pkg.quantized_scaled_dot_product_attention(q.to(cuda), kq, vq, dk ** -0.5, "causal")
+    assert_close_out(got.float().cpu().numpy(), want, got.dtype, what="L=2 drop-in")
+    view, N = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got2 = pkg.kernels.attention(view, q.to(cuda), dk ** -0.5, kv_len, N, causal=True,
+                                 out_dtype=torch.float32, mode="prefill")
+    assert_close(got2.cpu().numpy(), want, what="L=2 prefill kernel")
+
+
+def test_prefill_ragged_kv_len(cuda, orc):
+    """Sequences shorter than the max_kv_len the workspace was sized for: the rows past a
+    sequence's end in its workspace plane are zeros and every output stays finite."""
+    B, Hq, Hkv, D, L, N = 2, 8, 2, 128, 64, 500
+    q, kq, vq = make_case(B, Hq, Hkv, N, D, D, L=L, cuda=cuda, seed=31)
+    view, _ = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.tensor([N, 300], dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q.to(cuda), 0.09, kv_len, N, causal=True,
+                                out_dtype=torch.float32, mode="prefill")
+    assert torch.isfinite(got).all()
+    want = oracle(orc, q, kq, vq, 0.09, causal=True, kv_len=np.array([N, 300]))
+    assert_close(got.cpu().numpy(), want, what="ragged kv_len")

@@ -73,3 +73,27 @@ def test_paged_decode_wait_timeout_is_flagged_and_recovers(cuda, orc, monkeypatc
                          tuple(_bits(t) for t in pool.v), D ** -0.5, n_kv_heads=Hkv, layout=1,
                          block_table=table.numpy(), kv_len=np.array([n]), causal=False)
     assert_close(got.cpu().numpy(), want, what="paged decode after a timed-out call")
+
+
+def test_prefill_wait_timeout_is_flagged_and_recovers(cuda, orc, monkeypatch):
+    """The tcgen05 prefill kernel: its TMA producer, MMA issuer and softmax warps all give
+    up, the kernel waits for its loads and MMAs in flight, frees its TMEM and returns; the
+    next call (fresh TMEM allocations on every SM) is correct."""
+    B, Hq, Hkv, D, L, N = 2, 16, 4, 128, 256, 1200
+    q, kq, vq = make_case(B, Hq, Hkv, N, D, D, L=L, cuda=cuda, seed=23)
+    view, n = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), n, dtype=torch.int32, device=cuda)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    monkeypatch.setenv("AM_Q4_TEST_WAIT_LIMIT_NS", "0")
+    pkg.kernels.attention(view, q.to(cuda), D ** -0.5, kv_len, n, causal=True, status=status,
+                          out_dtype=torch.float32, mode="prefill")
+    torch.cuda.synchronize(cuda)
+    assert int(status.item()) & TIMEOUT
+    monkeypatch.delenv("AM_Q4_TEST_WAIT_LIMIT_NS")
+    status.zero_()
+    got = pkg.kernels.attention(view, q.to(cuda), D ** -0.5, kv_len, n, causal=True, status=status,
+                                out_dtype=torch.float32, mode="prefill")
+    torch.cuda.synchronize(cuda)
+    assert int(status.item()) == 0
+    want = oracle(orc, q, kq, vq, D ** -0.5, causal=True)
+    assert_close(got.cpu().numpy(), want, what="prefill after a timed-out call")

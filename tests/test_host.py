@@ -2,6 +2,8 @@
 tests/unit block-pool tests), structured masks vs mlx-lm's create_causal_mask rule, and
 the agent partition used for multi-GPU sharding."""
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -131,34 +133,45 @@ def test_group_size_other_than_64_raises():
         pkg.quantized_scaled_dot_product_attention(None, None, None, 1.0, None, group_size=32)
 
 
-def test_decode_slices_for_query_blocks_without_prefill_kernel(monkeypatch):
-    """Query blocks on head dims without a prefill instantiation are cut into slices of
-    64 / n_rep positions; under the causal mask a slice ending `gap` positions early sees
-    kv_len - gap keys (its queries at their own positions), without it every slice sees all
-    keys; dense masks are sliced along the query axis."""
-    K = pkg.kernels
-    calls = []
+def _prefill_desc_args(k_dim, v_dim, hkv, hq, batch, q_len, max_kv_len, window=0):
+    d = pkg._lib.Q4CacheDesc()
+    d.k_codes = d.k_scales = d.k_biases = d.v_codes = d.v_scales = d.v_biases = 4096
+    d.scale_dtype, d.layout, d.n_kv_heads, d.k_dim, d.v_dim = 0, 0, hkv, k_dim, v_dim
+    d.capacity, d.batch = (max_kv_len + 15) // 16 * 16, batch
+    a = pkg._lib.AttnArgs()
+    a.q, a.out, a.kv_len = 4096, 4096, 4096
+    a.batch, a.n_q_heads, a.q_len, a.max_kv_len, a.window, a.scale = batch, hq, q_len, max_kv_len, window, 0.1
+    return d, a
 
-    def fake_attention(view, q, scale, kv_len, max_kv_len, **kw):
-        calls.append((q.shape[2], kv_len.tolist(), max_kv_len, kw["out"].shape[2],
-                       None if kw["mask"] is None else kw["mask"].shape[-2], kw["mode"]))
-        return kw["out"]
 
-    monkeypatch.setattr(K, "attention", fake_attention)
-    view = type("V", (), {"n_kv_heads": 8, "k_dim": 256, "v_dim": 256})()
-    B, Hq, L = 2, 16, 100  # n_rep 2 -> slices of 32 positions
-    q = torch.zeros(B, Hq, L, 256)
-    out = torch.zeros(B, Hq, L, 256)
-    kv_len = torch.tensor([400, 300], dtype=torch.int32)
-    assert not K._prefill_kernel_covers(256, 256) and K._prefill_kernel_covers(128, 128)
-    K._attention_in_decode_slices(view, q, 0.1, kv_len, 400, None, True, 0, None, out, None, None)
-    assert [c[0] for c in calls] == [32, 32, 32, 4]
-    assert [c[1] for c in calls] == [[332, 232], [364, 264], [396, 296], [400, 300]]
-    assert [c[2] for c in calls] == [332, 364, 396, 400]
-    assert all(c[3] == c[0] and c[5] == "decode" for c in calls)
-    calls.clear()
-    mask = torch.ones(B, 1, L, 400, dtype=torch.bool)
-    K._attention_in_decode_slices(view, q, 0.1, kv_len, 400, None, False, 0, mask, out, None, None)
-    assert [c[1] for c in calls] == [[400, 300]] * 4 and [c[4] for c in calls] == [32, 32, 32, 4]
-    with pytest.raises(ValueError, match="sliding window without the causal mask"):
-        K._attention_in_decode_slices(view, q, 0.1, kv_len, 400, None, False, 64, None, out, None, None)
+@pytest.mark.parametrize("dims", [(128, 128), (256, 256), (192, 128), (64, 64), (128, 64)])
+def test_prefill_workspace_sizing(dims):
+    """The prefill workspace holds fp16 rows of every key the block can see, per (sequence,
+    KV head): max_kv_len keys, or window + q_len - 1 with a sliding window; K rows first,
+    V rows after them on a 256-byte boundary.  am_q4_attention sizes for the kernel it
+    dispatches to."""
+    lib = pkg._lib.load()
+    dk, dv = dims
+    d, a = _prefill_desc_args(dk, dv, 8, 32, 2, 512, 4608)
+    want = 2 * 8 * 4608 * (dk + dv) * 2
+    assert lib.am_q4_prefill_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == want
+    assert lib.am_q4_attention_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == want
+    a.window = 1024  # window + q_len - 1 = 1535 keys, rounded up to 1536 rows
+    rows = 2 * 8 * 1536
+    k_bytes = (rows * dk * 2 + 255) // 256 * 256
+    assert lib.am_q4_prefill_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == k_bytes + rows * dv * 2
+    a.q_len = 1  # decode-shaped: am_q4_attention takes the split-KV kernel
+    assert lib.am_q4_attention_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == \
+        lib.am_q4_decode_workspace_bytes(ctypes.byref(d), ctypes.byref(a))
+
+
+def test_prefill_without_workspace_is_refused_before_any_launch():
+    lib = pkg._lib.load()
+    d, a = _prefill_desc_args(128, 128, 8, 32, 2, 512, 4608)
+    rc = lib.am_q4_prefill(ctypes.byref(d), ctypes.byref(a), None, 0, None)
+    assert rc == pkg._lib.AM_ERR_WORKSPACE
+    assert b"workspace" in lib.am_last_error()
+    rc = lib.am_q4_prefill(ctypes.byref(d), ctypes.byref(a), 4096 + 128, 1 << 30, None)  # misaligned
+    assert rc == pkg._lib.AM_ERR_WORKSPACE
+    d.k_dim = d.v_dim = 320
+    assert lib.am_q4_prefill(ctypes.byref(d), ctypes.byref(a), None, 0, None) == pkg._lib.AM_ERR_UNSUPPORTED
