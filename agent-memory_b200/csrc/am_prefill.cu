@@ -12,25 +12,29 @@
 //
 // 2. prefill_kernel: one CTA = 128 query rows of one KV head of one sequence.  Rows are
 //    (token, GQA head) pairs, token-major: 128 / n_rep query tokens times the n_rep heads
-//    that share the KV head, so each K/V tile feeds all of them.  320 threads:
-//    * warp 8 (one thread) streams BN-key tiles of K and V from the workspace into NS-stage
-//      shared-memory rings with 2-D tensor-map TMA loads (128-byte swizzle, no multicast);
-//    * warp 9 (one thread) issues every MMA: S_j = Q . K_j^T (tcgen05.mma kind::f16, M = 128,
-//      N = BN, 16-deep K steps) into TMEM S[j % 2], then O += P_{j-1} . V_{j-1} with P read
-//      from TMEM, so the tensor core computes S_j while the softmax warps work on tile j-1;
-//    * softmax warps 0-7: warp w owns TMEM lanes 32 (w % 4) .. +31 (one query row per
-//      thread) and key columns BN/2 (w / 4) .. +BN/2 - 1 of each tile; tcgen05.ld of its half
-//      row, row maxima exchanged with the partner warp through shared memory, fp32 online
-//      softmax, P as fp16 pairs stored back over the warp's own S columns (tcgen05.st); O
-//      rows rescaled in TMEM only when the running max moves by more than 2^8.  A fixed
-//      share of the exponentials runs as a polynomial on the FMA pipe instead of the MUFU
-//      unit (ex2_fma below), which the other share saturates otherwise.
+//    that share the KV head, so each K/V tile feeds all of them.  4 CG + 2 warps, CG = BN / 32
+//    (576 threads for 128-key tiles, 320 for the 64-key tiles of head dim 256):
+//    * one thread of warp 4 CG streams BN-key tiles of K and V from the workspace into
+//      NS-stage shared-memory rings with 2-D tensor-map TMA loads (128-byte swizzle, no
+//      multicast);
+//    * one thread of warp 4 CG + 1 issues every MMA: S_j = Q . K_j^T (tcgen05.mma kind::f16,
+//      M = 128, N = BN, 16-deep K steps) into TMEM S[j % 2], then O += P_{j-1} . V_{j-1} with
+//      P read from TMEM, so the tensor core computes S_j while the softmax warps work on tile
+//      j-1;
+//    * softmax warps 0 .. 4 CG - 1: warp w owns TMEM lanes 32 (w % 4) .. +31 (one query row
+//      per thread) and key columns 32 (w / 4) .. +31 of each tile; tcgen05.ld of its 32
+//      scores, row maxima exchanged among the quarter's CG warps through shared memory, fp32
+//      online softmax, P as fp16 pairs stored back over the warp's own S columns
+//      (tcgen05.st); O rows rescaled in TMEM only when the running max moves by more than
+//      2^8.  A fixed share of the exponentials runs as a polynomial on the FMA pipe instead
+//      of the MUFU unit (ex2_fma below), which the other share saturates otherwise.
 //    mbarriers chain the stages: TMA completions (K/V full), MMA commits (S full, S free,
-//    O full, K/V empty) and the 256 softmax arrivals (P full).  TMEM: S x2 + O (512 columns,
-//    one CTA per SM).  Operands are fp16: queries (fp16 or bf16) are rescaled per row by a
-//    power of two so their conversion is exact.  Every wait is bounded (DecodeParams::
-//    wait_ns, 2 s); on timeout the kernel flags AM_STATUS_TIMEOUT, stops issuing work, waits
-//    (bounded) for its TMA loads and MMAs in flight, frees its TMEM and returns.
+//    O full, K/V empty) and the softmax threads' arrivals (P full).  TMEM: S x2 + O (512
+//    columns, one CTA per SM).  Operands are fp16: queries (fp16 or bf16) are rescaled per
+//    row by a power of two so their conversion is exact.  Every wait is bounded
+//    (DecodeParams::wait_ns, 2 s); on timeout the kernel flags AM_STATUS_TIMEOUT, stops
+//    issuing work, waits (bounded) for its TMA loads and MMAs in flight, frees its TMEM and
+//    returns.
 //
 // The attention grid is launched with programmatic stream serialization: its prologue (TMEM
 // allocation, barriers, the query tile) overlaps the end of the stage kernel, and the TMA
@@ -131,13 +135,30 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
 }
 #undef AM_R8
 
+// Warp loads 32 lanes x 16 consecutive fp32 columns of TMEM.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]) {
-  static_assert(N == 32 || N == 64, "32 or 64 columns");
+  static_assert(N == 16 || N == 32 || N == 64, "16, 32 or 64 columns");
   if constexpr (N == 64) {
     tmem_ld64(taddr, v);
-  } else {
+  } else if constexpr (N == 32) {
     tmem_ld32(taddr, v);
+  } else {
+    tmem_ld16(taddr, v);
   }
 }
 
@@ -175,12 +196,13 @@ __device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&v)[N]) 
   }
 }
 
-// Warp stores 32 lanes x 32 fp32 columns.
-__device__ __forceinline__ void tmem_st32f(uint32_t taddr, const float (&v)[32]) {
-  uint32_t u[32];
+// Warp stores 32 lanes x N fp32 columns (N = 16 or 32).
+template <int N>
+__device__ __forceinline__ void tmem_stf(uint32_t taddr, const float (&v)[N]) {
+  uint32_t u[N];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(v[i]);
-  tmem_st32(taddr, u);
+  for (int i = 0; i < N; ++i) u[i] = __float_as_uint(v[i]);
+  tmem_st<N>(taddr, u);
 }
 
 }  // namespace tc
@@ -201,9 +223,10 @@ __device__ __forceinline__ float ex2_fma(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
-// Exponentials of softmax element pairs (2c, 2c+1): pairs with c % kFmaExpEvery ==
-// kFmaExpEvery - 1 go through ex2_fma, the rest through the MUFU unit.
-constexpr int kFmaExpEvery = 4;
+// Exponentials of softmax element pairs (2c, 2c+1): with kFmaExpEvery > 0, pairs with
+// c % kFmaExpEvery == kFmaExpEvery - 1 go through ex2_fma, the rest through the MUFU unit;
+// 0 keeps every exponential on the MUFU unit.
+constexpr int kFmaExpEvery = 0;
 
 // Lazy rescaling: a row's running max is raised only when a tile's max exceeds it by more
 // than 2^8 (log2 units), so P <= 256 (exact range for the fp16 P operand) and the O
@@ -224,83 +247,117 @@ __device__ __forceinline__ void prefill_block_range(const DecodeParams& p, int b
 }
 
 // ---------------------------------------------------------------- stage kernel
-// grid (ceil(nw / 8), Hkv, batch), 8 warps: warp w converts workspace row 8 blockIdx.x + w of
-// plane (b, h), K words then V words, one 32-bit code word (8 elements) per lane step.
+// grid (ceil(nw / kStageRows), Hkv, batch), 256 threads.  A block converts kStageRows rows of
+// plane (b, h); the work items are 16-byte chunks of code words (32 elements each, K chunks
+// then V chunks of a row), and each thread issues the loads of all its items (codes, scale,
+// bias) before converting any, so enough bytes are in flight to stream at HBM speed.
+constexpr int kStageRows = 128;
+
 template <int DK, int DV, bool SBF16, bool PAGED>
 __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constant__ DecodeParams p) {
   griddep_launch_dependents();
-  constexpr int KW = DK / 8, VW = DV / 8, NGK = DK / 64, NGV = DV / 64;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int CK = DK / 32, CV = DV / 32, CPR = CK + CV;  // chunks per row
+  constexpr int ITEMS = (kStageRows * CPR + 255) / 256;
+  constexpr int NGK = DK / 64, NGV = DV / 64;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int r = blockIdx.x * 8 + warp;
-  if (r >= p.nw) return;
+  const int r0 = blockIdx.x * kStageRows;
   int lo, hi;
   prefill_block_range(p, b, lo, hi);
   if (hi - lo > p.nw) {  // kv_len beyond the max_kv_len the workspace was sized for
-    if (r == 0 && h == 0 && lane == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
+    if (blockIdx.x == 0 && h == 0 && threadIdx.x == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
     hi = lo + p.nw;
   }
-  const int t = lo + r;
-  int64_t row = -1;
-  if (t < hi) {
-    if constexpr (PAGED) {
-      const int bi = t / p.block_tokens;
-      const int32_t blk = bi < p.table_stride ? p.table[(int64_t)b * p.table_stride + bi] : -1;
-      if (blk < 0 || blk >= p.capacity) {
-        if (lane == 0) flag_status(p.status, AM_STATUS_BAD_BLOCK);
+  uint4 code[ITEMS];
+  uint16_t sc[ITEMS], bi[ITEMS];
+  bool live[ITEMS];
+#pragma unroll
+  for (int k = 0; k < ITEMS; ++k) {
+    const int item = threadIdx.x + 256 * k;
+    const int r = r0 + item / CPR, c = item % CPR;
+    const int t = lo + r;
+    live[k] = false;
+    code[k] = make_uint4(0, 0, 0, 0);
+    sc[k] = bi[k] = 0;
+    if (item < kStageRows * CPR && r < p.nw && t < hi) {
+      int64_t row = -1;
+      if constexpr (PAGED) {
+        const int blk_i = t / p.block_tokens;
+        const int32_t blk = blk_i < p.table_stride ? p.table[(int64_t)b * p.table_stride + blk_i] : -1;
+        if (blk < 0 || blk >= p.capacity) {
+          flag_status(p.status, AM_STATUS_BAD_BLOCK);
+        } else {
+          row = ((int64_t)blk * p.hkv + h) * p.block_tokens + t % p.block_tokens;
+        }
       } else {
-        row = ((int64_t)blk * p.hkv + h) * p.block_tokens + t % p.block_tokens;
+        if (t < p.capacity) {
+          row = ((int64_t)b * p.hkv + h) * p.capacity + t;
+        } else {
+          flag_status(p.status, AM_STATUS_BAD_POSITION);
+        }
       }
-    } else {
-      if (t < p.capacity) {
-        row = ((int64_t)b * p.hkv + h) * p.capacity + t;
-      } else if (lane == 0) {
-        flag_status(p.status, AM_STATUS_BAD_POSITION);
+      if (row >= 0) {
+        live[k] = true;
+        if (c < CK) {
+          code[k] = __ldg(reinterpret_cast<const uint4*>(p.kc + row * (DK / 8)) + c);
+          sc[k] = __ldg(p.ks + row * NGK + c / 2);
+          bi[k] = __ldg(p.kb + row * NGK + c / 2);
+        } else {
+          code[k] = __ldg(reinterpret_cast<const uint4*>(p.vc + row * (DV / 8)) + (c - CK));
+          sc[k] = __ldg(p.vs + row * NGV + (c - CK) / 2);
+          bi[k] = __ldg(p.vb + row * NGV + (c - CK) / 2);
+        }
       }
     }
   }
-  const int64_t plane_row = ((int64_t)b * p.hkv + h) * p.nw + r;
-  uint16_t* kdst = p.kd + plane_row * DK;
-  uint16_t* vdst = p.vd + plane_row * DV;
 #pragma unroll
-  for (int w0 = 0; w0 < KW + VW; w0 += 32) {
-    const int w = w0 + lane;
-    if (w < KW + VW) {
-      const bool isk = w < KW;
-      const int wi = isk ? w : w - KW;
-      uint4 outv = make_uint4(0, 0, 0, 0);
-      if (row >= 0) {
-        uint32_t code;
-        uint16_t sb, bb;
-        if (isk) {
-          code = p.kc[row * KW + wi];
-          sb = p.ks[row * NGK + wi / 8];
-          bb = p.kb[row * NGK + wi / 8];
-        } else {
-          code = p.vc[row * VW + wi];
-          sb = p.vs[row * NGV + wi / 8];
-          bb = p.vb[row * NGV + wi / 8];
-        }
-        const float s = h2f<SBF16>(sb), bias = h2f<SBF16>(bb);
-        uint32_t o[4];
+  for (int k = 0; k < ITEMS; ++k) {
+    const int item = threadIdx.x + 256 * k;
+    const int r = r0 + item / CPR, c = item % CPR;
+    if (item >= kStageRows * CPR || r >= p.nw) continue;
+    const int64_t plane_row = ((int64_t)b * p.hkv + h) * p.nw + r;
+    uint16_t* dst = c < CK ? p.kd + plane_row * DK + c * 32 : p.vd + plane_row * DV + (c - CK) * 32;
+    const float s = h2f<SBF16>(sc[k]), bias = h2f<SBF16>(bi[k]);
+    const uint32_t w[4] = {code[k].x, code[k].y, code[k].z, code[k].w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t o[4] = {0u, 0u, 0u, 0u};
+      if (live[k]) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float x0 = fmaf(static_cast<float>((code >> (8 * e)) & 15u), s, bias);
-          float x1 = fmaf(static_cast<float>((code >> (8 * e + 4)) & 15u), s, bias);
+          float x0 = fmaf(static_cast<float>((w[q] >> (8 * e)) & 15u), s, bias);
+          float x1 = fmaf(static_cast<float>((w[q] >> (8 * e + 4)) & 15u), s, bias);
           x0 = fminf(fmaxf(x0, -65504.0f), 65504.0f);
           x1 = fminf(fmaxf(x1, -65504.0f), 65504.0f);
           o[e] = pack_half2(x0, x1);
         }
-        outv = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      *reinterpret_cast<uint4*>((isk ? kdst : vdst) + wi * 8) = outv;
+      reinterpret_cast<uint4*>(dst)[q] = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
 }
 
 // ---------------------------------------------------------------- attention kernel
+// Softmax geometry: CG = BN / CPW warps share each TMEM lane quarter (32 query rows), each
+// owning CPW key columns of every tile, so 4 CG softmax warps overlap one another's
+// TMEM-load, exponential and barrier latencies.
+// Warp 4 CG streams K/V tiles (TMA) and warp 4 CG + 1 issues the MMAs.
+// Key columns each softmax warp owns per tile (32 or 64): fewer columns mean more warps per
+// SM sub-partition to overlap latencies, more columns less fixed cost per score.
+constexpr int kPrefillColsPerWarp = 64;
+
+template <int BN>
+struct SoftmaxGeom {
+  static constexpr int CPW = BN / 2 < kPrefillColsPerWarp ? BN / 2 : kPrefillColsPerWarp;
+  static constexpr int CG = BN / CPW;
+  static constexpr int WARPS = 4 * CG;
+  static constexpr int THREADS = 32 * WARPS;
+  static constexpr int TMA_WARP = WARPS, MMA_WARP = WARPS + 1;
+  static constexpr int CTA_THREADS = THREADS + 64;
+};
+
 template <int DK, int DV, int BN, int NS>
 struct PrefillLayout {
+  static constexpr int CG = SoftmaxGeom<BN>::CG;
   static constexpr int QSLAB = 128 * 128;  // 128 query rows x 64 fp16 (one swizzled slab)
   static constexpr int KSLAB = BN * 128;   // BN keys x 64 fp16
   static constexpr int VSLAB = BN * 128;
@@ -310,29 +367,27 @@ struct PrefillLayout {
   static constexpr int OFF_K = OFF_Q + (DK / 64) * QSLAB;
   static constexpr int OFF_V = OFF_K + NS * KSTAGE;
   static constexpr int OFF_QF = OFF_V + NS * VSTAGE;  // per-row query factor (128 floats)
-  static constexpr int OFF_RX = OFF_QF + 128 * 4;     // row exchange between column halves [2][128]
-  static constexpr int OFF_BAR = OFF_RX + 2 * 128 * 4;
+  static constexpr int OFF_RX = OFF_QF + 128 * 4;     // row exchange between column groups [CG][128]
+  static constexpr int OFF_BAR = OFF_RX + CG * 128 * 4;
   // mbarriers: K full / empty, V full / empty (NS each), S full x2, S free x2, P full x2,
-  // O full, drain
+  // O full x2, drain.  Every barrier that completes once per tile alternates between two
+  // copies by tile parity, so a parity wait can never be satisfied by the phase of the
+  // tile before last.
   static constexpr int B_KFULL = 0, B_KEMPTY = NS, B_VFULL = 2 * NS, B_VEMPTY = 3 * NS;
   static constexpr int B_SFULL = 4 * NS, B_SFREE = B_SFULL + 2, B_PFULL = B_SFREE + 2;
-  static constexpr int B_OFULL = B_PFULL + 2, B_DRAIN = B_OFULL + 1, B_COUNT = B_DRAIN + 1;
-  static constexpr int SMEM = OFF_BAR + B_COUNT * 8 + 16 + 1024;  // + TMEM slot, abort flag, alignment
+  static constexpr int B_OFULL = B_PFULL + 2, B_DRAIN = B_OFULL + 2, B_COUNT = B_DRAIN + 1;
+  static constexpr int SMEM = OFF_BAR + B_COUNT * 8 + 16;  // + TMEM slot and abort flag
   static constexpr uint32_t TMEM_COLS = 512;  // S x2 (2 BN) + O (DV)
   static constexpr int O_COL = 2 * BN;
   static_assert(DK % 64 == 0 && DV % 64 == 0 && DK <= 256 && DV <= 256, "head dims");
   static_assert(BN == 64 || BN == 128, "key tiles of 64 or 128");
   static_assert(2 * BN + DV <= 512, "S x2 + O must fit in TMEM");
+  static_assert((DV / CG) % 16 == 0, "O columns per softmax warp");
 };
 
-constexpr int kPrefillThreads = 320;
-constexpr int kSoftmaxThreads = 256;
-constexpr int kTmaWarp = 8;
-constexpr int kMmaWarp = 9;
-
 // Named barrier over `count` threads that also ORs a flag across them: every thread gets the
-// same answer, so a warp pair leaves its loop together even if the shared abort flag changes
-// while its threads read it.
+// same answer, so the warps of a lane quarter leave their loop together even if the shared
+// abort flag changes while their threads read it.
 __device__ __forceinline__ bool group_bar_any(int id, bool v, int count) {
   uint32_t r;
   asm volatile(
@@ -371,30 +426,38 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, uin
 // Multiply this thread's TMEM row of O (NC columns at taddr) by f.
 template <int NC>
 __device__ __forceinline__ void rescale_o(uint32_t taddr, float f) {
+  constexpr int C = NC < 32 ? NC : 32;
 #pragma unroll 1
-  for (int c = 0; c < NC / 32; ++c) {
-    float v[32];
-    tc::tmem_ld32(taddr + c * 32, v);
+  for (int c = 0; c < NC / C; ++c) {
+    float v[C];
+    tc::tmem_ld<C>(taddr + c * C, v);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= f;
-    tc::tmem_st32f(taddr + c * 32, v);
+    for (int j = 0; j < C; ++j) v[j] *= f;
+    tc::tmem_stf<C>(taddr + c * C, v);
   }
 }
 
 template <int DK, int DV, int BN, int NS, bool DENSE>
-__global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
+    prefill_kernel(const __grid_constant__ DecodeParams p) {
   using LY = PrefillLayout<DK, DV, BN, NS>;
+  using SG = SoftmaxGeom<BN>;
   static_assert(LY::SMEM <= 232448, "dynamic shared memory of one CTA");
-  constexpr int KSTEPS = DK / 16;     // S = Q . K^T: 16-deep steps over the head dim
-  constexpr int PSTEPS = BN / 16;     // O += P . V: 16 keys per step
-  constexpr int HB = BN / 2;          // key columns per softmax warp
-  constexpr int DH = DV / 2;          // O columns each softmax warp rescales and stores
+  constexpr int CG = SG::CG;
+  constexpr int CPW = SG::CPW;
+  constexpr int KSTEPS = DK / 16;  // S = Q . K^T: 16-deep steps over the head dim
+  constexpr int PSTEPS = BN / 16;  // O += P . V: 16 keys per step
+  constexpr int DH = DV / CG;      // O columns each softmax warp rescales and stores
 
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw_addr = smem_u32(smem_raw);
-  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
-  uint8_t* smem = smem_raw + pad;
-  const uint32_t s_base = raw_addr + pad;
+  // The swizzled operand tiles need a 1024-byte aligned window: refuse (every thread alike,
+  // before any barrier or TMEM allocation) rather than feed the tensor cores a shifted pattern.
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t s_base = smem_u32(smem);
+  if (s_base & 1023u) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+      flag_status(p.status, AM_STATUS_BAD_POSITION);
+    return;
+  }
   const uint32_t sQ = s_base + LY::OFF_Q, sK = s_base + LY::OFF_K, sV = s_base + LY::OFF_V;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::OFF_BAR + LY::B_COUNT * 8);
@@ -427,7 +490,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
   // ---- setup
   if (tid == 0) {
     for (int i = 0; i < LY::B_COUNT; ++i)
-      mbar_init(bar(i), (i == LY::B_PFULL || i == LY::B_PFULL + 1) ? kSoftmaxThreads : 1);
+      mbar_init(bar(i), (i == LY::B_PFULL || i == LY::B_PFULL + 1) ? SG::THREADS : 1);
     fence_mbar_init();
     *abort_flag = 0;
   }
@@ -464,6 +527,9 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
       frexpf(amax, &e);
       pw = ldexpf(1.0f, 15 - e);
     }
+    // a negative softmax scale negates the stored query row, so the factor that turns raw
+    // scores into scaled log2 scores is always positive
+    if (p.scale_log2 < 0.0f) pw = -pw;
     sqf[r] = p.scale_log2 / pw;
 #pragma unroll 1
     for (int c = 0; c < DK / 8; ++c) {
@@ -492,7 +558,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
   int issued_k = 0, issued_v = 0;  // TMA thread: tiles whose loads were issued
   bool mma_issued = false;         // MMA thread: any tcgen05.mma issued
 
-  if (warp == kTmaWarp) {
+  if (warp == SG::TMA_WARP) {
     // ================================================================ TMA producer
     if (lane == 0 && n_tiles > 0) {
       griddep_wait();  // the stage kernel's workspace rows are complete and visible
@@ -519,7 +585,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
       }
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == SG::MMA_WARP) {
     // ================================================================ MMA issuer
     if (lane == 0) {
       bool ok = true;
@@ -552,12 +618,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
           const uint32_t vst = sV + s * LY::VSTAGE;
 #pragma unroll
           for (int ks = 0; ks < PSTEPS; ++ks) {
-            // keys 16 ks .. +15: P pairs of softmax half ks / (BN / 32), 8 columns per step
-            const int pcol = (ks / (BN / 32)) * HB + (ks % (BN / 32)) * 8;
+            // keys 16 ks .. +15: P pairs of column group ks / (CPW / 16) (CPW keys in CPW / 2
+            // P columns each)
+            const int pcol = (ks / (CPW / 16)) * CPW + (ks % (CPW / 16)) * 8;
             tc::mma_ts(tmem + LY::O_COL, tmem + buf * BN + pcol,
                        tc::sdesc(vst + ks * 2048, LY::VSLAB, 1024), ID_O, (jj > 0 || ks > 0) ? 1u : 0u);
           }
-          tc::commit(bar(LY::B_OFULL));
+          tc::commit(bar(LY::B_OFULL + buf));
           tc::commit(bar(LY::B_SFREE + buf));
           tc::commit(bar(LY::B_VEMPTY + s));
         }
@@ -567,12 +634,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
   } else {
     // ================================================================ softmax warps
     // Warp w owns S rows 32 (w % 4) .. +31 (its TMEM lane quarter) and key columns
-    // HB (w / 4) .. +HB-1 of every tile; warps w and w + 4 share rows, exchange their row
-    // maxima through shared memory (a 64-thread named barrier per pair) and keep partial
-    // sums that are added at the end.  Each also rescales and writes back half of O.
-    const int quarter = warp & 3, half = warp >> 2;
-    const int r = quarter * 32 + lane;      // query row == TMEM lane
-    const int pair_bar = 3 + quarter;       // named barrier of warps quarter and quarter + 4
+    // CPW (w / 4) .. +CPW-1 of every tile; the CG warps of a quarter exchange their row maxima
+    // through shared memory (a named barrier per quarter) and keep partial sums that are
+    // added at the end.  Each also rescales and writes back DV / CG columns of O.
+    const int quarter = warp & 3, cg = warp >> 2;
+    const int r = quarter * 32 + lane;     // query row == TMEM lane
+    const int qbar = 1 + quarter;          // named barrier of the quarter's CG warps
+    constexpr int QBAR_THREADS = 32 * CG;
     const int rl = r / n_rep;
     const bool row_ok = r < tok_per_cta * n_rep && l0 + rl < p.q_len;
     const int l = l0 + (row_ok ? rl : 0);
@@ -586,9 +654,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
     const int tlo = max(st, p.window > 0 ? pos_max - p.window + 1 : 0);
     const int thi = min(p.causal ? min(n, pos_min + 1) : n, bhi);
     const float q_fac = sqf[r];
-    const bool q_pos = q_fac >= 0.0f;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    float* rx = reinterpret_cast<float*>(smem + LY::OFF_RX);  // [2][128]
+    float* rx = reinterpret_cast<float*>(smem + LY::OFF_RX);  // [CG][128]
 
     float m_run = -INFINITY, l_run = 0.0f;
     const uint32_t o_row = tmem + LY::O_COL + lane_base;  // this thread's row of O
@@ -612,46 +679,52 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
 
     for (int i = 0; i < n_tiles; ++i) {
       const int buf = i & 1;
-      const int t0 = lo + i * BN + half * HB;  // first key of this warp's columns
+      const int t0 = lo + i * BN + cg * CPW;  // first key of this warp's columns
       bool ok = !*abort_flag && wait_or_abort(bar(LY::B_SFULL + buf), (i >> 1) & 1, p.wait_ns, abort_flag);
-      if (group_bar_any(pair_bar, !ok, 64)) {
+      // (this barrier also keeps every warp of the quarter from overwriting rx before the
+      // others have read the previous tile's maxima)
+      if (group_bar_any(qbar, !ok, QBAR_THREADS)) {
         *abort_flag = 1;
         break;
       }
       tc::fence_after();
       const bool need_mask =
-          __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + HB > thi);  // warp-uniform
-      float v[HB];
-      tc::tmem_ld<HB>(tmem + buf * BN + half * HB + lane_base, v);
+          __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + CPW > thi);  // warp-uniform
+      float v[CPW];
+      tc::tmem_ld<CPW>(tmem + buf * BN + cg * CPW + lane_base, v);
       if (need_mask) {
 #pragma unroll
-        for (int j2 = 0; j2 < HB; ++j2) v[j2] = masked(v[j2] * q_fac, t0 + j2);
+        for (int j2 = 0; j2 < CPW; ++j2) v[j2] = masked(v[j2] * q_fac, t0 + j2);
       }
+      // q_fac > 0 (the sign of the softmax scale lives in the query tile), so the row max of
+      // the raw scores is the max of the scaled ones
       float mp[8];
-      const bool take_max = need_mask || q_pos;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mp[k] = take_max ? -INFINITY : INFINITY;
+      for (int k = 0; k < 8; ++k) mp[k] = v[k];
 #pragma unroll
-      for (int j2 = 0; j2 < HB; ++j2)
-        mp[j2 & 7] = take_max ? fmaxf(mp[j2 & 7], v[j2]) : fminf(mp[j2 & 7], v[j2]);
+      for (int j2 = 8; j2 < CPW; ++j2) mp[j2 & 7] = fmaxf(mp[j2 & 7], v[j2]);
 #pragma unroll
-      for (int k = 1; k < 8; ++k) mp[0] = take_max ? fmaxf(mp[0], mp[k]) : fminf(mp[0], mp[k]);
+      for (int k = 1; k < 8; ++k) mp[0] = fmaxf(mp[0], mp[k]);
       const float my_max = need_mask ? mp[0] : mp[0] * q_fac;
-      rx[half * 128 + r] = my_max;
-      if (group_bar_any(pair_bar, false, 64)) {  // publishes rx between the pair
+      rx[cg * 128 + r] = my_max;
+      if (group_bar_any(qbar, false, QBAR_THREADS)) {  // publishes rx within the quarter
         *abort_flag = 1;
         break;
       }
-      const float tile_max = fmaxf(my_max, rx[(half ^ 1) * 128 + r]);
+      float tile_max = rx[r];
+#pragma unroll
+      for (int g2 = 1; g2 < CG; ++g2) tile_max = fmaxf(tile_max, rx[g2 * 128 + r]);
       const bool raise = tile_max > m_run + kPrefillRescaleSlack;
-      if (__any_sync(0xffffffffu, raise)) {  // the same rows, so the same answer in both halves
+      if (__any_sync(0xffffffffu, raise)) {  // the same rows, so the same answer in every group
         const float m_new = raise ? tile_max : m_run;
         const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
         if (i >= 1) {
           // O is rescaled in TMEM only after P . V of the previous tile has landed in it
-          if (__all_sync(0xffffffffu, wait_or_abort(bar(LY::B_OFULL), (i - 1) & 1, p.wait_ns, abort_flag))) {
+          const int pv = i - 1;
+          if (__all_sync(0xffffffffu, wait_or_abort(bar(LY::B_OFULL + (pv & 1)), (pv >> 1) & 1,
+                                                    p.wait_ns, abort_flag))) {
             tc::fence_after();
-            rescale_o<DH>(o_row + half * DH, alpha);
+            rescale_o<DH>(o_row + cg * DH, alpha);
           } else {
             *abort_flag = 1;
           }
@@ -664,15 +737,17 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
       float lp[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) lp[k] = 0.0f;
-      // P (fp16 pairs) replaces this warp's own S columns: keys half * HB + 2c, +1 in column
-      // half * HB + c of the tile's S buffer, the A operand of P . V
-      uint32_t pk[HB / 2];
+      // P (fp16 pairs) replaces this warp's own S columns: keys cg * CPW + 2c, +1 in column
+      // cg * CPW + c of the tile's S buffer, the A operand of P . V
+      uint32_t pk[CPW / 2];
 #pragma unroll
-      for (int c = 0; c < HB / 2; ++c) {
+      for (int c = 0; c < CPW / 2; ++c) {
         const float x0 = fmaf(v[2 * c], fac, -m_safe);
         const float x1 = fmaf(v[2 * c + 1], fac, -m_safe);
-        float p0, p1;
-        if ((c % kFmaExpEvery) == kFmaExpEvery - 1) {
+        float p0 = 0.0f, p1 = 0.0f;
+        bool fma_exp = false;
+        if constexpr (kFmaExpEvery > 0) fma_exp = (c % kFmaExpEvery) == kFmaExpEvery - 1;
+        if (fma_exp) {
           p0 = ex2_fma(x0);
           p1 = ex2_fma(x1);
         } else {
@@ -683,40 +758,49 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
         lp[(2 * c + 1) & 7] += p1;
         pk[c] = pack_half2(p0, p1);
       }
-      tc::tmem_st<HB / 2>(tmem + buf * BN + half * HB + lane_base, pk);
+      tc::tmem_st<CPW / 2>(tmem + buf * BN + cg * CPW + lane_base, pk);
 #pragma unroll
       for (int k = 0; k < 8; ++k) l_run += lp[k];
       tc::fence_before();
       mbar_arrive(bar(LY::B_PFULL + buf));
     }
-    // ---- epilogue: this thread's half of its output row.  The pair adds its partial sums
-    // (the OR barrier also publishes them).
+    // ---- epilogue: this thread's DV / CG columns of its output row.  P . V of the last tile
+    // (and, by the order of commits, of every earlier tile) must have landed in O.  The
+    // quarter adds its partial sums; the first OR barrier makes sure every warp has read the
+    // last tile's maxima from rx before the partial sums overwrite them.
     bool fin = !*abort_flag;
-    if (fin && n_tiles > 0) fin = wait_or_abort(bar(LY::B_OFULL), (n_tiles - 1) & 1, p.wait_ns, abort_flag);
+    if (fin && n_tiles > 0) {
+      const int pv = n_tiles - 1;
+      fin = wait_or_abort(bar(LY::B_OFULL + (pv & 1)), (pv >> 1) & 1, p.wait_ns, abort_flag);
+    }
     fin = __all_sync(0xffffffffu, fin);
-    rx[half * 128 + r] = l_run;
-    const bool bad = group_bar_any(pair_bar, !fin, 64);
+    const bool bad0 = group_bar_any(qbar, !fin, QBAR_THREADS);
+    rx[cg * 128 + r] = l_run;
+    const bool bad = group_bar_any(qbar, bad0, QBAR_THREADS);
     if (!bad) {
       tc::fence_after();
       float o_acc[DH];
       if (n_tiles > 0) {
+        constexpr int C = DH < 32 ? DH : 32;
 #pragma unroll
-        for (int c = 0; c < DH / 32; ++c) {
-          float t32[32];
-          tc::tmem_ld32(o_row + half * DH + c * 32, t32);
+        for (int c = 0; c < DH / C; ++c) {
+          float tcv[C];
+          tc::tmem_ld<C>(o_row + cg * DH + c * C, tcv);
 #pragma unroll
-          for (int j2 = 0; j2 < 32; ++j2) o_acc[c * 32 + j2] = t32[j2];
+          for (int j2 = 0; j2 < C; ++j2) o_acc[c * C + j2] = tcv[j2];
         }
       } else {
 #pragma unroll
         for (int j2 = 0; j2 < DH; ++j2) o_acc[j2] = 0.0f;
       }
       if (row_ok) {
-        const float l_tot = rx[r] + rx[128 + r];
+        float l_tot = 0.0f;
+#pragma unroll
+        for (int g2 = 0; g2 < CG; ++g2) l_tot += rx[g2 * 128 + r];
         const bool sink = p.sinks != nullptr;
         const float inv =
             softmax_out_factor(m_run, l_tot, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
-        const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + half * DH;
+        const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + cg * DH;
         if (p.out_dtype == AM_DTYPE_F32) {
           float* o = static_cast<float*>(p.out) + ob;
           if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
@@ -759,13 +843,13 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_kernel(const __gri
   __syncthreads();
   if (*abort_flag) {
     constexpr uint64_t kDrainNs = 100000000ull;
-    if (warp == kTmaWarp && lane == 0) {
+    if (warp == SG::TMA_WARP && lane == 0) {
       for (int jj = max(0, issued_k - NS); jj < issued_k; ++jj)
         mbar_wait_bounded(bar(LY::B_KFULL + jj % NS), (jj / NS) & 1, kDrainNs);
       for (int jj = max(0, issued_v - NS); jj < issued_v; ++jj)
         mbar_wait_bounded(bar(LY::B_VFULL + jj % NS), (jj / NS) & 1, kDrainNs);
     }
-    if (warp == kMmaWarp && lane == 0 && mma_issued) {
+    if (warp == SG::MMA_WARP && lane == 0 && mma_issued) {
       tc::commit(bar(LY::B_DRAIN));
       mbar_wait_bounded(bar(LY::B_DRAIN), 0, kDrainNs);
     }
@@ -815,7 +899,7 @@ static cudaError_t prefill_smem_once(F kfn, int bytes, unsigned long long* done_
 
 template <int DK, int DV, bool SBF16, bool PAGED>
 static cudaError_t launch_stage_t(const DecodeParams& p, int batch, cudaStream_t stream) {
-  dim3 grid((p.nw + 7) / 8, p.hkv, batch);
+  dim3 grid((p.nw + kStageRows - 1) / kStageRows, p.hkv, batch);
   prefill_stage_kernel<DK, DV, SBF16, PAGED><<<grid, 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
@@ -830,7 +914,7 @@ static cudaError_t launch_attn_t(const DecodeParams& p, int batch, cudaStream_t 
   const int tok_per_cta = 128 / p.n_rep;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.hkv, batch, (p.q_len + tok_per_cta - 1) / tok_per_cta);
-  cfg.blockDim = dim3(kPrefillThreads);
+  cfg.blockDim = dim3(SoftmaxGeom<C::BN>::CTA_THREADS);
   cfg.dynamicSmemBytes = C::LY::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
