@@ -150,6 +150,23 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// The x64 load without its wait (tcgen05.wait::ld separately, before the values are used).
+__device__ __forceinline__ void tmem_ld64_nowait(uint32_t taddr, float (&v)[64]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+#define AM_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), \
+                 "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {"
+      "%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n"
+      : AM_R8(0), AM_R8(8), AM_R8(16), AM_R8(24), AM_R8(32), AM_R8(40), AM_R8(48), AM_R8(56)
+      : "r"(taddr));
+#undef AM_R8
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float (&v)[N]) {
   static_assert(N == 16 || N == 32 || N == 64, "16, 32 or 64 columns");
@@ -223,10 +240,36 @@ __device__ __forceinline__ float ex2_fma(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// The same on a pair of values with the packed fp32x2 FMA pipe operations of sm_100 (two
+// lanes per instruction for the range reduction and the polynomial).
+__device__ __forceinline__ float2 ex2_fma2(float2 x) {
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 big = make_float2(12582912.0f, 12582912.0f);
+  const float2 t = __fadd2_rn(x, big);
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);  // in [-0.5, 0.5]
+  float2 q = __ffma2_rn(f, make_float2(0.0551716685295105f, 0.0551716685295105f),
+                        make_float2(0.2426111251115799f, 0.2426111251115799f));
+  q = __ffma2_rn(f, q, make_float2(0.6932609677314758f, 0.6932609677314758f));
+  q = __ffma2_rn(f, q, make_float2(0.9999280571937561f, 0.9999280571937561f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Exponentials of softmax element pairs (2c, 2c+1): with kFmaExpEvery > 0, pairs with
-// c % kFmaExpEvery == kFmaExpEvery - 1 go through ex2_fma, the rest through the MUFU unit;
-// 0 keeps every exponential on the MUFU unit.
-constexpr int kFmaExpEvery = 0;
+// c % kFmaExpEvery == kFmaExpEvery - 1 go through the FMA-pipe polynomial, the rest through
+// the MUFU unit; 0 keeps every exponential on the MUFU unit.  One thread per query row puts
+// 128 exponentials per tile on its sub-partition's MUFU; a quarter on the FMA pipe measured
+// best (655 TFLOP/s against 645 with none and 632 with half).
+constexpr int kFmaExpEvery = 4;
 
 // Lazy rescaling: a row's running max is raised only when a tile's max exceeds it by more
 // than 2^8 (log2 units), so P <= 256 (exact range for the fp16 P operand) and the O
@@ -746,7 +789,7 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
         const float x1 = fmaf(v[2 * c + 1], fac, -m_safe);
         float p0 = 0.0f, p1 = 0.0f;
         bool fma_exp = false;
-        if constexpr (kFmaExpEvery > 0) fma_exp = (c % kFmaExpEvery) == kFmaExpEvery - 1;
+        if constexpr (kFmaExpEvery > 0) fma_exp = (c % (kFmaExpEvery > 0 ? kFmaExpEvery : 1)) == kFmaExpEvery - 1;
         if (fma_exp) {
           p0 = ex2_fma(x0);
           p1 = ex2_fma(x1);
@@ -864,6 +907,494 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
   }
 }
 
+// Two-tile softmax: issue the TMEM load of a row's second half before processing the first
+// (1), or load each half right before it is used (0: fewer live registers, no spills; measured
+// 655 vs 650 TFLOP/s on the chunked-prefill shape).
+constexpr int kOverlapScoreLoads = 0;
+
+// 64 scores of one row -> 32 fp16 P pairs stored to TMEM at taddr (keys 2c, 2c + 1 in
+// column c), the exponentials added into ls: x = s * fac - m on packed fp32 pairs, a fixed
+// share of the 2^x through the FMA-pipe polynomial.
+__device__ __forceinline__ void softmax_half(const float (&v)[64], float2 fac2, float2 nm2,
+                                             float2 (&ls)[4], uint32_t taddr) {
+  uint32_t pk[32];
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const float2 x = __ffma2_rn(make_float2(v[2 * c], v[2 * c + 1]), fac2, nm2);
+    bool fma_exp = false;
+    if constexpr (kFmaExpEvery > 0) fma_exp = (c % (kFmaExpEvery > 0 ? kFmaExpEvery : 1)) == kFmaExpEvery - 1;
+    const float2 pr = fma_exp ? ex2_fma2(x) : make_float2(ex2(x.x), ex2(x.y));
+    ls[c & 3] = __fadd2_rn(ls[c & 3], pr);
+    pk[c] = pack_half2(pr.x, pr.y);
+  }
+  tc::tmem_st32(taddr, pk);
+}
+
+// ---------------------------------------------------------------- two-tile attention kernel
+// Head dims up to 128: one CTA holds two 128-row query tiles (qt = 0, 1: 256 query rows, 256 /
+// n_rep tokens) of one KV head of one sequence, so every 128-key K/V tile fed from L2 serves
+// twice the rows, and the tensor core works on one query tile while the softmax warps of the
+// other run.  TMEM: S[qt] (128 columns each, P written back over it) and O[qt] (Dv columns
+// each).  Softmax warps: 4 per query tile, warp w owning TMEM lane quarter w % 4 of tile
+// w / 4: one thread per query row, all 128 key columns of a tile, so no exchange between
+// warps.  320 threads: softmax warps 0-7, the TMA thread in warp 8, the MMA thread in warp 9
+// (its issue order is described there).
+constexpr int kTile2Threads = 320;
+
+template <int DK, int DV, int NS>
+struct Prefill2Layout {
+  static constexpr int BN = 128;
+  static constexpr int QSLAB = 128 * 128;          // 128 query rows x 64 fp16
+  static constexpr int QTILE = (DK / 64) * QSLAB;  // one query tile
+  static constexpr int KSLAB = BN * 128, VSLAB = BN * 128;
+  static constexpr int KSTAGE = (DK / 64) * KSLAB, VSTAGE = (DV / 64) * VSLAB;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + 2 * QTILE;
+  static constexpr int OFF_V = OFF_K + NS * KSTAGE;
+  static constexpr int OFF_QF = OFF_V + NS * VSTAGE;  // per-row query factor (256 floats)
+  static constexpr int OFF_BAR = OFF_QF + 256 * 4;
+  // mbarriers: K full / empty, V full / empty (NS each); per query tile: S full, P full,
+  // O full; drain
+  static constexpr int B_KFULL = 0, B_KEMPTY = NS, B_VFULL = 2 * NS, B_VEMPTY = 3 * NS;
+  static constexpr int B_SFULL = 4 * NS, B_PFULL = B_SFULL + 2;
+  static constexpr int B_OFULL = B_PFULL + 2, B_DRAIN = B_OFULL + 2, B_COUNT = B_DRAIN + 1;
+  static constexpr int SMEM = OFF_BAR + B_COUNT * 8 + 16;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int O_COL = 2 * BN;  // S[qt] at qt * BN, O[qt] at O_COL + qt * DV
+  static_assert(DK <= 128 && DV <= 128 && DK % 64 == 0 && DV % 64 == 0, "head dims up to 128");
+  static_assert(2 * BN + 2 * DV <= 512, "S x2 + O x2 must fit in TMEM");
+};
+
+template <int DK, int DV, int NS, bool DENSE>
+__global__ void __launch_bounds__(kTile2Threads, 1) prefill2_kernel(const __grid_constant__ DecodeParams p) {
+  using LY = Prefill2Layout<DK, DV, NS>;
+  static_assert(LY::SMEM <= 232448, "dynamic shared memory of one CTA");
+  constexpr int BN = LY::BN;
+  constexpr int KSTEPS = DK / 16;  // S = Q . K^T: 16-deep steps over the head dim
+  constexpr int PSTEPS = BN / 16;  // O += P . V: 16 keys per step
+  constexpr int TMA_WARP = 8, MMA_WARP = 9;
+
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t s_base = smem_u32(smem);
+  if (s_base & 1023u) {  // swizzled tiles need a 1024-byte aligned window (every thread returns)
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+      flag_status(p.status, AM_STATUS_BAD_POSITION);
+    return;
+  }
+  const uint32_t sQ = s_base + LY::OFF_Q, sK = s_base + LY::OFF_K, sV = s_base + LY::OFF_V;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + LY::OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + LY::OFF_BAR + LY::B_COUNT * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + LY::OFF_BAR + LY::B_COUNT * 8 + 4);
+  float* sqf = reinterpret_cast<float*>(smem + LY::OFF_QF);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  // Grid (KV head, sequence, query block) with the query block slowest and reversed: under
+  // the causal mask later blocks see more keys, so the heaviest CTAs are dispatched first.
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int n_rep = p.n_rep;
+  const int tpq = 128 / n_rep;  // query tokens per query tile
+  const int l0 = (gridDim.z - 1 - blockIdx.z) * 2 * tpq;
+  const int l_last = min(l0 + 2 * tpq, p.q_len) - 1;
+
+  const int n = p.kv_len[b];
+  const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
+  int blo, bhi;  // the workspace plane holds keys [blo, blo + nw)
+  prefill_block_range(p, b, blo, bhi);
+  bhi = min(bhi, blo + p.nw);
+  const int pos_min = n - p.q_len + l0, pos_max = n - p.q_len + l_last;
+  int lo = blo, hi = bhi;  // keys the CTA's rows can see
+  if (!DENSE && p.window > 0) lo = max(lo, pos_min - p.window + 1);
+  if (p.causal) hi = min(hi, pos_max + 1);
+  const int n_tiles = hi > lo ? (hi - lo + BN - 1) / BN : 0;
+
+  // ---- setup
+  if (tid == 0) {
+    for (int i = 0; i < LY::B_COUNT; ++i)
+      mbar_init(bar(i), (i == LY::B_PFULL || i == LY::B_PFULL + 1) ? 128 : 1);
+    fence_mbar_init();
+    *abort_flag = 0;
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(LY::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  if (tid < 256) {
+    // query row R = tid of the CTA (tile R / 128, row R % 128) -> fp16 with a power-of-two
+    // prescale (exact for fp16 / bf16 inputs); a negative softmax scale negates the row, so
+    // the factor back to scaled log2 scores is always positive
+    const int qt = tid >> 7, r = tid & 127;
+    const int rl = r / n_rep;
+    const bool row_ok = r < tpq * n_rep && l0 + qt * tpq + rl < p.q_len;
+    const int l = l0 + qt * tpq + (row_ok ? rl : 0);
+    const int hq = h * n_rep + r % n_rep;
+    const uint16_t* qrow = p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl;
+    float amax = 0.0f;
+    if (row_ok) {
+#pragma unroll 1
+      for (int c = 0; c < DK / 8; ++c) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(qrow + c * 8);
+        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          amax = fmaxf(amax, fabsf(h2f_rt(u[i] & 0xffffu, p.q_bf16)));
+          amax = fmaxf(amax, fabsf(h2f_rt(u[i] >> 16, p.q_bf16)));
+        }
+      }
+    }
+    float pw = 1.0f;
+    if (amax > 0.0f && isfinite(amax)) {
+      int e;
+      frexpf(amax, &e);
+      pw = ldexpf(1.0f, 15 - e);
+    }
+    if (p.scale_log2 < 0.0f) pw = -pw;
+    sqf[tid] = p.scale_log2 / pw;
+#pragma unroll 1
+    for (int c = 0; c < DK / 8; ++c) {
+      uint4 outv = make_uint4(0, 0, 0, 0);
+      if (row_ok) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(qrow + c * 8);
+        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+        uint32_t o4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o4[i] = pack_half2(h2f_rt(u[i] & 0xffffu, p.q_bf16) * pw, h2f_rt(u[i] >> 16, p.q_bf16) * pw);
+        outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+      const uint32_t off = (c / 8) * LY::QSLAB + r * 128 + (c % 8) * 16;
+      *reinterpret_cast<uint4*>(smem + LY::OFF_Q + qt * LY::QTILE + (off ^ (((off >> 7) & 7u) << 4))) = outv;
+    }
+  }
+  fence_proxy_async_smem();
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  constexpr uint32_t ID_S = tc::idesc(128, BN, false);
+  constexpr uint32_t ID_O = tc::idesc(128, DV, true);
+
+  int issued_k = 0, issued_v = 0;  // TMA thread: tiles whose loads were issued
+  bool mma_issued = false;         // MMA thread: any tcgen05.mma issued
+
+  if (warp == TMA_WARP) {
+    // ================================================================ TMA producer
+    if (lane == 0 && n_tiles > 0) {
+      griddep_wait();  // the stage kernel's workspace rows are complete and visible
+      const int y0 = (b * p.hkv + h) * p.nw + (lo - blo);
+      bool ok = true;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j % NS;
+        if (j >= NS) ok = wait_or_abort(bar(LY::B_KEMPTY + s), ((j - NS) / NS) & 1, p.wait_ns, abort_flag);
+        if (!ok) break;
+        mbar_arrive_expect_tx(bar(LY::B_KFULL + s), LY::KSTAGE);
+#pragma unroll
+        for (int x = 0; x < DK / 64; ++x)
+          tma_load_2d(sK + s * LY::KSTAGE + x * LY::KSLAB, &p.tmap_kd, x * 128, y0 + j * BN,
+                      bar(LY::B_KFULL + s));
+        issued_k = j + 1;
+        if (j >= NS) ok = wait_or_abort(bar(LY::B_VEMPTY + s), ((j - NS) / NS) & 1, p.wait_ns, abort_flag);
+        if (!ok) break;
+        mbar_arrive_expect_tx(bar(LY::B_VFULL + s), LY::VSTAGE);
+#pragma unroll
+        for (int x = 0; x < DV / 64; ++x)
+          tma_load_2d(sV + s * LY::VSTAGE + x * LY::VSLAB, &p.tmap_vd, x * 128, y0 + j * BN,
+                      bar(LY::B_VFULL + s));
+        issued_v = j + 1;
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == MMA_WARP) {
+    // ================================================================ MMA issuer
+    // Staggered order per key tile i: S[0]_i, O[1] += P[1]_{i-1} . V_{i-1}, S[1]_i,
+    // O[0] += P[0]_i . V_i, so each query tile's softmax overlaps two MMAs of the other tile.
+    // S[qt]_i overwrites the TMEM columns that held P[qt]_{i-1}: the P . V that reads them was
+    // issued earlier by this thread, and tcgen05.mma operations from one thread execute in
+    // issue order.  A commit arrives once every operation issued before it has completed, so
+    // "S full" of tile i also means P . V of tile i - 1 has landed in O.
+    if (lane == 0) {
+      bool ok = true;
+      auto issue_s = [&](int qt, int j) {
+        const uint32_t kst = sK + (j % NS) * LY::KSTAGE;
+#pragma unroll
+        for (int ks = 0; ks < KSTEPS; ++ks) {
+          tc::mma(tmem + qt * BN,
+                  tc::sdesc(sQ + qt * LY::QTILE + (ks / 4) * LY::QSLAB + (ks % 4) * 32, 16, 1024),
+                  tc::sdesc(kst + (ks / 4) * LY::KSLAB + (ks % 4) * 32, 16, 1024), ID_S,
+                  ks > 0 ? 1u : 0u);
+        }
+        mma_issued = true;
+        tc::commit(bar(LY::B_SFULL + qt));
+      };
+      auto issue_pv = [&](int qt, int jj) {  // after P[qt]_jj is written and V_jj has landed
+        bool w = wait_or_abort(bar(LY::B_PFULL + qt), jj & 1, p.wait_ns, abort_flag);
+        if (w && qt == 0) w = wait_or_abort(bar(LY::B_VFULL + jj % NS), (jj / NS) & 1, p.wait_ns, abort_flag);
+        if (!w) return false;
+        tc::fence_after();
+        const uint32_t vst = sV + (jj % NS) * LY::VSTAGE;
+#pragma unroll
+        for (int ks = 0; ks < PSTEPS; ++ks) {
+          // keys 16 ks .. +15: their P pairs sit in columns 8 ks .. +7 of S[qt]
+          tc::mma_ts(tmem + LY::O_COL + qt * DV, tmem + qt * BN + ks * 8,
+                     tc::sdesc(vst + ks * 2048, LY::VSLAB, 1024), ID_O, (jj > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc::commit(bar(LY::B_OFULL + qt));
+        return true;
+      };
+      for (int i = 0; i < n_tiles && ok; ++i) {
+        ok = wait_or_abort(bar(LY::B_KFULL + i % NS), (i / NS) & 1, p.wait_ns, abort_flag);
+        if (!ok) break;
+        tc::fence_after();
+        issue_s(0, i);
+        if (i >= 1) {
+          ok = issue_pv(1, i - 1);
+          if (!ok) break;
+          tc::commit(bar(LY::B_VEMPTY + (i - 1) % NS));  // both P . V of tile i - 1 issued
+        }
+        issue_s(1, i);
+        tc::commit(bar(LY::B_KEMPTY + i % NS));
+        ok = issue_pv(0, i);
+      }
+      if (ok && n_tiles > 0) {
+        ok = issue_pv(1, n_tiles - 1);
+        if (ok) tc::commit(bar(LY::B_VEMPTY + (n_tiles - 1) % NS));
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ================================================================ softmax warps
+    // Warp w: query tile qt = w / 4, TMEM lane quarter w % 4, one query row per thread, all
+    // 128 key columns of every tile.
+    const int qt = warp >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int rl = r / n_rep;
+    const int tl0 = l0 + qt * tpq;  // first token of this query tile
+    const bool row_ok = r < tpq * n_rep && tl0 + rl < p.q_len;
+    const int l = tl0 + (row_ok ? rl : 0);
+    const int hq = h * n_rep + r % n_rep;
+    const int pos = n - p.q_len + l;
+    const int klo = max(st, p.window > 0 ? pos - p.window + 1 : 0);
+    const int khi = min(p.causal ? min(n, pos + 1) : n, bhi);
+    // keys every row of this query tile sees (tiles inside need no per-element mask)
+    const int t_last = min(tl0 + tpq, p.q_len) - 1;
+    const int tlo = max(st, p.window > 0 ? n - p.q_len + t_last - p.window + 1 : 0);
+    const int thi = min(p.causal ? min(n, n - p.q_len + tl0 + 1) : n, bhi);
+    const float q_fac = sqf[qt * 128 + r];
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_row = tmem + qt * BN + lane_base;               // this row of S[qt]
+    const uint32_t o_row = tmem + LY::O_COL + qt * DV + lane_base;   // this row of O[qt]
+
+    float m_run = -INFINITY, l_run = 0.0f;
+    auto masked = [&](float s, int tok) -> float {
+      if (!(row_ok && tok >= klo && tok < khi)) return -INFINITY;
+      if constexpr (DENSE) {
+        const int64_t idx = (int64_t)b * p.msb + (int64_t)hq * p.msh + (int64_t)l * p.msl +
+                            (int64_t)tok * p.msn;
+        if (p.mask_kind == AM_MASK_BOOL) {
+          if (static_cast<const uint8_t*>(p.mask)[idx] == 0) return -1.0e30f;
+        } else {
+          const float mv = p.mask_dtype == AM_DTYPE_F32
+                               ? static_cast<const float*>(p.mask)[idx]
+                               : h2f_rt(static_cast<const uint16_t*>(p.mask)[idx],
+                                        p.mask_dtype == AM_DTYPE_BF16);
+          s = fmaf(mv, 1.4426950408889634f, s);
+        }
+      }
+      return s;
+    };
+
+    int done_tiles = 0;
+    for (int i = 0; i < n_tiles; ++i) {
+      const int t0 = lo + i * BN;
+      const bool ok = !*abort_flag && wait_or_abort(bar(LY::B_SFULL + qt), i & 1, p.wait_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc::fence_after();
+      const bool need_mask =
+          __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + BN > thi);  // warp-uniform
+      // Scores are read from TMEM twice, 64 columns at a time: once for the row max, once for
+      // the exponentials, so at most half a row is held in registers; the load of the second
+      // half is in flight while the first is processed.  A masked tile is masked on each read
+      // (its scores then carry q_fac).
+      auto mask_half = [&](int hh, float (&v)[64]) {
+        if (need_mask) {
+#pragma unroll
+          for (int j2 = 0; j2 < 64; ++j2) v[j2] = masked(v[j2] * q_fac, t0 + 64 * hh + j2);
+        }
+      };
+      // row max: three-input maxima into eight partial results
+      float mp[8];
+      if constexpr (kOverlapScoreLoads != 0) {
+        float va[64], vb[64];
+        tc::tmem_ld64_nowait(s_row, va);
+        tc::tmem_wait_ld();
+        tc::tmem_ld64_nowait(s_row + 64, vb);
+        mask_half(0, va);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mp[k] = va[k];
+#pragma unroll
+        for (int j2 = 8; j2 < 64; j2 += 2) mp[(j2 >> 1) & 7] = max3f(mp[(j2 >> 1) & 7], va[j2], va[j2 + 1]);
+        tc::tmem_wait_ld();
+        mask_half(1, vb);
+#pragma unroll
+        for (int j2 = 0; j2 < 64; j2 += 2) mp[(j2 >> 1) & 7] = max3f(mp[(j2 >> 1) & 7], vb[j2], vb[j2 + 1]);
+      } else {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float v[64];
+          tc::tmem_ld64(s_row + 64 * hh, v);
+          mask_half(hh, v);
+          if (hh == 0) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) mp[k] = v[k];
+          }
+#pragma unroll
+          for (int j2 = hh == 0 ? 8 : 0; j2 < 64; j2 += 2)
+            mp[(j2 >> 1) & 7] = max3f(mp[(j2 >> 1) & 7], v[j2], v[j2 + 1]);
+        }
+      }
+      mp[0] = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+      const float tile_max = need_mask ? mp[0] : mp[0] * q_fac;
+      const bool raise = tile_max > m_run + kPrefillRescaleSlack;
+      if (__any_sync(0xffffffffu, raise)) {
+        const float m_new = raise ? tile_max : m_run;
+        const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
+        if (i >= 1) {
+          // P . V of the previous tile has landed in O: it read S[qt] before this tile's
+          // scores were written there
+          if (__all_sync(0xffffffffu, wait_or_abort(bar(LY::B_OFULL + qt), (i - 1) & 1, p.wait_ns,
+                                                    abort_flag))) {
+            tc::fence_after();
+            rescale_o<DV>(o_row, alpha);
+          } else {
+            *abort_flag = 1;
+          }
+        }
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
+      const float fac = need_mask ? 1.0f : q_fac;  // masked scores already carry q_fac
+      // exponentials, row sum and P on packed fp32 pairs: x = s * fac - m, p = 2^x
+      const float2 fac2 = make_float2(fac, fac), nm2 = make_float2(-m_safe, -m_safe);
+      float2 ls[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) ls[k] = make_float2(0.0f, 0.0f);
+      // P (fp16 pairs) replaces S[qt]: keys 2c, 2c + 1 in column c, the A operand of P . V;
+      // written in two halves of 32 columns
+      if constexpr (kOverlapScoreLoads != 0) {
+        float va[64], vb[64];
+        tc::tmem_ld64_nowait(s_row, va);
+        tc::tmem_wait_ld();
+        tc::tmem_ld64_nowait(s_row + 64, vb);
+        mask_half(0, va);
+        softmax_half(va, fac2, nm2, ls, s_row);
+        tc::tmem_wait_ld();
+        mask_half(1, vb);
+        softmax_half(vb, fac2, nm2, ls, s_row + 32);
+      } else {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          float v[64];
+          tc::tmem_ld64(s_row + 64 * hh, v);
+          mask_half(hh, v);
+          softmax_half(v, fac2, nm2, ls, s_row + 32 * hh);
+        }
+      }
+      l_run += ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
+      tc::fence_before();
+      mbar_arrive(bar(LY::B_PFULL + qt));
+      done_tiles = i + 1;
+    }
+    // ---- epilogue: this thread's output row, once P . V of the last tile (and, by the order
+    // of commits, of every earlier tile) has landed in O
+    bool fin = !*abort_flag && done_tiles == n_tiles;
+    if (fin && n_tiles > 0)
+      fin = wait_or_abort(bar(LY::B_OFULL + qt), (n_tiles - 1) & 1, p.wait_ns, abort_flag);
+    if (!__all_sync(0xffffffffu, fin)) {
+      *abort_flag = 1;
+    } else {
+      tc::fence_after();
+      const bool sink = p.sinks != nullptr;
+      const float inv =
+          softmax_out_factor(m_run, l_run, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
+      const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl;
+#pragma unroll
+      for (int c = 0; c < DV / 32; ++c) {
+        float o_acc[32];
+        if (n_tiles > 0) {
+          tc::tmem_ld32(o_row + c * 32, o_acc);
+        } else {
+#pragma unroll
+          for (int j2 = 0; j2 < 32; ++j2) o_acc[j2] = 0.0f;
+        }
+        if (!row_ok) continue;
+        if (p.out_dtype == AM_DTYPE_F32) {
+          float* o = static_cast<float*>(p.out) + ob + c * 32;
+          if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+            for (int d = 0; d < 32; d += 4)
+              *reinterpret_cast<float4*>(o + d) =
+                  make_float4(o_acc[d] * inv, o_acc[d + 1] * inv, o_acc[d + 2] * inv, o_acc[d + 3] * inv);
+          } else {
+#pragma unroll
+            for (int d = 0; d < 32; ++d) o[d] = o_acc[d] * inv;
+          }
+        } else {
+          const bool bf = p.out_dtype == AM_DTYPE_BF16;
+          uint16_t* o = static_cast<uint16_t*>(p.out) + ob + c * 32;
+          if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+            for (int d = 0; d < 32; d += 8) {
+              uint32_t w[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float a = o_acc[d + 2 * e] * inv, c2 = o_acc[d + 2 * e + 1] * inv;
+                w[e] = bf ? (static_cast<uint32_t>(f2h<true>(a)) | (static_cast<uint32_t>(f2h<true>(c2)) << 16))
+                          : pack_half2(a, c2);
+              }
+              *reinterpret_cast<uint4*>(o + d) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+#pragma unroll
+            for (int d = 0; d < 32; ++d) o[d] = bf ? f2h<true>(o_acc[d] * inv) : f2h<false>(o_acc[d] * inv);
+          }
+        }
+      }
+    }
+  }
+
+  // ---- teardown: after an abort, let this CTA's TMA loads and MMAs in flight finish
+  // (bounded) before the shared memory and TMEM are released.
+  __syncthreads();
+  if (*abort_flag) {
+    constexpr uint64_t kDrainNs = 100000000ull;
+    if (warp == TMA_WARP && lane == 0) {
+      for (int jj = max(0, issued_k - NS); jj < issued_k; ++jj)
+        mbar_wait_bounded(bar(LY::B_KFULL + jj % NS), (jj / NS) & 1, kDrainNs);
+      for (int jj = max(0, issued_v - NS); jj < issued_v; ++jj)
+        mbar_wait_bounded(bar(LY::B_VFULL + jj % NS), (jj / NS) & 1, kDrainNs);
+    }
+    if (warp == MMA_WARP && lane == 0 && mma_issued) {
+      tc::commit(bar(LY::B_DRAIN));
+      mbar_wait_bounded(bar(LY::B_DRAIN), 0, kDrainNs);
+    }
+    if (tid == 0) flag_status(p.status, AM_STATUS_TIMEOUT);
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                 "r"(LY::TMEM_COLS));
+  }
+}
+
 // ---------------------------------------------------------------- host side
 
 // Key-tile size and pipeline depth per head-dim pair (shared memory: Q tile + NS K and V
@@ -882,7 +1413,22 @@ bool prefill_supported(int k_dim, int v_dim) {
          (k_dim == 192 && v_dim == 128) || (k_dim == 256 && v_dim == 256);
 }
 
-int prefill_key_tile(int k_dim, int v_dim) { return (k_dim + v_dim) > 384 ? 64 : 128; }
+// Head dims up to 128 take the two-tile kernel (64-key tiles); the others the one-tile kernel.
+static bool prefill_two_tiles(int k_dim, int v_dim) { return k_dim <= 128 && v_dim <= 128; }
+
+int prefill_key_tile(int k_dim, int v_dim) {
+  return prefill_two_tiles(k_dim, v_dim) ? 128 : ((k_dim + v_dim) > 384 ? 64 : 128);
+}
+
+// Pipeline depth of the two-tile kernel: as many K/V stages (up to 4) as fit beside the two
+// query tiles.
+template <int DK, int DV>
+struct Prefill2Cfg {
+  static constexpr int NS = Prefill2Layout<DK, DV, 4>::SMEM <= 232448   ? 4
+                            : Prefill2Layout<DK, DV, 3>::SMEM <= 232448 ? 3
+                                                                         : 2;
+  using LY = Prefill2Layout<DK, DV, NS>;
+};
 
 // cudaFuncSetAttribute is per device: remember, per kernel instantiation, the devices done.
 template <typename F>
@@ -906,23 +1452,36 @@ static cudaError_t launch_stage_t(const DecodeParams& p, int batch, cudaStream_t
 
 template <int DK, int DV, bool DENSE>
 static cudaError_t launch_attn_t(const DecodeParams& p, int batch, cudaStream_t stream) {
-  using C = PrefillCfg<DK, DV>;
-  auto kfn = prefill_kernel<DK, DV, C::BN, C::NS, DENSE>;
-  static unsigned long long done = 0;
-  cudaError_t e = prefill_smem_once(kfn, C::LY::SMEM, &done);
-  if (e != cudaSuccess) return e;
-  const int tok_per_cta = 128 / p.n_rep;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.hkv, batch, (p.q_len + tok_per_cta - 1) / tok_per_cta);
-  cfg.blockDim = dim3(SoftmaxGeom<C::BN>::CTA_THREADS);
-  cfg.dynamicSmemBytes = C::LY::SMEM;
+  void (*kfn)(DecodeParams) = nullptr;
+  if constexpr (DK <= 128 && DV <= 128) {
+    using C = Prefill2Cfg<DK, DV>;
+    kfn = prefill2_kernel<DK, DV, C::NS, DENSE>;
+    static unsigned long long done = 0;
+    cudaError_t e = prefill_smem_once(kfn, C::LY::SMEM, &done);
+    if (e != cudaSuccess) return e;
+    const int tok_per_cta = 2 * (128 / p.n_rep);
+    cfg.gridDim = dim3(p.hkv, batch, (p.q_len + tok_per_cta - 1) / tok_per_cta);
+    cfg.blockDim = dim3(kTile2Threads);
+    cfg.dynamicSmemBytes = C::LY::SMEM;
+  } else {
+    using C = PrefillCfg<DK, DV>;
+    kfn = prefill_kernel<DK, DV, C::BN, C::NS, DENSE>;
+    static unsigned long long done = 0;
+    cudaError_t e = prefill_smem_once(kfn, C::LY::SMEM, &done);
+    if (e != cudaSuccess) return e;
+    const int tok_per_cta = 128 / p.n_rep;
+    cfg.gridDim = dim3(p.hkv, batch, (p.q_len + tok_per_cta - 1) / tok_per_cta);
+    cfg.blockDim = dim3(SoftmaxGeom<C::BN>::CTA_THREADS);
+    cfg.dynamicSmemBytes = C::LY::SMEM;
+  }
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kfn, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kfn, p);
   if (e == cudaErrorNotSupported || e == cudaErrorInvalidValue) {
     (void)cudaGetLastError();
     kfn<<<cfg.gridDim, cfg.blockDim, cfg.dynamicSmemBytes, stream>>>(p);

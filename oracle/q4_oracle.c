@@ -61,6 +61,9 @@
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
+#ifdef __AVX2__
+#include <immintrin.h>
+#endif
 #ifdef _OPENMP
 #include <omp.h>
 #endif
@@ -248,10 +251,23 @@ static inline void dequant_row(const uint32_t* codes, const uint16_t* scales,
   for (int g = 0; g < dim / 64; g++) {
     float s = h2f(scales[g], sdtype);
     float b = h2f(biases[g], sdtype);
+#ifdef __AVX2__
+    /* the 8 codes of a word: one broadcast, one variable shift per lane, a mask, a convert
+       and one fused multiply-add (code * scale + bias, fp32) */
+    const __m256i shifts = _mm256_setr_epi32(0, 4, 8, 12, 16, 20, 24, 28);
+    const __m256i nib = _mm256_set1_epi32(15);
+    const __m256 vs = _mm256_set1_ps(s), vb = _mm256_set1_ps(b);
+    for (int word = 0; word < 8; word++) {
+      const __m256i c = _mm256_and_si256(
+          _mm256_srlv_epi32(_mm256_set1_epi32((int)codes[g * 8 + word]), shifts), nib);
+      _mm256_storeu_ps(out + g * 64 + word * 8, _mm256_fmadd_ps(_mm256_cvtepi32_ps(c), vs, vb));
+    }
+#else
     for (int word = 0; word < 8; word++) {
       uint32_t w = codes[g * 8 + word];
       for (int k = 0; k < 8; k++) out[g * 64 + word * 8 + k] = (float)((w >> (4 * k)) & 0xfu) * s + b;
     }
+#endif
   }
 }
 
@@ -352,9 +368,14 @@ int amo_attention(const float* q, int B, int Hq, int L, int Hkv, int Dk, int Dv,
               if (causal && t > pos) keep = 0;
               if (window > 0 && t <= pos - window) keep = 0;
               if (valid[i]) {
+                /* eight partial sums (head dims are multiples of 64), so the compiler can keep
+                   them in one vector register; fp32 throughout */
                 const float* kr = kbuf + (size_t)i * Dk;
-                float dot = 0.0f;
-                for (int d = 0; d < Dk; d++) dot += qv[d] * kr[d];
+                float part[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                for (int d = 0; d < Dk; d += 8)
+                  for (int j = 0; j < 8; j++) part[j] += qv[d + j] * kr[d + j];
+                const float dot = ((part[0] + part[4]) + (part[1] + part[5])) +
+                                  ((part[2] + part[6]) + (part[3] + part[7]));
                 s = dot * scale;
               }
               if (mask_kind != AMO_MASK_NONE) {
