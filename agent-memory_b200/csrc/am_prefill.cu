@@ -367,8 +367,12 @@ __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constan
       if (live[k]) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float x0 = fmaf(static_cast<float>((w[q] >> (8 * e)) & 15u), s, bias);
-          float x1 = fmaf(static_cast<float>((w[q] >> (8 * e + 4)) & 15u), s, bias);
+          // a code OR-ed into the mantissa of 2^23 is exactly 2^23 + code (no int->float
+          // conversion on the XU pipe)
+          const float c0 = __int_as_float(0x4B000000 | ((w[q] >> (8 * e)) & 15u)) - 8388608.0f;
+          const float c1 = __int_as_float(0x4B000000 | ((w[q] >> (8 * e + 4)) & 15u)) - 8388608.0f;
+          float x0 = fmaf(c0, s, bias);
+          float x1 = fmaf(c1, s, bias);
           x0 = fminf(fmaxf(x0, -65504.0f), 65504.0f);
           x1 = fminf(fmaxf(x1, -65504.0f), 65504.0f);
           o[e] = pack_half2(x0, x1);

@@ -14,6 +14,7 @@
 // each); a warp covers 4 groups.  Min/max are reduced with 3 xor-shuffles inside the
 // 8-lane team.  The kernels are HBM-bound: 128 B read + 36 B written per group (fp16).
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 
 #include "am_common.cuh"
@@ -51,18 +52,43 @@ __device__ __forceinline__ uint32_t quantize_team(const float (&w)[8], float& sc
   float scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), 15.0f), 1e-7f);
   scale = side ? scale : -scale;
   const float edge = side ? mn : mx;
-  const float q0 = rintf(__fdiv_rn(edge, scale));
+  // q0 = rint(fl(edge / scale)); |edge / scale| <= 15, so the reciprocal product decides it
+  // except within 2^-16 of a half-integer (see the codes below)
+  float q0;
+  {
+    const float t = __fmul_rn(edge, __frcp_rn(scale));
+    q0 = rintf(t);
+    if (fabsf(t - q0) > 0.5f - 1.52587890625e-05f) q0 = rintf(__fdiv_rn(edge, scale));
+  }
   float bias = 0.0f;
   if (q0 != 0.0f) {
     scale = __fdiv_rn(edge, q0);
     bias = edge;
   }
+  // code = clamp(rint(fl((w - bias) / scale)), 0, 15) with the IEEE-rounded quotient.  The
+  // product with the correctly rounded reciprocal is within 2^-19 of the exact quotient for
+  // |quotient| < 16 (two roundings of 2^-24 relative each), so its rint can only differ from
+  // the rint of the rounded quotient within that distance of a half-integer: there (and only
+  // there) the division itself is done.  Quotients of 16 and more clamp to 15 either way.
+  // The rounding itself stays on the FMA/ALU pipes: t is first clamped to [-1, 16] (codes of
+  // quotients below -0.5 are 0 and above 15.5 are 15 either way; NaN clamps to -1 -> 0, as
+  // fmaxf(rint(NaN), 0) does), then adding 1.5 * 2^23 rounds it to the nearest integer (ties
+  // to even, as rint) in the low mantissa bits.
+  const float inv = __frcp_rn(scale);
   uint32_t packed = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    float c = rintf(__fdiv_rn(__fsub_rn(w[i], bias), scale));
-    c = fminf(fmaxf(c, 0.0f), 15.0f);
-    packed |= static_cast<uint32_t>(c) << (4 * i);
+    const float d = __fsub_rn(w[i], bias);
+    float t = fminf(fmaxf(__fmul_rn(d, inv), -1.0f), 16.0f);
+    const float big = __fadd_rn(t, 12582912.0f);
+    if (fabsf(t - __fsub_rn(big, 12582912.0f)) > 0.5f - 1.52587890625e-05f) {  // 0.5 - 2^-16
+      t = fminf(fmaxf(__fdiv_rn(d, scale), -1.0f), 16.0f);
+      const int c = __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+      packed |= static_cast<uint32_t>(min(max(c, 0), 15)) << (4 * i);
+    } else {
+      const int c = __float_as_int(big) - 0x4B400000;
+      packed |= static_cast<uint32_t>(min(max(c, 0), 15)) << (4 * i);
+    }
   }
   scale_out = scale;
   bias_out = bias;
@@ -122,69 +148,87 @@ __global__ void __launch_bounds__(256) dequantize_kernel(const uint32_t* __restr
   }
 }
 
-// Quantize-on-append: groups are enumerated as [K groups of all (b,h,l)] then [V groups].
+// Quantize-on-append.  An 8-lane team owns one new row (b, h, l): it loads every K and V
+// group of the row (16 bytes per lane per group, all loads issued before any arithmetic),
+// resolves the destination row once, then quantizes and stores group by group.  A warp
+// covers 4 rows; index arithmetic is 32-bit (the launcher refuses more than 2^31 rows).
+constexpr int kMaxGroupsPerRow = 4;  // head dims up to 256
+
 template <bool BF16>
 __global__ void __launch_bounds__(256) append_kernel(AppendParams p) {
   const int lane = threadIdx.x & 31;
   const int team = lane >> 3, sub = lane & 7;
   const int ngk = p.k_dim / kGroup, ngv = p.v_dim / kGroup;
-  const int64_t rows = (int64_t)p.batch * p.hkv * p.n_new;
-  const int64_t gk = rows * ngk;
-  const int64_t n_groups = gk + rows * ngv;
-  const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
-  const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  for (int64_t wg = warp0; wg * 4 < n_groups; wg += warps_total) {
-    int64_t gi = wg * 4 + team;
-    bool active = gi < n_groups;
-    const bool is_v = gi >= gk;
-    const int ng = is_v ? ngv : ngk;
-    const int64_t gl = is_v ? gi - gk : gi;
-    const int64_t row = gl / ng;
-    const int g = static_cast<int>(gl % ng);
-    const int l = static_cast<int>(row % p.n_new);
-    const int h = static_cast<int>((row / p.n_new) % p.hkv);
-    const int b = static_cast<int>(row / ((int64_t)p.n_new * p.hkv));
-    float w[8];
-    if (active) {
-      const uint16_t* src = is_v ? p.v + b * p.vsb + h * p.vsh + l * p.vsl
-                                 : p.k + b * p.ksb + h * p.ksh + l * p.ksl;
-      load8<BF16>(src + g * kGroup + sub * 8, w);
-    } else {
+  const int rows = p.batch * p.hkv * p.n_new;
+  const int warps_total = gridDim.x * (blockDim.x >> 5);
+  const int warp0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int wr = warp0; wr < (rows + 3) / 4; wr += warps_total) {
+    const int row = wr * 4 + team;
+    const bool active = row < rows;
+    const int bh = active ? row / p.n_new : 0;
+    const int l = active ? row - bh * p.n_new : 0;
+    const int b = bh / p.hkv;
+    const int h = bh - b * p.hkv;
+    uint4 rk[kMaxGroupsPerRow], rv[kMaxGroupsPerRow];
+    {
+      const uint16_t* ksrc = p.k + b * p.ksb + h * p.ksh + l * p.ksl + sub * 8;
+      const uint16_t* vsrc = p.v + b * p.vsb + h * p.vsh + l * p.vsl + sub * 8;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) w[i] = 0.0f;
+      for (int g = 0; g < kMaxGroupsPerRow; ++g) {
+        rk[g] = (active && g < ngk) ? __ldg(reinterpret_cast<const uint4*>(ksrc + g * kGroup)) : make_uint4(0, 0, 0, 0);
+        rv[g] = (active && g < ngv) ? __ldg(reinterpret_cast<const uint4*>(vsrc + g * kGroup)) : make_uint4(0, 0, 0, 0);
+      }
     }
-    float s, bias;
-    const uint32_t packed = quantize_team(w, s, bias);
-    if (!active) continue;
-    // destination row
-    const int64_t pos = (int64_t)p.positions[b] + l;
-    int64_t drow;
-    if (p.layout == AM_LAYOUT_PAGED) {
-      const int64_t bi = pos / p.block_tokens;
-      if (pos < 0 || bi >= p.table_stride) {
+    // destination row (-1: skipped and flagged)
+    int64_t drow = -1;
+    if (active) {
+      const int64_t pos = (int64_t)p.positions[b] + l;
+      if (p.layout == AM_LAYOUT_PAGED) {
+        if (pos < 0 || pos / p.block_tokens >= p.table_stride) {
+          if (sub == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
+        } else {
+          const int pi = static_cast<int>(pos);
+          const int bi = pi / p.block_tokens;
+          const int32_t blk = p.table[(int64_t)b * p.table_stride + bi];
+          if (blk < 0 || blk >= p.capacity) {
+            if (sub == 0) flag_status(p.status, AM_STATUS_BAD_BLOCK);
+          } else {
+            drow = ((int64_t)blk * p.hkv + h) * p.block_tokens + (pi - bi * p.block_tokens);
+          }
+        }
+      } else if (pos < 0 || pos >= p.capacity) {
         if (sub == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
-        continue;
+      } else {
+        drow = ((int64_t)b * p.hkv + h) * p.capacity + pos;
       }
-      const int32_t blk = p.table[(int64_t)b * p.table_stride + bi];
-      if (blk < 0 || blk >= p.capacity) {
-        if (sub == 0) flag_status(p.status, AM_STATUS_BAD_BLOCK);
-        continue;
-      }
-      drow = ((int64_t)blk * p.hkv + h) * p.block_tokens + pos % p.block_tokens;
-    } else {
-      if (pos < 0 || pos >= p.capacity) {
-        if (sub == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
-        continue;
-      }
-      drow = ((int64_t)b * p.hkv + h) * p.capacity + pos;
     }
-    uint32_t* codes = is_v ? p.vc : p.kc;
-    uint16_t* scales = is_v ? p.vs : p.ks;
-    uint16_t* biases = is_v ? p.vb : p.kb;
-    codes[drow * (ng * 8) + g * 8 + sub] = packed;
-    if (sub == 0) {
-      scales[drow * ng + g] = f2h<BF16>(s);
-      biases[drow * ng + g] = f2h<BF16>(bias);
+    // every lane of the warp runs every quantize_team (its shuffles use the full mask); the
+    // group counts are the same for all rows
+#pragma unroll
+    for (int g = 0; g < 2 * kMaxGroupsPerRow; ++g) {
+      const bool is_v = g >= kMaxGroupsPerRow;
+      const int gg = is_v ? g - kMaxGroupsPerRow : g;
+      const int ng = is_v ? ngv : ngk;
+      if (gg >= ng) continue;  // uniform across the warp
+      const uint4 raw = is_v ? rv[gg] : rk[gg];
+      const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+      float w[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        w[2 * i] = h2f<BF16>(static_cast<uint16_t>(u[i] & 0xffffu));
+        w[2 * i + 1] = h2f<BF16>(static_cast<uint16_t>(u[i] >> 16));
+      }
+      float sc, bias;
+      const uint32_t packed = quantize_team(w, sc, bias);
+      if (drow < 0) continue;
+      uint32_t* codes = is_v ? p.vc : p.kc;
+      uint16_t* scales = is_v ? p.vs : p.ks;
+      uint16_t* biases = is_v ? p.vb : p.kb;
+      codes[drow * (ng * 8) + gg * 8 + sub] = packed;
+      if (sub == 0) {
+        scales[drow * ng + gg] = f2h<BF16>(sc);
+        biases[drow * ng + gg] = f2h<BF16>(bias);
+      }
     }
   }
 }
@@ -240,7 +284,9 @@ cudaError_t launch_append(const AppendParams& p, bool bf16, cudaStream_t stream)
   const int64_t rows = (int64_t)p.batch * p.hkv * p.n_new;
   const int64_t n_groups = rows * (p.k_dim / kGroup + p.v_dim / kGroup);
   if (n_groups == 0) return cudaSuccess;
-  const int grid = grid_for((n_groups + 3) / 4, 8);
+  if (rows + 3 > INT32_MAX || p.k_dim > kMaxGroupsPerRow * kGroup || p.v_dim > kMaxGroupsPerRow * kGroup)
+    return cudaErrorNotSupported;  // 32-bit row indices; head dims up to 256
+  const int grid = grid_for((rows + 3) / 4, 8);
   if (bf16) {
     append_kernel<true><<<grid, 256, 0, stream>>>(p);
   } else {
