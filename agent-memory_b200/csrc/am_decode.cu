@@ -76,10 +76,13 @@ struct DecodeLayout {
   // The queries are staged (as fp32 when they fit, else as their 16-bit inputs, plus
   // per-group sums and maxima) in the last stage of warp 0's ring, which no copy touches
   // before the main loop starts.
-  static constexpr bool Q32 = 8 * DK * 4 + 2 * 8 * NGK * 4 <= STAGE;
+  // A staged column is padded by 16 bytes, so that the 8 columns' fragment reads (one
+  // column per lane group) fall into different banks.
+  static constexpr bool Q32 = 8 * (DK + 4) * 4 + 2 * 8 * NGK * 4 <= STAGE;
+  static constexpr int QROW = Q32 ? DK + 4 : DK + 8;  // elements per staged column
   static constexpr int OFF_Q = (NS - 1) * STAGE;
-  static constexpr int OFF_QS = OFF_Q + 8 * DK * (Q32 ? 4 : 2);
-  static_assert(8 * DK * 2 + 2 * 8 * NGK * 4 <= STAGE, "query staging must fit in one stage");
+  static constexpr int OFF_QS = OFF_Q + 8 * QROW * (Q32 ? 4 : 2);
+  static_assert(8 * (DK + 8) * 2 + 2 * 8 * NGK * 4 <= STAGE, "query staging must fit in one stage");
   static_assert((16 + 8 * (DV + 1)) * 4 <= RING, "warp result must fit in its ring");
   static_assert((kWarps * 8 + 24) * 4 <= kMaxBlk * 4, "CTA merge factors must fit in the block-id area");
 };
@@ -112,8 +115,16 @@ __device__ __forceinline__ float load_mask(const DecodeParams& p, int b, int hq,
 // more than 2^3 (log2 units), so P <= 8 and P * scale_v stays well inside fp16.
 constexpr float kRescaleSlack = 3.0f;
 
+// Resident CTAs per SM the register allocation aims at: 2 for the largest heads (their
+// output accumulators and query fragments alone take ~100 registers a thread), 3 for the
+// rest, where shared memory allows no more.  (Without the hint the compiler may settle
+// on fewer registers and spill in the streaming loop.)
+template <int DK, int DV>
+constexpr int decode_min_ctas() { return DK + DV >= 512 ? 2 : 3; }
+
 template <int DK, int DV, bool SBF16, bool PAGED, int NS, int TS>
-__global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ DecodeParams p) {
+__global__ void __launch_bounds__(128, decode_min_ctas<DK, DV>())
+    decode_kernel(const __grid_constant__ DecodeParams p) {
   using LY = DecodeLayout<DK, DV, NS, TS>;
   constexpr int NH = TS / 16;  // 16-token MMA tiles per stage
   constexpr int NGK = LY::NGK, NGV = LY::NGV;
@@ -154,6 +165,28 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   const int h0 = hrg / row_groups;
   const int rg = hrg % row_groups;
 
+  // The 8 query columns (16-byte vectors) and the sequence's length are independent
+  // global loads: issue them together so that their latencies overlap (the stage copies
+  // cannot start before the length is known).
+  constexpr int QV = 8 * (DK / 8);  // query vectors of the CTA's 8 columns
+  constexpr int QPT = (QV + 127) / 128;
+  static_assert(QV % 32 == 0, "query vectors fill whole warps");
+  uint4 qraw[QPT];
+#pragma unroll
+  for (int j = 0; j < QPT; ++j) {
+    const int i = tid + 128 * j;
+    qraw[j] = make_uint4(0u, 0u, 0u, 0u);
+    if (QV % 128 == 0 || i < QV) {
+      const int c = i / (DK / 8), c8 = i % (DK / 8);
+      int rr = rg * 8 + c;
+      if (rr >= rph) rr = rph - 1;
+      const int l = rr / p.n_rep;
+      const int hq = h0 * p.n_rep + rr % p.n_rep;
+      qraw[j] = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh +
+                                                (int64_t)l * p.qsl + c8 * 8);
+    }
+  }
+
   const int n = p.kv_len[b];
   const int st = p.kv_start != nullptr ? p.kv_start[b] : 0;
   const bool dense_mask = p.mask_kind != AM_MASK_NONE;
@@ -179,7 +212,6 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   int32_t* tile_ok = reinterpret_cast<int32_t*>(smem + LY::OFF_OK) + warp * NS;
   int32_t* sblk = reinterpret_cast<int32_t*>(smem + LY::OFF_BLK);
   int32_t* col_i = reinterpret_cast<int32_t*>(smem + LY::OFF_COL);           // [8][4]
-  float* col_pw = reinterpret_cast<float*>(smem + LY::OFF_COL + 128);         // [8]
   int64_t* col_oo = reinterpret_cast<int64_t*>(smem + LY::OFF_COL + 160);     // [8]
   int64_t* col_wo = reinterpret_cast<int64_t*>(smem + LY::OFF_COL + 224);     // [8]
   int32_t* col_mask = reinterpret_cast<int32_t*>(smem + LY::OFF_COL + 288);   // [2]
@@ -259,15 +291,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   // Column c of the MMA N dimension is query row rg*8 + c of this KV head (row r = l*n_rep
   // + head offset); columns past the head's rows repeat its last row and are never written.
   const bool qbf = p.q_bf16 != 0;
-  float* qs32 = reinterpret_cast<float*>(smem + LY::OFF_Q);         // [8][DK] fp32, or
-  uint16_t* qs16 = reinterpret_cast<uint16_t*>(smem + LY::OFF_Q);   // [8][DK] 16-bit inputs
-  auto qget = [&](int c, int d) -> float {
-    if constexpr (LY::Q32) {
-      return qs32[c * DK + d];
-    } else {
-      return h2f_rt(qs16[c * DK + d], qbf);
-    }
-  };
+  float* qs32 = reinterpret_cast<float*>(smem + LY::OFF_Q);         // [8][QROW] fp32, or
+  uint16_t* qs16 = reinterpret_cast<uint16_t*>(smem + LY::OFF_Q);   // [8][QROW] 16-bit inputs
   float* qsum_s = reinterpret_cast<float*>(smem + LY::OFF_QS);   // [8][NGK]
   float* qmax_s = qsum_s + 8 * NGK;                              // [8][NGK]
   if (tid < 8) {
@@ -293,72 +318,72 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
       col_mask[1] = p.causal ? min(n, pos_min + 1) : n;
     }
   }
-  for (int i = tid; i < 8 * (DK / 8); i += 128) {
-    const int c = i / (DK / 8), c8 = i % (DK / 8);
-    int rr = rg * 8 + c;
-    if (rr >= rph) rr = rph - 1;
-    const int l = rr / p.n_rep;
-    const int hq = h0 * p.n_rep + rr % p.n_rep;
-    const uint4 raw = *reinterpret_cast<const uint4*>(p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh +
-                                                      (int64_t)l * p.qsl + c8 * 8);
-    if constexpr (LY::Q32) {
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-      float4 lo4, hi4;
-      float* f = &lo4.x;
-      float* h = &hi4.x;
+  // The query vectors to shared memory, with the per (column, 64-dim group) sum and max
+  // |q| reduced over the 8 lanes that hold one group (8 consecutive vectors of a column;
+  // whole warps take part, as QV is a multiple of 32).
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        f[2 * j] = h2f_rt(static_cast<uint16_t>(w[j] & 0xffffu), qbf);
-        f[2 * j + 1] = h2f_rt(static_cast<uint16_t>(w[j] >> 16), qbf);
-        h[2 * j] = h2f_rt(static_cast<uint16_t>(w[2 + j] & 0xffffu), qbf);
-        h[2 * j + 1] = h2f_rt(static_cast<uint16_t>(w[2 + j] >> 16), qbf);
+  for (int j = 0; j < QPT; ++j) {
+    const int i = tid + 128 * j;
+    if (QV % 128 == 0 || i < QV) {
+      const int c = i / (DK / 8), c8 = i % (DK / 8);
+      const uint32_t w[4] = {qraw[j].x, qraw[j].y, qraw[j].z, qraw[j].w};
+      float f[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        f[2 * k] = h2f_rt(static_cast<uint16_t>(w[k] & 0xffffu), qbf);
+        f[2 * k + 1] = h2f_rt(static_cast<uint16_t>(w[k] >> 16), qbf);
       }
-      *reinterpret_cast<float4*>(qs32 + c * DK + c8 * 8) = lo4;
-      *reinterpret_cast<float4*>(qs32 + c * DK + c8 * 8 + 4) = hi4;
-    } else {
-      *reinterpret_cast<uint4*>(qs16 + c * DK + c8 * 8) = raw;
-    }
-  }
-  __syncthreads();
-  {
-    // per (column, 64-dim group) sum and max |q|: 4 threads per pair, 16 dims each
-    constexpr int NQ = 8 * NGK * 4;
-    static_assert(NQ % 32 == 0 && NQ <= 128, "query statistics use whole warps");
-    if (tid < NQ) {
-      const int r = tid / (NGK * 4), G = (tid / 4) % NGK, part = tid % 4;
       float sm = 0.0f, mx = 0.0f;
 #pragma unroll
-      for (int d = 0; d < 16; ++d) {
-        const float v = qget(r, G * 64 + part * 16 + d);
-        sm += v;
-        mx = fmaxf(mx, fabsf(v));
+      for (int k = 0; k < 8; ++k) {
+        sm += f[k];
+        mx = fmaxf(mx, fabsf(f[k]));
       }
 #pragma unroll
-      for (int off = 1; off < 4; off <<= 1) {
+      for (int off = 1; off < 8; off <<= 1) {
         sm += __shfl_xor_sync(0xffffffffu, sm, off);
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       }
-      if (part == 0) {
-        qsum_s[r * NGK + G] = sm;
-        qmax_s[r * NGK + G] = mx;
+      if ((lane & 7) == 0) {
+        qsum_s[c * NGK + c8 / 8] = sm;
+        qmax_s[c * NGK + c8 / 8] = mx;
+      }
+      if constexpr (LY::Q32) {
+        *reinterpret_cast<float4*>(qs32 + c * LY::QROW + c8 * 8) = make_float4(f[0], f[1], f[2], f[3]);
+        *reinterpret_cast<float4*>(qs32 + c * LY::QROW + c8 * 8 + 4) = make_float4(f[4], f[5], f[6], f[7]);
+      } else {
+        *reinterpret_cast<uint4*>(qs16 + c * LY::QROW + c8 * 8) = qraw[j];
       }
     }
   }
   __syncthreads();
-  if (tid < 8) {
-    // power-of-two prescale per column so fp16 MMA operands keep full precision
+  // Power-of-two prescale of a column, so that fp16 MMA operands keep full precision:
+  // 2^(15 - e) for max |q| in [2^(e-1), 2^e), from its exponent field E (e = E - 126),
+  // capped at 2^127 for a tiny or subnormal maximum.
+  auto prescale = [&](int c) -> float {
     float m = 0.0f;
 #pragma unroll
-    for (int G = 0; G < NGK; ++G) m = fmaxf(m, qmax_s[tid * NGK + G]);
-    float pw = 1.0f;
-    if (m > 0.0f && isfinite(m)) {
-      int e;
-      frexpf(m, &e);  // m in [2^(e-1), 2^e)
-      pw = ldexpf(1.0f, 15 - e);
+    for (int G = 0; G < NGK; ++G) m = fmaxf(m, qmax_s[c * NGK + G]);
+    if (!(m > 0.0f) || !isfinite(m)) return 1.0f;
+    const int E = (__float_as_int(m) >> 23) & 0xff;
+    return __int_as_float(min(254, 268 - E) << 23);
+  };
+  // 8 consecutive query values of column c from dim d (d a multiple of 8)
+  auto q8 = [&](int c, int d, float (&f)[8]) {
+    if constexpr (LY::Q32) {
+      const float4 x = *reinterpret_cast<const float4*>(qs32 + c * LY::QROW + d);
+      const float4 y = *reinterpret_cast<const float4*>(qs32 + c * LY::QROW + d + 4);
+      f[0] = x.x, f[1] = x.y, f[2] = x.z, f[3] = x.w, f[4] = y.x, f[5] = y.y, f[6] = y.z, f[7] = y.w;
+    } else {
+      const uint4 r = *reinterpret_cast<const uint4*>(qs16 + c * LY::QROW + d);
+      const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        f[2 * k] = h2f_rt(static_cast<uint16_t>(w[k] & 0xffffu), qbf);
+        f[2 * k + 1] = h2f_rt(static_cast<uint16_t>(w[k] >> 16), qbf);
+      }
     }
-    col_pw[tid] = pw;
-  }
-  __syncthreads();
+  };
 
   // B fragments of Q for S = K . Q^T.  k-step s = 4G + 2j covers words 8G + 2t + j of
   // column g's slots: nibbles (0, 4) feed k-slots 2t, 2t+1 and nibbles (1, 5) feed 2t+8,
@@ -368,24 +393,19 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   // shift and one mask per operand pair.
   uint32_t qf[KSTEPS][2];
   {
-    const float pw = col_pw[g];
+    const float pw = prescale(g);
 #pragma unroll
     for (int G = 0; G < NGK; ++G) {
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int s = 4 * G + 2 * j + e;
-          const int d8 = 8 * (8 * G + 2 * t + j);
-          if (e == 0) {
-            qf[s][0] = pack_half2(qget(g, d8) * pw, qget(g, d8 + 4) * pw);
-            qf[s][1] = pack_half2(qget(g, d8 + 1) * pw * 0.0625f, qget(g, d8 + 5) * pw * 0.0625f);
-          } else {
-            const float q3 = qget(g, d8 + 3) * pw * 0.0625f, q7 = qget(g, d8 + 7) * pw * 0.0625f;
-            qf[s][0] = pack_half2(q3, q7);
-            qf[s][1] = pack_half2(fmaf(qget(g, d8 + 2), pw, -q3), fmaf(qget(g, d8 + 6), pw, -q7));
-          }
-        }
+        const int s = 4 * G + 2 * j;
+        float x[8];
+        q8(g, 8 * (8 * G + 2 * t + j), x);
+        qf[s][0] = pack_half2(x[0] * pw, x[4] * pw);
+        qf[s][1] = pack_half2(x[1] * pw * 0.0625f, x[5] * pw * 0.0625f);
+        const float q3 = x[3] * pw * 0.0625f, q7 = x[7] * pw * 0.0625f;
+        qf[s + 1][0] = pack_half2(q3, q7);
+        qf[s + 1][1] = pack_half2(fmaf(x[2], pw, -q3), fmaf(x[6], pw, -q7));
       }
     }
   }
@@ -412,7 +432,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     const int col = 2 * t + c;
-    fac[c] = 16777216.0f / col_pw[col] * p.scale_log2;  // 2^24 undoes the subnormal code encoding
+    fac[c] = 16777216.0f / prescale(col) * p.scale_log2;  // 2^24 undoes the subnormal code encoding
     hq_c[c] = col_i[col * 4 + 0];
     l_c[c] = col_i[col * 4 + 1];
     pos_c[c] = col_i[col * 4 + 2];
@@ -811,9 +831,9 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
   }
   __syncthreads();
   float* wres0 = reinterpret_cast<float*>(smem);  // warp 0's result
-  for (int i = tid; i < 8 * DV; i += 128) {
+  const int cols = min(8, rph - rg * 8);          // valid columns are 0 .. cols-1
+  for (int i = tid; i < cols * DV; i += 128) {
     const int c = i / DV, d = i % DV;
-    if (!col_i[c * 4 + 3]) continue;
     float O = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w)
@@ -835,56 +855,39 @@ __global__ void __launch_bounds__(128) decode_kernel(const __grid_constant__ Dec
 
   // ------------------------------------------------------------------ cluster merge
   // The max_chunks CTAs of this column group form one cluster; each holds its chunk's
-  // (M, L) in cf and its O in warp 0's result area.  Threads 0..7 turn the cluster's (M, L)
-  // of one column into per-chunk weights and the output factor; then the cluster's CTAs
-  // each write an interleaved share of the output elements, reading the chunks' O through
-  // distributed shared memory.  The second barrier keeps every CTA (and its shared memory)
-  // alive until all peers are done reading it.
+  // (M, L) in cf and its O in warp 0's result area.  After the first cluster barrier the
+  // CTAs each write an interleaved share of the output elements: a thread reads every
+  // chunk's (M, L) of its column and O of its element through distributed shared memory
+  // in one round (all loads independent), then merges them.  The second barrier keeps
+  // every CTA (and its shared memory) alive until all peers are done reading it.
   cluster_sync_all();
   const int nc = p.max_chunks;
-  float* cw = reinterpret_cast<float*>(smem + LY::RING);  // warp 1's ring: [8][kMaxCluster] weights, [8] factors
-  if (tid < 8) {
-    const int c = tid;
+  const uint32_t o_loc = smem_u32(wres0 + 16);
+  const bool sink = p.sinks != nullptr;
+  for (int i = chunk * 128 + tid; i < cols * DV; i += nc * 128) {
+    const int c = i / DV, d = i % DV;
     const uint32_t m_loc = smem_u32(cf + kWarps * 8 + c), l_loc = smem_u32(cf + kWarps * 8 + 8 + c);
-    float mj[kMaxCluster], lj[kMaxCluster];
+    const uint32_t a = o_loc + (c * OS + d) * 4;
+    float mj[kMaxCluster], lj[kMaxCluster], xj[kMaxCluster];
 #pragma unroll
     for (int j = 0; j < kMaxCluster; ++j) {
       mj[j] = j < nc ? ld_dsmem_f32(dsmem_addr(m_loc, j)) : -INFINITY;
       lj[j] = j < nc ? ld_dsmem_f32(dsmem_addr(l_loc, j)) : 0.0f;
+      xj[j] = j < nc ? ld_dsmem_f32(dsmem_addr(a, j)) : 0.0f;
     }
     float M = -INFINITY;
 #pragma unroll
     for (int j = 0; j < kMaxCluster; ++j) M = fmaxf(M, mj[j]);
-    float L = 0.0f;
+    float L = 0.0f, O = 0.0f;
 #pragma unroll
     for (int j = 0; j < kMaxCluster; ++j) {
+      // a chunk with no visible key (M = -inf) has weight 0 and contributes nothing
       const float w = mj[j] == -INFINITY ? 0.0f : ex2(mj[j] - M);
-      cw[c * kMaxCluster + j] = w;
       L = fmaf(lj[j], w, L);
+      O = w != 0.0f ? fmaf(xj[j], w, O) : O;
     }
-    const bool sink = p.sinks != nullptr;
-    cw[8 * kMaxCluster + c] =
-        softmax_out_factor(M, L, sink, sink ? p.sinks[col_i[c * 4 + 0]] * 1.4426950408889634f : 0.0f);
-  }
-  __syncthreads();
-  const int cols = min(8, rph - rg * 8);  // valid columns are 0 .. cols-1
-  const uint32_t o_loc = smem_u32(wres0 + 16);
-  for (int i = chunk * 128 + tid; i < cols * DV; i += nc * 128) {
-    const int c = i / DV, d = i % DV;
-    const uint32_t a = o_loc + (c * OS + d) * 4;
-    const float* wc = cw + c * kMaxCluster;
-    float O = 0.0f;
-#pragma unroll
-    for (int j0 = 0; j0 < kMaxCluster; j0 += 8) {
-      if (j0 >= nc) break;
-      float x[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        x[j] = (j0 + j < nc && wc[j0 + j] != 0.0f) ? ld_dsmem_f32(dsmem_addr(a, j0 + j)) : 0.0f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) O = fmaf(x[j], wc[j0 + j], O);
-    }
-    store_out(p.out, col_oo[c] + d, O * cw[8 * kMaxCluster + c], p.out_dtype);
+    const float f = softmax_out_factor(M, L, sink, sink ? p.sinks[col_i[c * 4 + 0]] * 1.4426950408889634f : 0.0f);
+    store_out(p.out, col_oo[c] + d, O * f, p.out_dtype);
   }
   cluster_sync_all();
 }
@@ -1118,7 +1121,9 @@ static cudaError_t set_smem_once(F kfn, int bytes, unsigned long long* done_mask
 // Stage geometry of an instantiation: 64-token stages when a token row of K and V is
 // small (Dk + Dv <= 256), so the per-stage work (copy issue, barrier wait, softmax max)
 // is spread over more tokens; 32-token stages for larger heads.  Three stages per warp
-// when a stage is at most 6 KB, else two.
+// when a stage is at most 6 KB, else two.  (Head dims 256/256 measured no faster with
+// three 9 KB stages: at 2 CTAs per SM their stage time is set by instruction issue, not
+// by the copies in flight.)
 template <int DK, int DV>
 struct DecodeCfg {
   static constexpr int TS = DK + DV <= 256 ? 64 : 32;

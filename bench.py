@@ -9,8 +9,10 @@ then split-KV decode attention of every agent over its blocks.  Agents are parti
 across ranks by balanced token count (greedy LPT); there is no collective on the data
 path (strong scaling: the 256 agents are fixed, each rank decodes its share).
 
-Other workloads (--workload): llama_layer, gemma, mla, prefill — the remaining shapes of
-the attention path, for their own measurement lines.
+Other workloads (--workload): llama_layer, gemma, mla (single-instance decode), prefill
+(Llama chunked prefill), gemma_prefill, mla_prefill (512-token chunks on the Gemma-3 and
+MLA geometries) — the remaining shapes of the attention path, for their own measurement
+lines; the default run also reports each of them under "configs".
 
 `python bench.py --impl reference` times the CPU restatement of the same computation (the
 reference's own MLX CPU path cannot run here: mlx is not installed) on a bounded sample.
@@ -45,7 +47,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", default="multi_agent",
-                   choices=["multi_agent", "llama_layer", "gemma", "mla", "prefill"])
+                   choices=["multi_agent", "llama_layer", "gemma", "mla", "prefill",
+                            "gemma_prefill", "mla_prefill"])
     p.add_argument("--agents", type=int, default=256)
     p.add_argument("--layers", type=int, default=None)
     p.add_argument("--min-len", type=int, default=1024)
@@ -408,7 +411,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize(dev)
         torch.cuda.empty_cache()
         sub = {w: measure_config(w, am, dev, steps=args.config_steps, warmup=3, seed=args.seed)
-               for w in ("llama_layer", "gemma", "mla", "prefill")}
+               for w in ("llama_layer", "gemma", "mla", "prefill", "gemma_prefill", "mla_prefill")}
 
     if rank == 0:
         line = {
@@ -449,13 +452,14 @@ def run_ours(args, rank, world, local_rank):
 def measure_config(w, am, dev, steps=5, warmup=3, seed=0):
     """One of the single-instance configurations, timed on this GPU; returns its record.
 
-    llama_layer / gemma / mla: decode attention over a contiguous Q4 cache (configs 1-3),
+    llama_layer / gemma / mla: decode attention over a contiguous Q4 cache (one Llama layer,
+    the Gemma-3 step, the MLA step),
     the whole step (every layer or rotating instance) captured in one CUDA graph, so the
     time is device time; per-call time = step / calls.
-    prefill (config 4): per layer, the 512-token chunk's K/V quantized and appended into
-    256-token pool blocks at shuffled offsets (am_q4_append), then causal attention of the
-    chunk over the 4096-token prefix plus itself (am_q4_prefill: dequantize stage + tcgen05
-    attention); launched eagerly with CUDA events around every call.
+    prefill / gemma_prefill / mla_prefill: per layer, a 512-token chunk's K/V quantized and
+    appended into 256-token pool blocks at shuffled offsets (am_q4_append), then causal
+    attention of the chunk over the cached prefix plus itself (am_q4_prefill: dequantize
+    stage + tcgen05 attention); launched eagerly with CUDA events around every call.
     """
     import torch
 
@@ -472,8 +476,8 @@ def measure_config(w, am, dev, steps=5, warmup=3, seed=0):
         B, layers, N, L = 16, MLA["layers"], 8192, 1
         hq, hkv, dk, dv, window = 16, 16, 192, 128, 0
         reps = 1
-    elif w == "prefill":
-        return measure_prefill(am, dev, steps, warmup, gen)
+    elif w in PREFILL_SHAPES:
+        return measure_prefill(am, dev, steps, warmup, gen, w)
     else:
         raise ValueError(w)
     inst = layers * reps
@@ -545,19 +549,32 @@ def measure_config(w, am, dev, steps=5, warmup=3, seed=0):
             "gpu_launches": steps * launches, "clocks": clk}
 
 
-def measure_prefill(am, dev, steps, warmup, gen):
-    """Config 4: chunked prefill of a 512-token bf16 chunk over a 4096-token Q4 prefix."""
+PREFILL_SHAPES = {
+    # 512-token bf16 chunks over a cached Q4 prefix, one per model geometry
+    "prefill": dict(model="Llama-3.1-8B", B=2, P=4096, window=0, global_every=1, **LLAMA),
+    "gemma_prefill": dict(model="Gemma-3-12B", B=8, P=4096, **GEMMA),
+    "mla_prefill": dict(model="DeepSeek-Coder-V2-Lite (MLA)", B=16, P=8192, window=0,
+                        global_every=1, **MLA),
+}
+
+
+def measure_prefill(am, dev, steps, warmup, gen, workload="prefill"):
+    """Chunked prefill of a 512-token bf16 chunk over a cached Q4 prefix (one geometry)."""
     import torch
 
-    B, layers, P, L = 2, LLAMA["layers"], 4096, 512
-    hq, hkv, dk, dv = LLAMA["hq"], LLAMA["hkv"], LLAMA["dk"], LLAMA["dv"]
+    g = PREFILL_SHAPES[workload]
+    B, layers, P, L = g["B"], g["layers"], g["P"], 512
+    hq, hkv, dk, dv = g["hq"], g["hkv"], g["dk"], g["dv"]
+    window, every = g["window"], g["global_every"]
+    is_global = [window == 0 or (l % every) == every - 1 for l in range(layers)]
     N, bt = P + L, 256
     spec = am.ModelCacheSpec(n_layers=layers, n_kv_heads=hkv, head_dim=dk, block_tokens=bt,
                              layer_types=["global"] * layers)
     blocks = layers * B * (-(-N // bt))
     alloc = am.shuffled_allocator(spec, blocks, seed=7)
-    pool = am.PagedQ4Pool.for_spec(spec, blocks, torch.bfloat16, dev)
-    caches = [am.PagedLayerCache(pool, alloc, l, ["a0", "a1"], N) for l in range(layers)]
+    pool = am.PagedQ4Pool(hkv, dk, dv, blocks, bt, torch.bfloat16, dev)
+    caches = [am.PagedLayerCache(pool, alloc, l, [f"a{r}" for r in range(B)], N)
+              for l in range(layers)]
     bf = torch.bfloat16
     for c in caches:
         c.append(torch.randn(B, hkv, P, dk, generator=gen, device=dev, dtype=bf),
@@ -582,7 +599,7 @@ def measure_prefill(am, dev, steps, warmup, gen):
             if ev is not None:
                 ev[l][1].record(stream)
             am.kernels.attention(views[l], q[l], dk ** -0.5, kv_len, N, causal=True, out=out[l],
-                                 mode="prefill")
+                                 window=0 if is_global[l] else window, mode="prefill")
             if ev is not None:
                 ev[l][2].record(stream)
 
@@ -606,19 +623,28 @@ def measure_prefill(am, dev, steps, warmup, gen):
     app_ms = float(np.mean([evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(steps)
                             for l in range(layers)]))
     hbm, _, tf_sus, kind = peaks()
-    flops = 4 * B * hq * dk * (L * P + L * (L + 1) / 2)
+    # visible (query, key) pairs per (sequence, head): causal over prefix + chunk, and for a
+    # window layer only the last `window` positions up to each query
+    def pairs(w):
+        return sum(min(P + i + 1, w) if w else P + i + 1 for i in range(L))
+    flops = sum(2 * B * hq * (dk + dv) * pairs(0 if is_global[l] else window)
+                for l in range(layers)) / layers
     app_bytes = B * hkv * L * (2 * (dk + dv) + q4_bytes_per_token(1, dk, dv))
     del caches, views, pool, kc, vc, q, out
     torch.cuda.empty_cache()
     return {"metric": "prefill tokens/s", "value": round(B * L / (ms / 1e3), 2), "unit": "tokens/s",
             "ms_per_step": round(ms, 4), "steps": steps, "dtype": "bf16",
-            "config": {"workload": "prefill", "batch": B, "layers": layers, "prefix": P, "q_len": L,
-                       "n_q_heads": hq, "n_kv_heads": hkv, "k_dim": dk, "v_dim": dv,
+            "config": {"workload": workload, "model_shape": g["model"], "batch": B,
+                       "layers": layers, "prefix": P, "q_len": L, "n_q_heads": hq,
+                       "n_kv_heads": hkv, "k_dim": dk, "v_dim": dv,
+                       "window": window, "global_layers": sum(is_global),
                        "cache": "256-token paged blocks at shuffled offsets",
                        "step": "per layer: append the chunk (am_q4_append) + causal attention "
                                "(am_q4_prefill)",
                        "timing": "eager launches, CUDA events around every call"},
-            "roofline": {"kernel": "am_q4_prefill (prefill_stage_kernel + prefill2_kernel)",
+            "roofline": {"kernel": "am_q4_prefill (prefill_stage_kernel + %s)" % (
+                             "prefill2_kernel" if dk <= 128 and dv <= 128 else "prefill_kernel"),
+                         "flops_per_launch_note": "layer mean of 2 * B * Hq * (Dk + Dv) * visible pairs",
                          "bound": "tensor", "achieved": round(flops / (attn_ms / 1e3) / 1e12, 2),
                          "peak": tf_sus, "peak_kind": kind + " sustained bf16", "unit": "TFLOP/s",
                          "frac": round(flops / (attn_ms / 1e3) / 1e12 / tf_sus, 4),
@@ -634,7 +660,8 @@ def measure_prefill(am, dev, steps, warmup, gen):
 
 
 def run_single_workload(args, am, dev, rank, world):
-    """Configs 1-4 on their own (replicas across ranks: every rank runs the same instance)."""
+    """One single-instance workload on its own (replicas across ranks: every rank runs the
+    same instance)."""
     import torch
     import torch.distributed as dist
 

@@ -44,7 +44,7 @@ def oracle(orc, q, kq, vq, scale, **kw):
 
 GEOMS = [
     # (B, Hq, Hkv, N, dk, dv)
-    (2, 32, 8, 2048, 128, 128),   # Llama-3.1-8B layer, config 1 shape
+    (2, 32, 8, 2048, 128, 128),   # one Llama-3.1-8B layer at its benchmark shape
     (3, 16, 8, 777, 256, 256),    # Gemma-3 geometry
     (2, 16, 16, 1500, 192, 128),  # DeepSeek-V2 MLA (n_rep 1)
     (2, 8, 4, 333, 128, 64),      # asymmetric K/V
