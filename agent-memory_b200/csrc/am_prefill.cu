@@ -10,31 +10,32 @@
 //    and rounded once to fp16 (saturating at +-65504).  HBM-bound: reads Dk/2 + Dk/16 +
 //    Dv/2 + Dv/16 bytes and writes 2 (Dk + Dv) bytes per (key, KV head).
 //
-// 2. prefill_kernel: one CTA = 128 query rows of one KV head of one sequence.  Rows are
-//    (token, GQA head) pairs, token-major: 128 / n_rep query tokens times the n_rep heads
-//    that share the KV head, so each K/V tile feeds all of them.  4 CG + 2 warps, CG = BN / 32
-//    (576 threads for 128-key tiles, 320 for the 64-key tiles of head dim 256):
-//    * one thread of warp 4 CG streams BN-key tiles of K and V from the workspace into
+// 2. The attention kernel streams the fp16 planes.  Query rows are (token, GQA head) pairs,
+//    token-major, so each K/V tile feeds the n_rep heads that share its KV head.  Two
+//    variants, chosen by head dims:
+//    * prefill2_kernel (Dk, Dv <= 128): one CTA = two 128-row query tiles of one KV head of
+//      one sequence, 320 threads.  One thread of warp 8 streams 128-key K and V tiles into
 //      NS-stage shared-memory rings with 2-D tensor-map TMA loads (128-byte swizzle, no
-//      multicast);
-//    * one thread of warp 4 CG + 1 issues every MMA: S_j = Q . K_j^T (tcgen05.mma kind::f16,
-//      M = 128, N = BN, 16-deep K steps) into TMEM S[j % 2], then O += P_{j-1} . V_{j-1} with
-//      P read from TMEM, so the tensor core computes S_j while the softmax warps work on tile
-//      j-1;
-//    * softmax warps 0 .. 4 CG - 1: warp w owns TMEM lanes 32 (w % 4) .. +31 (one query row
-//      per thread) and key columns 32 (w / 4) .. +31 of each tile; tcgen05.ld of its 32
-//      scores, row maxima exchanged among the quarter's CG warps through shared memory, fp32
-//      online softmax, P as fp16 pairs stored back over the warp's own S columns
-//      (tcgen05.st); O rows rescaled in TMEM only when the running max moves by more than
-//      2^8.  A fixed share of the exponentials runs as a polynomial on the FMA pipe instead
-//      of the MUFU unit (ex2_fma below), which the other share saturates otherwise.
-//    mbarriers chain the stages: TMA completions (K/V full), MMA commits (S full, S free,
-//    O full, K/V empty) and the softmax threads' arrivals (P full).  TMEM: S x2 + O (512
-//    columns, one CTA per SM).  Operands are fp16: queries (fp16 or bf16) are rescaled per
-//    row by a power of two so their conversion is exact.  Every wait is bounded
-//    (DecodeParams::wait_ns, 2 s); on timeout the kernel flags AM_STATUS_TIMEOUT, stops
-//    issuing work, waits (bounded) for its TMA loads and MMAs in flight, frees its TMEM and
-//    returns.
+//      multicast); one thread of warp 9 issues every tcgen05.mma (kind::f16, M = 128,
+//      N = 128, 16-deep steps): S = Q . K^T into TMEM S[qt], then O[qt] += P . V with P read
+//      from TMEM, alternating the tiles (S0_i, PV1_{i-1}, S1_i, PV0_i) so the tensor core
+//      works on one tile while the softmax warps of the other run; softmax warps 0-7, four
+//      per tile, one thread per query row and all 128 key columns of a tile.
+//    * prefill_kernel (MLA 192/128 and Gemma-3 256/256, whose two tiles do not fit in TMEM):
+//      one CTA = one 128-row query tile, 320 threads; BN-key tiles (128, or 64 for Dk + Dv >
+//      384); 8 softmax warps, two per TMEM lane quarter, each owning BN / 2 key columns of
+//      every tile and exchanging row maxima with its partner through shared memory; the
+//      tensor core computes S_j while the softmax warps work on tile j-1.
+//    Both: tcgen05.ld of the scores, fp32 online softmax, P as fp16 pairs stored back over
+//    the S columns (tcgen05.st); O rows rescaled in TMEM only when the running max moves by
+//    more than 2^8.  A fixed share of the exponentials runs as a polynomial on the FMA pipe
+//    instead of the MUFU unit (ex2_fma below), which the other share saturates otherwise.
+//    mbarriers chain the stages: TMA completions (K/V full), MMA commits (S full, O full,
+//    K/V empty) and the softmax threads' arrivals (P full).  TMEM: 512 columns, one CTA per
+//    SM.  Operands are fp16: queries (fp16 or bf16) are rescaled per row by a power of two
+//    so their conversion is exact.  Every wait is bounded (DecodeParams::wait_ns, 2 s); on
+//    timeout the kernel flags AM_STATUS_TIMEOUT, stops issuing work, waits (bounded) for
+//    its TMA loads and MMAs in flight, frees its TMEM and returns.
 //
 // The attention grid is launched with programmatic stream serialization: its prologue (TMEM
 // allocation, barriers, the query tile) overlaps the end of the stage kernel, and the TMA
@@ -1417,7 +1418,7 @@ bool prefill_supported(int k_dim, int v_dim) {
          (k_dim == 192 && v_dim == 128) || (k_dim == 256 && v_dim == 256);
 }
 
-// Head dims up to 128 take the two-tile kernel (64-key tiles); the others the one-tile kernel.
+// Head dims up to 128 take the two-tile kernel (128-key tiles); the others the one-tile kernel.
 static bool prefill_two_tiles(int k_dim, int v_dim) { return k_dim <= 128 && v_dim <= 128; }
 
 int prefill_key_tile(int k_dim, int v_dim) {
