@@ -297,6 +297,13 @@ __device__ __forceinline__ void prefill_block_range(const DecodeParams& p, int b
 // bias) before converting any, so enough bytes are in flight to stream at HBM speed.
 constexpr int kStageRows = 128;
 
+// One 32-byte store of 8 words (p 32-byte aligned).
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&v)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 template <int DK, int DV, bool SBF16, bool PAGED>
 __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constant__ DecodeParams p) {
   griddep_launch_dependents();
@@ -362,24 +369,31 @@ __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constan
     uint16_t* dst = c < CK ? p.kd + plane_row * DK + c * 32 : p.vd + plane_row * DV + (c - CK) * 32;
     const float s = h2f<SBF16>(sc[k]), bias = h2f<SBF16>(bi[k]);
     const uint32_t w[4] = {code[k].x, code[k].y, code[k].z, code[k].w};
+    // the chunk's 64 output bytes as two 32-byte stores: each one writes whole sectors
+    // (dst is 64-byte aligned: planes start on 256 bytes, rows and chunks are 64-byte
+    // multiples)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t o[4] = {0u, 0u, 0u, 0u};
+    for (int half = 0; half < 2; ++half) {
+      uint32_t o[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
       if (live[k]) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          // a code OR-ed into the mantissa of 2^23 is exactly 2^23 + code (no int->float
-          // conversion on the XU pipe)
-          const float c0 = __int_as_float(0x4B000000 | ((w[q] >> (8 * e)) & 15u)) - 8388608.0f;
-          const float c1 = __int_as_float(0x4B000000 | ((w[q] >> (8 * e + 4)) & 15u)) - 8388608.0f;
-          float x0 = fmaf(c0, s, bias);
-          float x1 = fmaf(c1, s, bias);
-          x0 = fminf(fmaxf(x0, -65504.0f), 65504.0f);
-          x1 = fminf(fmaxf(x1, -65504.0f), 65504.0f);
-          o[e] = pack_half2(x0, x1);
+        for (int qq = 0; qq < 2; ++qq) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            // a code OR-ed into the mantissa of 2^23 is exactly 2^23 + code (no int->float
+            // conversion on the XU pipe)
+            const uint32_t wq = w[2 * half + qq];
+            const float c0 = __int_as_float(0x4B000000 | ((wq >> (8 * e)) & 15u)) - 8388608.0f;
+            const float c1 = __int_as_float(0x4B000000 | ((wq >> (8 * e + 4)) & 15u)) - 8388608.0f;
+            float x0 = fmaf(c0, s, bias);
+            float x1 = fmaf(c1, s, bias);
+            x0 = fminf(fmaxf(x0, -65504.0f), 65504.0f);
+            x1 = fminf(fmaxf(x1, -65504.0f), 65504.0f);
+            o[4 * qq + e] = pack_half2(x0, x1);
+          }
         }
       }
-      reinterpret_cast<uint4*>(dst)[q] = make_uint4(o[0], o[1], o[2], o[3]);
+      st_global_v8(dst + 16 * half, o);
     }
   }
 }
