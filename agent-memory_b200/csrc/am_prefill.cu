@@ -529,13 +529,15 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  // Grid (KV head, sequence, query tile) with the query tile slowest and reversed: under
-  // the causal mask later query tiles see more keys, so the heaviest CTAs are dispatched
-  // first and the lightest fill the last wave.
-  const int h = blockIdx.x, b = blockIdx.y;
+  // Grid (query tile, KV head, sequence) with the query tile fastest: the CTAs that stream
+  // the same K/V plane run side by side, so each tile of the plane comes from DRAM once and
+  // from L2 for the others (with the query tile slowest, a plane larger than a share of L2
+  // was read from DRAM once per query tile).  Reversed, so the causal tiles that see the
+  // most keys start first.
+  const int h = blockIdx.y, b = blockIdx.z;
   const int n_rep = p.n_rep;
   const int tok_per_cta = 128 / n_rep;
-  const int l0 = (gridDim.z - 1 - blockIdx.z) * tok_per_cta;
+  const int l0 = (gridDim.x - 1 - blockIdx.x) * tok_per_cta;
   const int l_last = min(l0 + tok_per_cta, p.q_len) - 1;
 
   const int n = p.kv_len[b];
@@ -1009,12 +1011,13 @@ __global__ void __launch_bounds__(kTile2Threads, 1) prefill2_kernel(const __grid
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  // Grid (KV head, sequence, query block) with the query block slowest and reversed: under
-  // the causal mask later blocks see more keys, so the heaviest CTAs are dispatched first.
-  const int h = blockIdx.x, b = blockIdx.y;
+  // Grid (query block, KV head, sequence) with the query block fastest, so the CTAs that
+  // stream the same K/V plane run side by side and share its tiles through L2; reversed, so
+  // the causal blocks that see the most keys start first.
+  const int h = blockIdx.y, b = blockIdx.z;
   const int n_rep = p.n_rep;
   const int tpq = 128 / n_rep;  // query tokens per query tile
-  const int l0 = (gridDim.z - 1 - blockIdx.z) * 2 * tpq;
+  const int l0 = (gridDim.x - 1 - blockIdx.x) * 2 * tpq;
   const int l_last = min(l0 + 2 * tpq, p.q_len) - 1;
 
   const int n = p.kv_len[b];
@@ -1480,7 +1483,7 @@ static cudaError_t launch_attn_t(const DecodeParams& p, int batch, cudaStream_t 
     cudaError_t e = prefill_smem_once(kfn, C::LY::SMEM, &done);
     if (e != cudaSuccess) return e;
     const int tok_per_cta = 2 * (128 / p.n_rep);
-    cfg.gridDim = dim3(p.hkv, batch, (p.q_len + tok_per_cta - 1) / tok_per_cta);
+    cfg.gridDim = dim3((p.q_len + tok_per_cta - 1) / tok_per_cta, p.hkv, batch);
     cfg.blockDim = dim3(kTile2Threads);
     cfg.dynamicSmemBytes = C::LY::SMEM;
   } else {
@@ -1490,7 +1493,7 @@ static cudaError_t launch_attn_t(const DecodeParams& p, int batch, cudaStream_t 
     cudaError_t e = prefill_smem_once(kfn, C::LY::SMEM, &done);
     if (e != cudaSuccess) return e;
     const int tok_per_cta = 128 / p.n_rep;
-    cfg.gridDim = dim3(p.hkv, batch, (p.q_len + tok_per_cta - 1) / tok_per_cta);
+    cfg.gridDim = dim3((p.q_len + tok_per_cta - 1) / tok_per_cta, p.hkv, batch);
     cfg.blockDim = dim3(SoftmaxGeom<C::BN>::CTA_THREADS);
     cfg.dynamicSmemBytes = C::LY::SMEM;
   }
