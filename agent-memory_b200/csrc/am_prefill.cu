@@ -431,12 +431,12 @@ struct PrefillLayout {
   static constexpr int OFF_QF = OFF_V + NS * VSTAGE;  // per-row query factor (128 floats)
   static constexpr int OFF_RX = OFF_QF + 128 * 4;     // row exchange between column groups [CG][128]
   static constexpr int OFF_BAR = OFF_RX + CG * 128 * 4;
-  // mbarriers: K full / empty, V full / empty (NS each), S full x2, S free x2, P full x2,
-  // O full x2, drain.  Every barrier that completes once per tile alternates between two
-  // copies by tile parity, so a parity wait can never be satisfied by the phase of the
-  // tile before last.
+  // mbarriers: K full / empty, V full / empty (NS each), S full x2, P full x2, O full x2,
+  // drain.  Every barrier that completes once per tile alternates between two copies by
+  // tile parity, so a parity wait can never be satisfied by the phase of the tile before
+  // last.
   static constexpr int B_KFULL = 0, B_KEMPTY = NS, B_VFULL = 2 * NS, B_VEMPTY = 3 * NS;
-  static constexpr int B_SFULL = 4 * NS, B_SFREE = B_SFULL + 2, B_PFULL = B_SFREE + 2;
+  static constexpr int B_SFULL = 4 * NS, B_PFULL = B_SFULL + 2;
   static constexpr int B_OFULL = B_PFULL + 2, B_DRAIN = B_OFULL + 2, B_COUNT = B_DRAIN + 1;
   static constexpr int SMEM = OFF_BAR + B_COUNT * 8 + 16;  // + TMEM slot and abort flag
   static constexpr uint32_t TMEM_COLS = 512;  // S x2 (2 BN) + O (DV)
@@ -657,8 +657,9 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
         if (j < n_tiles) {
           const int s = j % NS, buf = j & 1;
           ok = wait_or_abort(bar(LY::B_KFULL + s), (j / NS) & 1, p.wait_ns, abort_flag);
-          // S[buf] still holds P of tile j - 2 until its P . V has completed
-          if (ok && j >= 2) ok = wait_or_abort(bar(LY::B_SFREE + buf), ((j - 2) >> 1) & 1, p.wait_ns, abort_flag);
+          // S[buf] holds P of tile j - 2: the P . V that reads it was issued before (in the
+          // previous iteration), and tcgen05.mma operations from one thread execute in issue
+          // order, so S_j is issued without waiting for that P . V to complete
           if (!ok) break;
           tc::fence_after();
           const uint32_t kst = sK + s * LY::KSTAGE;
@@ -689,7 +690,6 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
                        tc::sdesc(vst + ks * 2048, LY::VSLAB, 1024), ID_O, (jj > 0 || ks > 0) ? 1u : 0u);
           }
           tc::commit(bar(LY::B_OFULL + buf));
-          tc::commit(bar(LY::B_SFREE + buf));
           tc::commit(bar(LY::B_VEMPTY + s));
         }
       }
