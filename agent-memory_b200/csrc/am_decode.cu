@@ -119,8 +119,9 @@ constexpr float kRescaleSlack = 3.0f;
 // output accumulators and query fragments alone take ~100 registers a thread), 3 for the
 // rest, where shared memory allows no more.  (Without the hint the compiler may settle
 // on fewer registers and spill in the streaming loop.)
+constexpr int kDecodeMinCtas = 3;
 template <int DK, int DV>
-constexpr int decode_min_ctas() { return DK + DV >= 512 ? 2 : 3; }
+constexpr int decode_min_ctas() { return DK + DV >= 512 ? 2 : kDecodeMinCtas; }
 
 template <int DK, int DV, bool SBF16, bool PAGED, int NS, int TS>
 __global__ void __launch_bounds__(128, decode_min_ctas<DK, DV>())
@@ -1009,6 +1010,9 @@ bool decode_supported(int k_dim, int v_dim) {
 // chunks form one thread-block cluster and all clusters are resident at once, inside the
 // cluster (*cluster = 1: ~64 tokens' worth plus 12 per chunk read, no workspace).  Cluster CTAs are held until the whole cluster is done,
 // so a grid of several waves keeps the workspace merge.
+// Fixed per-CTA cost of a decode chunk in the split planner, in streamed tokens' worth.
+constexpr int kPlanFixedTokens = 256;
+
 void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_per_sm, int k_dim,
                  int v_dim, int* chunk, int* n_chunks, int* cluster) {
   int dev = 0, sms = 148;
@@ -1025,7 +1029,7 @@ void decode_plan(int batch, int n_kv_heads, int row_groups, int span, int ctas_p
     c = (c + 63) / 64 * 64;
     return c < 128 ? (int64_t)128 : (c > cap ? cap : c);
   };
-  constexpr int64_t kFixed = 256, kCombine = 320, kClusterMerge = 64, kClusterPerChunk = 12;
+  constexpr int64_t kFixed = kPlanFixedTokens, kCombine = 320, kClusterMerge = 64, kClusterPerChunk = 12;
   // the 4 warps of a CTA stream stages in parallel, so a partial round of 4 stages costs
   // about half a round more than its tokens (measured: 2-stage chunks take most of a
   // 4-stage chunk's time)
@@ -1118,6 +1122,9 @@ static cudaError_t set_smem_once(F kfn, int bytes, unsigned long long* done_mask
   return e;
 }
 
+// Largest stage (bytes) that gets a 3-stage ring per warp.
+constexpr int kDecodeNs3MaxStage = 6144;
+
 // Stage geometry of an instantiation: 64-token stages when a token row of K and V is
 // small (Dk + Dv <= 256), so the per-stage work (copy issue, barrier wait, softmax max)
 // is spread over more tokens; 32-token stages for larger heads.  Three stages per warp
@@ -1127,7 +1134,7 @@ static cudaError_t set_smem_once(F kfn, int bytes, unsigned long long* done_mask
 template <int DK, int DV>
 struct DecodeCfg {
   static constexpr int TS = DK + DV <= 256 ? 64 : 32;
-  static constexpr int NS = DecodeLayout<DK, DV, 3, TS>::STAGE <= 6144 ? 3 : 2;
+  static constexpr int NS = DecodeLayout<DK, DV, 3, TS>::STAGE <= kDecodeNs3MaxStage ? 3 : 2;
   using LY = DecodeLayout<DK, DV, NS, TS>;
 };
 
