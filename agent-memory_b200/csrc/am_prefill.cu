@@ -244,8 +244,11 @@ __device__ __forceinline__ float ex2_fma(float x) {
 // The same on a pair of values with the packed fp32x2 FMA pipe operations of sm_100 (two
 // lanes per instruction for the range reduction and the polynomial).
 __device__ __forceinline__ float2 ex2_fma2(float2 x) {
-  x.x = fmaxf(x.x, -125.0f);
-  x.y = fmaxf(x.y, -125.0f);
+  // clamped to [-125, 64]: the exponent add below stays inside the float's exponent range
+  // (a larger argument, possible against a running max that has fallen behind, must give a
+  // large value, not a wrapped one)
+  x.x = fminf(fmaxf(x.x, -125.0f), 64.0f);
+  x.y = fminf(fmaxf(x.y, -125.0f), 64.0f);
   const float2 big = make_float2(12582912.0f, 12582912.0f);
   const float2 t = __fadd2_rn(x, big);
   const float2 j = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
@@ -267,10 +270,13 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 
 // Exponentials of softmax element pairs (2c, 2c+1): with kFmaExpEvery > 0, pairs with
 // c % kFmaExpEvery == kFmaExpEvery - 1 go through the FMA-pipe polynomial, the rest through
-// the MUFU unit; 0 keeps every exponential on the MUFU unit.  One thread per query row puts
-// 128 exponentials per tile on its sub-partition's MUFU; a quarter on the FMA pipe measured
-// best (655 TFLOP/s against 645 with none and 632 with half).
+// the MUFU unit; 0 keeps every exponential on the MUFU unit.  One-tile kernel: a quarter on
+// the FMA pipe.  Two-tile kernel (one thread per query row, 128 exponentials per tile): a
+// quarter measured best while every tile also took a max pass (655 TFLOP/s against 645 with
+// none and 632 with half); with the one-pass softmax all on the MUFU unit measures best (700
+// against 686 with a quarter and 679 with a third).
 constexpr int kFmaExpEvery = 4;
+constexpr int kTile2FmaExpEvery = 0;
 
 // Lazy rescaling: a row's running max is raised only when a tile's max exceeds it by more
 // than 2^8 (log2 units), so P <= 256 (exact range for the fp16 P operand) and the O
@@ -928,27 +934,28 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
   }
 }
 
-// Two-tile softmax: issue the TMEM load of a row's second half before processing the first
-// (1), or load each half right before it is used (0: fewer live registers, no spills; measured
-// 655 vs 650 TFLOP/s on the chunked-prefill shape).
-constexpr int kOverlapScoreLoads = 0;
-
 // 64 scores of one row -> 32 fp16 P pairs stored to TMEM at taddr (keys 2c, 2c + 1 in
 // column c), the exponentials added into ls: x = s * fac - m on packed fp32 pairs, a fixed
 // share of the 2^x through the FMA-pipe polynomial.
 __device__ __forceinline__ void softmax_half(const float (&v)[64], float2 fac2, float2 nm2,
                                              float2 (&ls)[4], uint32_t taddr) {
-  uint32_t pk[32];
+  // stored 16 columns at a time, so at most 16 packed pairs are live beside the scores
 #pragma unroll
-  for (int c = 0; c < 32; ++c) {
-    const float2 x = __ffma2_rn(make_float2(v[2 * c], v[2 * c + 1]), fac2, nm2);
-    bool fma_exp = false;
-    if constexpr (kFmaExpEvery > 0) fma_exp = (c % (kFmaExpEvery > 0 ? kFmaExpEvery : 1)) == kFmaExpEvery - 1;
-    const float2 pr = fma_exp ? ex2_fma2(x) : make_float2(ex2(x.x), ex2(x.y));
-    ls[c & 3] = __fadd2_rn(ls[c & 3], pr);
-    pk[c] = pack_half2(pr.x, pr.y);
+  for (int h16 = 0; h16 < 2; ++h16) {
+    uint32_t pk[16];
+#pragma unroll
+    for (int c16 = 0; c16 < 16; ++c16) {
+      const int c = 16 * h16 + c16;
+      const float2 x = __ffma2_rn(make_float2(v[2 * c], v[2 * c + 1]), fac2, nm2);
+      bool fma_exp = false;
+      if constexpr (kTile2FmaExpEvery > 0)
+        fma_exp = (c % (kTile2FmaExpEvery > 0 ? kTile2FmaExpEvery : 1)) == kTile2FmaExpEvery - 1;
+      const float2 pr = fma_exp ? ex2_fma2(x) : make_float2(ex2(x.x), ex2(x.y));
+      ls[c & 3] = __fadd2_rn(ls[c & 3], pr);
+      pk[c16] = pack_half2(pr.x, pr.y);
+    }
+    tc::tmem_st16(taddr + 16 * h16, pk);
   }
-  tc::tmem_st32(taddr, pk);
 }
 
 // ---------------------------------------------------------------- two-tile attention kernel
@@ -1239,33 +1246,26 @@ __global__ void __launch_bounds__(kTile2Threads, 1) prefill2_kernel(const __grid
       tc::fence_after();
       const bool need_mask =
           __any_sync(0xffffffffu, DENSE || !row_ok || t0 < tlo || t0 + BN > thi);  // warp-uniform
-      // Scores are read from TMEM twice, 64 columns at a time: once for the row max, once for
-      // the exponentials, so at most half a row is held in registers; the load of the second
-      // half is in flight while the first is processed.  A masked tile is masked on each read
-      // (its scores then carry q_fac).
       auto mask_half = [&](int hh, float (&v)[64]) {
         if (need_mask) {
 #pragma unroll
           for (int j2 = 0; j2 < 64; ++j2) v[j2] = masked(v[j2] * q_fac, t0 + 64 * hh + j2);
         }
       };
-      // row max: three-input maxima into eight partial results
-      float mp[8];
-      if constexpr (kOverlapScoreLoads != 0) {
-        float va[64], vb[64];
-        tc::tmem_ld64_nowait(s_row, va);
-        tc::tmem_wait_ld();
-        tc::tmem_ld64_nowait(s_row + 64, vb);
-        mask_half(0, va);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mp[k] = va[k];
-#pragma unroll
-        for (int j2 = 8; j2 < 64; j2 += 2) mp[(j2 >> 1) & 7] = max3f(mp[(j2 >> 1) & 7], va[j2], va[j2 + 1]);
-        tc::tmem_wait_ld();
-        mask_half(1, vb);
-#pragma unroll
-        for (int j2 = 0; j2 < 64; j2 += 2) mp[(j2 >> 1) & 7] = max3f(mp[(j2 >> 1) & 7], vb[j2], vb[j2 + 1]);
-      } else {
+      const float fac = need_mask ? 1.0f : q_fac;  // masked scores already carry q_fac
+      const float2 fac2 = make_float2(fac, fac);
+      // P against the running max as it stands, in one pass over the scores.  Every p is
+      // >= 0, so a tile sum <= 2^15 bounds every p by 2^15 (inside fp16 for the P operand);
+      // a larger or non-finite sum means the running max has fallen more than 15 behind, and
+      // the tile is redone after a max pass (scores read once more) and a lazy rescale: the
+      // running max is raised when the tile's max exceeds it by more than 2^8, so the redone
+      // sum is at most 128 * 2^8.  A row with no running max yet starts with the max pass.
+      // (The passes over the two 64-column halves are not unrolled: unrolled, the kernel
+      // needs more registers than 320 threads get and spills.)
+      bool need_max = !__all_sync(0xffffffffu, m_run != -INFINITY);
+      // row max of the tile's scores (one read of S), then the lazy rescale
+      auto max_pass = [&]() {
+        float mp[8];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           float v[64];
@@ -1279,56 +1279,52 @@ __global__ void __launch_bounds__(kTile2Threads, 1) prefill2_kernel(const __grid
           for (int j2 = hh == 0 ? 8 : 0; j2 < 64; j2 += 2)
             mp[(j2 >> 1) & 7] = max3f(mp[(j2 >> 1) & 7], v[j2], v[j2 + 1]);
         }
-      }
-      mp[0] = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
-      const float tile_max = need_mask ? mp[0] : mp[0] * q_fac;
-      const bool raise = tile_max > m_run + kPrefillRescaleSlack;
-      if (__any_sync(0xffffffffu, raise)) {
-        const float m_new = raise ? tile_max : m_run;
-        const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
-        if (i >= 1) {
-          // P . V of the previous tile has landed in O: it read S[qt] before this tile's
-          // scores were written there
-          if (__all_sync(0xffffffffu, wait_or_abort(bar(LY::B_OFULL + qt), (i - 1) & 1, p.wait_ns,
-                                                    abort_flag))) {
-            tc::fence_after();
-            rescale_o<DV>(o_row, alpha);
-          } else {
-            *abort_flag = 1;
+        mp[0] = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+        const float tile_max = need_mask ? mp[0] : mp[0] * q_fac;
+        const bool raise = tile_max > m_run + kPrefillRescaleSlack;
+        if (__any_sync(0xffffffffu, raise)) {
+          const float m_new = raise ? tile_max : m_run;
+          const float alpha = m_run == -INFINITY ? 0.0f : ex2(m_run - m_new);
+          if (i >= 1) {
+            // P . V of the previous tile has landed in O: it read S[qt] before this tile's
+            // scores were written there
+            if (__all_sync(0xffffffffu, wait_or_abort(bar(LY::B_OFULL + qt), (i - 1) & 1, p.wait_ns,
+                                                      abort_flag))) {
+              tc::fence_after();
+              rescale_o<DV>(o_row, alpha);
+            } else {
+              *abort_flag = 1;
+            }
           }
+          l_run *= alpha;
+          m_run = m_new;
         }
-        l_run *= alpha;
-        m_run = m_new;
-      }
-      const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
-      const float fac = need_mask ? 1.0f : q_fac;  // masked scores already carry q_fac
-      // exponentials, row sum and P on packed fp32 pairs: x = s * fac - m, p = 2^x
-      const float2 fac2 = make_float2(fac, fac), nm2 = make_float2(-m_safe, -m_safe);
-      float2 ls[4];
+      };
+      // exponentials, row sum and P on packed fp32 pairs: x = s * fac - m, p = 2^x; P (fp16
+      // pairs, keys 2c, 2c + 1 in column c: the A operand of P . V) replaces S[qt], written in
+      // two halves of 32 columns
+      auto exp_pass = [&]() -> float {
+        const float m_safe = m_run == -INFINITY ? 0.0f : m_run;
+        const float2 nm2 = make_float2(-m_safe, -m_safe);
+        float2 ls[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) ls[k] = make_float2(0.0f, 0.0f);
-      // P (fp16 pairs) replaces S[qt]: keys 2c, 2c + 1 in column c, the A operand of P . V;
-      // written in two halves of 32 columns
-      if constexpr (kOverlapScoreLoads != 0) {
-        float va[64], vb[64];
-        tc::tmem_ld64_nowait(s_row, va);
-        tc::tmem_wait_ld();
-        tc::tmem_ld64_nowait(s_row + 64, vb);
-        mask_half(0, va);
-        softmax_half(va, fac2, nm2, ls, s_row);
-        tc::tmem_wait_ld();
-        mask_half(1, vb);
-        softmax_half(vb, fac2, nm2, ls, s_row + 32);
-      } else {
-#pragma unroll
+        for (int k = 0; k < 4; ++k) ls[k] = make_float2(0.0f, 0.0f);
+#pragma unroll 1
         for (int hh = 0; hh < 2; ++hh) {
           float v[64];
           tc::tmem_ld64(s_row + 64 * hh, v);
           mask_half(hh, v);
           softmax_half(v, fac2, nm2, ls, s_row + 32 * hh);
         }
+        return ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
+      };
+      if (need_max) max_pass();
+      float tile_sum = exp_pass();
+      if (!need_max && !__all_sync(0xffffffffu, tile_sum <= 32768.0f)) {  // false for inf / NaN
+        max_pass();
+        tile_sum = exp_pass();
       }
-      l_run += ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
+      l_run += tile_sum;
       tc::fence_before();
       mbar_arrive(bar(LY::B_PFULL + qt));
       done_tiles = i + 1;
