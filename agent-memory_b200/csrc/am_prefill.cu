@@ -423,7 +423,7 @@ struct SoftmaxGeom {
   static constexpr int CTA_THREADS = THREADS + 64;
 };
 
-template <int DK, int DV, int BN, int NS>
+template <int DK, int DV, int BN, int NS, int NSV>
 struct PrefillLayout {
   static constexpr int CG = SoftmaxGeom<BN>::CG;
   static constexpr int QSLAB = 128 * 128;  // 128 query rows x 64 fp16 (one swizzled slab)
@@ -434,15 +434,15 @@ struct PrefillLayout {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + (DK / 64) * QSLAB;
   static constexpr int OFF_V = OFF_K + NS * KSTAGE;
-  static constexpr int OFF_QF = OFF_V + NS * VSTAGE;  // per-row query factor (128 floats)
+  static constexpr int OFF_QF = OFF_V + NSV * VSTAGE;  // per-row query factor (128 floats)
   static constexpr int OFF_RX = OFF_QF + 128 * 4;     // row exchange between column groups [CG][128]
   static constexpr int OFF_BAR = OFF_RX + CG * 128 * 4;
-  // mbarriers: K full / empty, V full / empty (NS each), S full x2, P full x2, O full x2,
-  // drain.  Every barrier that completes once per tile alternates between two copies by
-  // tile parity, so a parity wait can never be satisfied by the phase of the tile before
-  // last.
-  static constexpr int B_KFULL = 0, B_KEMPTY = NS, B_VFULL = 2 * NS, B_VEMPTY = 3 * NS;
-  static constexpr int B_SFULL = 4 * NS, B_PFULL = B_SFULL + 2;
+  // mbarriers: K full / empty (NS each), V full / empty (NSV each), S full x2, P full x2,
+  // O full x2, drain.  Every barrier that completes once per tile alternates between two
+  // copies by tile parity, so a parity wait can never be satisfied by the phase of the tile
+  // before last.
+  static constexpr int B_KFULL = 0, B_KEMPTY = NS, B_VFULL = 2 * NS, B_VEMPTY = 2 * NS + NSV;
+  static constexpr int B_SFULL = 2 * NS + 2 * NSV, B_PFULL = B_SFULL + 2;
   static constexpr int B_OFULL = B_PFULL + 2, B_DRAIN = B_OFULL + 2, B_COUNT = B_DRAIN + 1;
   static constexpr int SMEM = OFF_BAR + B_COUNT * 8 + 16;  // + TMEM slot and abort flag
   static constexpr uint32_t TMEM_COLS = 512;  // S x2 (2 BN) + O (DV)
@@ -505,10 +505,10 @@ __device__ __forceinline__ void rescale_o(uint32_t taddr, float f) {
   }
 }
 
-template <int DK, int DV, int BN, int NS, bool DENSE>
+template <int DK, int DV, int BN, int NS, int NSV, bool DENSE>
 __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
     prefill_kernel(const __grid_constant__ DecodeParams p) {
-  using LY = PrefillLayout<DK, DV, BN, NS>;
+  using LY = PrefillLayout<DK, DV, BN, NS, NSV>;
   using SG = SoftmaxGeom<BN>;
   static_assert(LY::SMEM <= 232448, "dynamic shared memory of one CTA");
   constexpr int CG = SG::CG;
@@ -644,13 +644,14 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
           tma_load_2d(sK + s * LY::KSTAGE + x * LY::KSLAB, &p.tmap_kd, x * 128, y0 + j * BN,
                       bar(LY::B_KFULL + s));
         issued_k = j + 1;
-        if (j >= NS) ok = wait_or_abort(bar(LY::B_VEMPTY + s), ((j - NS) / NS) & 1, p.wait_ns, abort_flag);
+        const int sv = j % NSV;
+        if (j >= NSV) ok = wait_or_abort(bar(LY::B_VEMPTY + sv), ((j - NSV) / NSV) & 1, p.wait_ns, abort_flag);
         if (!ok) break;
-        mbar_arrive_expect_tx(bar(LY::B_VFULL + s), LY::VSTAGE);
+        mbar_arrive_expect_tx(bar(LY::B_VFULL + sv), LY::VSTAGE);
 #pragma unroll
         for (int x = 0; x < DV / 64; ++x)
-          tma_load_2d(sV + s * LY::VSTAGE + x * LY::VSLAB, &p.tmap_vd, x * 128, y0 + j * BN,
-                      bar(LY::B_VFULL + s));
+          tma_load_2d(sV + sv * LY::VSTAGE + x * LY::VSLAB, &p.tmap_vd, x * 128, y0 + j * BN,
+                      bar(LY::B_VFULL + sv));
         issued_v = j + 1;
       }
       if (!ok) *abort_flag = 1;
@@ -681,8 +682,8 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
           tc::commit(bar(LY::B_KEMPTY + s));
         }
         if (j >= 1) {
-          const int jj = j - 1, s = jj % NS, buf = jj & 1;
-          ok = wait_or_abort(bar(LY::B_VFULL + s), (jj / NS) & 1, p.wait_ns, abort_flag);
+          const int jj = j - 1, s = jj % NSV, buf = jj & 1;
+          ok = wait_or_abort(bar(LY::B_VFULL + s), (jj / NSV) & 1, p.wait_ns, abort_flag);
           if (ok) ok = wait_or_abort(bar(LY::B_PFULL + buf), (jj >> 1) & 1, p.wait_ns, abort_flag);
           if (!ok) break;
           tc::fence_after();
@@ -916,8 +917,8 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
     if (warp == SG::TMA_WARP && lane == 0) {
       for (int jj = max(0, issued_k - NS); jj < issued_k; ++jj)
         mbar_wait_bounded(bar(LY::B_KFULL + jj % NS), (jj / NS) & 1, kDrainNs);
-      for (int jj = max(0, issued_v - NS); jj < issued_v; ++jj)
-        mbar_wait_bounded(bar(LY::B_VFULL + jj % NS), (jj / NS) & 1, kDrainNs);
+      for (int jj = max(0, issued_v - NSV); jj < issued_v; ++jj)
+        mbar_wait_bounded(bar(LY::B_VFULL + jj % NSV), (jj / NSV) & 1, kDrainNs);
     }
     if (warp == SG::MMA_WARP && lane == 0 && mma_issued) {
       tc::commit(bar(LY::B_DRAIN));
@@ -937,6 +938,21 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
 // 64 scores of one row -> 32 fp16 P pairs stored to TMEM at taddr (keys 2c, 2c + 1 in
 // column c), the exponentials added into ls: x = s * fac - m on packed fp32 pairs, a fixed
 // share of the 2^x through the FMA-pipe polynomial.
+// The same without the store: the 32 packed pairs are returned in pk.
+__device__ __forceinline__ void softmax_pack(const float (&v)[64], float2 fac2, float2 nm2,
+                                             float2 (&ls)[4], uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c) {
+    const float2 x = __ffma2_rn(make_float2(v[2 * c], v[2 * c + 1]), fac2, nm2);
+    bool fma_exp = false;
+    if constexpr (kTile2FmaExpEvery > 0)
+      fma_exp = (c % (kTile2FmaExpEvery > 0 ? kTile2FmaExpEvery : 1)) == kTile2FmaExpEvery - 1;
+    const float2 pr = fma_exp ? ex2_fma2(x) : make_float2(ex2(x.x), ex2(x.y));
+    ls[c & 3] = __fadd2_rn(ls[c & 3], pr);
+    pk[c] = pack_half2(pr.x, pr.y);
+  }
+}
+
 __device__ __forceinline__ void softmax_half(const float (&v)[64], float2 fac2, float2 nm2,
                                              float2 (&ls)[4], uint32_t taddr) {
   // stored 16 columns at a time, so at most 16 packed pairs are live beside the scores
@@ -1318,9 +1334,36 @@ __global__ void __launch_bounds__(kTile2Threads, 1) prefill2_kernel(const __grid
         }
         return ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
       };
-      if (need_max) max_pass();
-      float tile_sum = exp_pass();
-      if (!need_max && !__all_sync(0xffffffffu, tile_sum <= 32768.0f)) {  // false for inf / NaN
+      float tile_sum;
+      bool done = false;
+      if (!need_max) {
+        // fast path: both halves' P held in registers until the sum check passes, so a
+        // failed check leaves S intact for the full path
+        const float2 nm2 = make_float2(-m_run, -m_run);
+        float2 ls[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) ls[k] = make_float2(0.0f, 0.0f);
+        uint32_t p0[32], p1[32];
+        {
+          float v[64];
+          tc::tmem_ld64(s_row, v);
+          mask_half(0, v);
+          softmax_pack(v, fac2, nm2, ls, p0);
+        }
+        {
+          float v[64];
+          tc::tmem_ld64(s_row + 64, v);
+          mask_half(1, v);
+          softmax_pack(v, fac2, nm2, ls, p1);
+        }
+        tile_sum = ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y));
+        if (__all_sync(0xffffffffu, tile_sum <= 32768.0f)) {  // false for inf / NaN
+          tc::tmem_st32(s_row, p0);
+          tc::tmem_st32(s_row + 32, p1);
+          done = true;
+        }
+      }
+      if (!done) {
         max_pass();
         tile_sum = exp_pass();
       }
@@ -1415,15 +1458,18 @@ __global__ void __launch_bounds__(kTile2Threads, 1) prefill2_kernel(const __grid
 
 // ---------------------------------------------------------------- host side
 
-// Key-tile size and pipeline depth per head-dim pair (shared memory: Q tile + NS K and V
-// stages must fit one CTA's 227 KB).
+// Key-tile size and pipeline depths per head-dim pair (shared memory: the query tile, NS K
+// stages and NSV V stages must fit one CTA's 227 KB).  The V ring is made the deeper one
+// when both cannot grow: V_j can only load once P . V of tile j - NSV has completed, and
+// that chain sets the tile period of the largest heads.
 template <int DK, int DV>
 struct PrefillCfg {
   static constexpr int BN = (DK + DV) > 384 ? 64 : 128;
-  static constexpr int NS = PrefillLayout<DK, DV, BN, 4>::SMEM <= 232448   ? 4
-                            : PrefillLayout<DK, DV, BN, 3>::SMEM <= 232448 ? 3
-                                                                            : 2;
-  using LY = PrefillLayout<DK, DV, BN, NS>;
+  template <int K, int V>
+  static constexpr bool kFits = PrefillLayout<DK, DV, BN, K, V>::SMEM <= 232448;
+  static constexpr int NS = kFits<4, 4> ? 4 : kFits<3, 3> ? 3 : 2;
+  static constexpr int NSV = kFits<4, 4> ? 4 : kFits<3, 3> ? 3 : kFits<2, 3> ? 3 : 2;
+  using LY = PrefillLayout<DK, DV, BN, NS, NSV>;
 };
 
 bool prefill_supported(int k_dim, int v_dim) {
@@ -1484,7 +1530,7 @@ static cudaError_t launch_attn_t(const DecodeParams& p, int batch, cudaStream_t 
     cfg.dynamicSmemBytes = C::LY::SMEM;
   } else {
     using C = PrefillCfg<DK, DV>;
-    kfn = prefill_kernel<DK, DV, C::BN, C::NS, DENSE>;
+    kfn = prefill_kernel<DK, DV, C::BN, C::NS, C::NSV, DENSE>;
     static unsigned long long done = 0;
     cudaError_t e = prefill_smem_once(kfn, C::LY::SMEM, &done);
     if (e != cudaSuccess) return e;

@@ -175,3 +175,33 @@ def test_prefill_ragged_kv_len(cuda, orc):
     assert torch.isfinite(got).all()
     want = oracle(orc, q, kq, vq, 0.09, causal=True, kv_len=np.array([N, 300]))
     assert_close(got.cpu().numpy(), want, what="ragged kv_len")
+
+
+@pytest.mark.parametrize("trend", ["rising", "falling"])
+@pytest.mark.parametrize("dims", [(128, 128), (256, 256)], ids=["d128", "d256"])
+def test_prefill_scores_that_jump_between_tiles(cuda, orc, trend, dims):
+    """Scores that jump by ~40 (log2 units) from one 128-key tile to the next, rising or
+    falling along the keys: the one-pass softmax must detect a running max that has fallen
+    behind (a tile sum beyond the fp16 range of P) and redo the tile after a max pass and
+    rescale; falling scores keep the first tiles' max and give tiny P.  Every key is a
+    constant vector a_t (a multiple of 1/8 below 32), which Q4 and the fp16 operands both
+    hold exactly, so large scores carry no operand rounding; the queries are |N(0,1)|, so
+    q . k grows with a_t."""
+    B, Hq, Hkv, L, P = 1, 8, 2, 256, 1024
+    dk, dv = dims
+    N = P + L
+    t = torch.arange(N)
+    a = 2.5 * (t // 128).float() + ((t * 5) % 8).float() / 8.0
+    if trend == "falling":
+        a = a.flip(0)
+    g = torch.Generator().manual_seed(57)
+    k = a[None, None, :, None].expand(B, Hkv, N, dk).half().contiguous()
+    v = torch.randn(B, Hkv, N, dv, generator=g).half()
+    q = torch.randn(B, Hq, L, dk, generator=g).abs().half()
+    kq, vq = pkg.quantize(k.to(cuda)), pkg.quantize(v.to(cuda))
+    view, n = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q.to(cuda), dk ** -0.5, kv_len, N, causal=True,
+                                out_dtype=torch.float32, mode="prefill")
+    want = oracle(orc, q, kq, vq, dk ** -0.5, causal=True)
+    assert_close(got.cpu().numpy(), want, what=f"prefill {trend} scores {dims}")
