@@ -178,7 +178,7 @@ def test_prefill_ragged_kv_len(cuda, orc):
 
 
 @pytest.mark.parametrize("trend", ["rising", "falling"])
-@pytest.mark.parametrize("dims", [(128, 128), (256, 256)], ids=["d128", "d256"])
+@pytest.mark.parametrize("dims", [(128, 128), (192, 128), (256, 256)], ids=["d128", "k192_v128", "d256"])
 def test_prefill_scores_that_jump_between_tiles(cuda, orc, trend, dims):
     """Scores that jump by ~40 (log2 units) from one 128-key tile to the next, rising or
     falling along the keys: the one-pass softmax must detect a running max that has fallen
