@@ -410,8 +410,20 @@ def run_ours(args, rank, world, local_rank):
             del hq_buf, hk_buf, hv_buf, ho_buf, dq, dk_, dv_
         torch.cuda.synchronize(dev)
         torch.cuda.empty_cache()
-        sub = {w: measure_config(w, am, dev, steps=args.config_steps, warmup=3, seed=args.seed)
-               for w in ("llama_layer", "gemma", "mla", "prefill", "gemma_prefill", "mla_prefill")}
+        sub = {}
+        for w in ("llama_layer", "gemma", "mla", "prefill", "gemma_prefill", "mla_prefill"):
+            # each record on its own: a configuration that fails (out of memory on a shared
+            # box, say) is reported as such and does not take the headline line with it
+            try:
+                sub[w] = measure_config(w, am, dev, steps=args.config_steps, warmup=3, seed=args.seed)
+            except Exception as e:  # noqa: BLE001 - reported in the line, never swallowed silently
+                sub[w] = {"error": f"{type(e).__name__}: {e}"[:300]}
+            try:
+                torch.cuda.synchronize(dev)
+                torch.cuda.empty_cache()
+            except Exception as e:  # noqa: BLE001 - a broken context ends the remaining records
+                sub["stopped"] = f"{type(e).__name__}: {e}"[:300]
+                break
 
     if rank == 0:
         line = {
