@@ -225,7 +225,8 @@ __device__ __forceinline__ void tmem_stf(uint32_t taddr, const float (&v)[N]) {
 
 }  // namespace tc
 
-// 2^x on the FMA pipe for x in [-125, 8] (Cody-Waite style range reduction and a cubic
+// 2^x on the FMA pipe for x in [-125, 8] (Cody-Waite range reduction, W. J. Cody and
+// W. Waite, "Software Manual for the Elementary Functions", Prentice-Hall 1980, and a cubic
 // minimax polynomial): x = j + f with j = rint(x) taken from the low mantissa bits of
 // x + 1.5 * 2^23 and f in [-0.5, 0.5]; 2^f ~= c0 + f (c1 + f (c2 + f c3)); the result's
 // exponent is raised by j with one integer add.  The coefficients minimise the relative
