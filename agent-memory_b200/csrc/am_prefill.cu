@@ -28,8 +28,10 @@
 //      tensor core computes S_j while the softmax warps work on tile j-1.
 //    Both: tcgen05.ld of the scores, fp32 online softmax, P as fp16 pairs stored back over
 //    the S columns (tcgen05.st); O rows rescaled in TMEM only when the running max moves by
-//    more than 2^8.  A fixed share of the exponentials runs as a polynomial on the FMA pipe
-//    instead of the MUFU unit (ex2_fma below), which the other share saturates otherwise.
+//    more than 2^8.  The two-tile kernel computes P against the running max in one read of
+//    the scores and takes the row max only when a tile's sum leaves the fp16 range of P (or
+//    for a row's first tile); the one-tile kernel takes the row max every tile and runs a
+//    fixed share of its exponentials as a polynomial on the FMA pipe (ex2_fma below).
 //    mbarriers chain the stages: TMA completions (K/V full), MMA commits (S full, O full,
 //    K/V empty) and the softmax threads' arrivals (P full).  TMEM: 512 columns, one CTA per
 //    SM.  Operands are fp16: queries (fp16 or bf16) are rescaled per row by a power of two
