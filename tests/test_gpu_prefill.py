@@ -82,33 +82,38 @@ def test_prefill_matches_decode_kernel(cuda):
     assert torch.allclose(a, b, atol=2e-3, rtol=1e-3), (a - b).abs().max()
 
 
-def test_chunked_prefill_paged(cuda, orc):
+@pytest.mark.parametrize("geom", [(2, 32, 8, 128, 128, 700, 300), (2, 16, 8, 256, 256, 420, 200),
+                                  (2, 16, 16, 192, 128, 330, 190)],
+                         ids=["llama_d128", "gemma_d256", "mla_k192_v128"])
+def test_chunked_prefill_paged(cuda, orc, geom):
     """Config-4 flow at reduced size on the paged pool: append the chunk's K/V into
-    256-token blocks, then attend the chunk over prefix + chunk."""
-    A, Hq, Hkv, D, bt = 2, 32, 8, 128, 256
-    P, L = 700, 300
-    spec = pkg.ModelCacheSpec(n_layers=1, n_kv_heads=Hkv, head_dim=D, block_tokens=bt,
-                              layer_types=["global"])
+    256-token blocks, then attend the chunk over prefix + chunk.  The Gemma-3 and MLA
+    geometries take the kernel that dequantizes its tiles from the pool blocks itself
+    (tiles that straddle two blocks, bf16 scales)."""
+    A, Hq, Hkv, Dk, Dv, P, L = geom
+    bt = 256
+    spec = pkg.ModelCacheSpec(n_layers=1, n_kv_heads=Hkv, head_dim=Dk, block_tokens=bt,
+                              layer_types=["global"], v_head_dim=Dv)
     alloc = pkg.shuffled_allocator(spec, 32, seed=1)
     pool = pkg.PagedQ4Pool.for_spec(spec, 32, torch.bfloat16, cuda)
-    layer = pkg.PagedLayerCache(pool, alloc, 0, ["a0", "a1"], P + L)
+    layer = pkg.PagedLayerCache(pool, alloc, 0, ["a0", "a1"][:A], P + L)
     g = torch.Generator().manual_seed(2)
-    kp = torch.randn(A, Hkv, P, D, generator=g).bfloat16()
-    vp = torch.randn(A, Hkv, P, D, generator=g).bfloat16()
+    kp = torch.randn(A, Hkv, P, Dk, generator=g).bfloat16()
+    vp = torch.randn(A, Hkv, P, Dv, generator=g).bfloat16()
     layer.append(kp.to(cuda), vp.to(cuda))
-    kc = torch.randn(A, Hkv, L, D, generator=g).bfloat16()
-    vc = torch.randn(A, Hkv, L, D, generator=g).bfloat16()
+    kc = torch.randn(A, Hkv, L, Dk, generator=g).bfloat16()
+    vc = torch.randn(A, Hkv, L, Dv, generator=g).bfloat16()
     layer.append(kc.to(cuda), vc.to(cuda))
-    q = torch.randn(A, Hq, L, D, generator=g).bfloat16()
-    got = layer.attention(q.to(cuda), D ** -0.5, mode="prefill")
+    q = torch.randn(A, Hq, L, Dk, generator=g).bfloat16()
+    got = layer.attention(q.to(cuda), Dk ** -0.5, mode="prefill")
     table = layer._table_host.numpy()
     want = orc.attention(q.float().numpy(), tuple(_bits(t) for t in pool.k),
-                         tuple(_bits(t) for t in pool.v), D ** -0.5, sdtype=1, n_kv_heads=Hkv,
+                         tuple(_bits(t) for t in pool.v), Dk ** -0.5, sdtype=1, n_kv_heads=Hkv,
                          layout=1, block_table=table, kv_len=np.array(layer.lengths), causal=True)
     assert got.dtype == torch.bfloat16
     assert_close_out(got.float().cpu().numpy(), want, got.dtype, what="paged chunked prefill")
-    out32 = torch.empty(A, Hq, L, D, dtype=torch.float32, device=cuda)
-    layer.attention(q.to(cuda), D ** -0.5, out=out32, mode="prefill")
+    out32 = torch.empty(A, Hq, L, Dv, dtype=torch.float32, device=cuda)
+    layer.attention(q.to(cuda), Dk ** -0.5, out=out32, mode="prefill")
     assert_close(out32.cpu().numpy(), want, what="paged chunked prefill, fp32 out")
 
 

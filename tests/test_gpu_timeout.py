@@ -75,12 +75,15 @@ def test_paged_decode_wait_timeout_is_flagged_and_recovers(cuda, orc, monkeypatc
     assert_close(got.cpu().numpy(), want, what="paged decode after a timed-out call")
 
 
-def test_prefill_wait_timeout_is_flagged_and_recovers(cuda, orc, monkeypatch):
-    """The tcgen05 prefill kernel: its TMA producer, MMA issuer and softmax warps all give
-    up, the kernel waits for its loads and MMAs in flight, frees its TMEM and returns; the
-    next call (fresh TMEM allocations on every SM) is correct."""
-    B, Hq, Hkv, D, L, N = 2, 16, 4, 128, 256, 1200
-    q, kq, vq = make_case(B, Hq, Hkv, N, D, D, L=L, cuda=cuda, seed=23)
+@pytest.mark.parametrize("geom", [(16, 4, 128, 128), (16, 16, 192, 128)], ids=["d128", "k192_v128"])
+def test_prefill_wait_timeout_is_flagged_and_recovers(cuda, orc, monkeypatch, geom):
+    """The tcgen05 prefill kernels (TMA-fed two-tile, and the one-tile kernel whose producer
+    warps dequantize the tiles): producer, MMA issuer and softmax warps all give up, the
+    kernel waits for its loads and MMAs in flight, frees its TMEM and returns; the next
+    call (fresh TMEM allocations on every SM) is correct."""
+    Hq, Hkv, D, Dv = geom
+    B, L, N = 2, 256, 1200
+    q, kq, vq = make_case(B, Hq, Hkv, N, D, Dv, L=L, cuda=cuda, seed=23)
     view, n = pkg.kernels.contiguous_view(kq, vq)
     kv_len = torch.full((B,), n, dtype=torch.int32, device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
