@@ -262,7 +262,7 @@ static void fill_params(DecodeParams& p, const am_q4_cache* cache, const am_attn
 // Workspace planes of a prefill call: nw rows per (sequence, KV head) hold the keys the query
 // block can see, [lo, kv_len) -- the window plus the block when a sliding window applies
 // (and no dense mask), else up to max_kv_len keys; K rows first, V rows 256-byte aligned
-// after them.
+// after them (none for head dims whose attention kernel dequantizes V itself).
 struct PrefillPlanes {
   int nw;
   int64_t rows;
@@ -277,7 +277,7 @@ static PrefillPlanes prefill_planes(const am_q4_cache* c, const am_attn_args* a)
   pl.nw = static_cast<int>(std::max<int64_t>(8, (span + 7) / 8 * 8));
   pl.rows = static_cast<int64_t>(a->batch) * c->n_kv_heads * pl.nw;
   pl.k_bytes = (static_cast<size_t>(pl.rows) * c->k_dim * 2 + 255) / 256 * 256;
-  pl.v_bytes = static_cast<size_t>(pl.rows) * c->v_dim * 2;
+  pl.v_bytes = prefill_v_in_kernel(c->k_dim, c->v_dim) ? 0 : static_cast<size_t>(pl.rows) * c->v_dim * 2;
   return pl;
 }
 
@@ -513,11 +513,11 @@ int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* workspa
   DecodeParams p{};
   fill_params(p, cache, a);
   p.kd = static_cast<uint16_t*>(workspace);
-  p.vd = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + pl.k_bytes);
+  p.vd = pl.v_bytes > 0 ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + pl.k_bytes) : nullptr;
   p.nw = pl.nw;
   const int bn = prefill_key_tile(cache->k_dim, cache->v_dim);
   if (!encode_codes_map(&p.tmap_kd, p.kd, pl.rows, cache->k_dim * 2, 128, bn) ||
-      !encode_codes_map(&p.tmap_vd, p.vd, pl.rows, cache->v_dim * 2, 128, bn)) {
+      (pl.v_bytes > 0 && !encode_codes_map(&p.tmap_vd, p.vd, pl.rows, cache->v_dim * 2, 128, bn))) {
     set_error("am_q4_prefill: cannot describe the workspace as tensor maps (a driver with "
               "cuTensorMapEncodeTiled is required)");
     return AM_ERR_CUDA;

@@ -374,6 +374,10 @@ struct DecodeParams {
   uint16_t* kd;
   uint16_t* vd;
   int32_t nw;  // rows per (sequence, KV head) plane
+  // Prefill kernels that dequantize V tiles themselves read the cache directly: block-pool
+  // layout (table, block_tokens) or contiguous rows, and the scale / bias type.
+  int32_t paged;
+  int32_t scale_bf16;
   alignas(64) CUtensorMap tmap_kd;
   alignas(64) CUtensorMap tmap_vd;
 };

@@ -31,6 +31,8 @@ cudaError_t launch_decode(const DecodeParams& p, int batch, int row_groups, bool
 bool prefill_supported(int k_dim, int v_dim);
 // Keys per tile of the prefill attention kernel for a head-dim pair (the tensor-map box rows).
 int prefill_key_tile(int k_dim, int v_dim);
+// True when the attention kernel dequantizes V itself (the workspace then holds K rows only).
+bool prefill_v_in_kernel(int k_dim, int v_dim);
 // Stage kernel (Q4 -> fp16 workspace rows) then attention kernel; p.kd / p.vd / p.nw and the
 // tensor maps tmap_kd / tmap_vd describe the workspace.
 cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16,

@@ -8,7 +8,9 @@
 //    Rows outside that range, past the end of the cache, or behind a bad block id are
 //    zeros, so every row a tile can reach is finite.  code * scale + bias is formed in fp32
 //    and rounded once to fp16 (saturating at +-65504).  HBM-bound: reads Dk/2 + Dk/16 +
-//    Dv/2 + Dv/16 bytes and writes 2 (Dk + Dv) bytes per (key, KV head).
+//    Dv/2 + Dv/16 bytes and writes 2 (Dk + Dv) bytes per (key, KV head) -- 2 Dk for MLA's
+//    192 / 128, whose V tiles the attention kernel dequantizes itself (HBM writes bound
+//    the stage, and at that shape they are 31% of the layer).
 //
 // 2. The attention kernel streams the fp16 planes.  Query rows are (token, GQA head) pairs,
 //    token-major, so each K/V tile feeds the n_rep heads that share its KV head.  Two
@@ -25,7 +27,11 @@
 //      one CTA = one 128-row query tile, 320 threads; BN-key tiles (128, or 64 for Dk + Dv >
 //      384); 8 softmax warps, two per TMEM lane quarter, each owning BN / 2 key columns of
 //      every tile and exchanging row maxima with its partner through shared memory; the
-//      tensor core computes S_j while the softmax warps work on tile j-1.
+//      tensor core computes S_j while the softmax warps work on tile j-1.  For MLA, four
+//      more warps (448 threads) fill the V ring from the Q4 cache: one thread per key keeps
+//      its code words, scales and biases for three tiles in registers and writes the
+//      swizzled fp16 rows with f16x2 arithmetic (rows with a group beyond fp16's range take
+//      an out-of-line fp32 path that saturates); the TMA thread then streams K only.
 //    Both: tcgen05.ld of the scores, fp32 online softmax, P as fp16 pairs stored back over
 //    the S columns (tcgen05.st); O rows rescaled in TMEM only when the running max moves by
 //    more than 2^8.  The two-tile kernel computes P against the running max in one read of
@@ -313,10 +319,11 @@ __device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&v)[8]) {
                : "memory");
 }
 
-template <int DK, int DV, bool SBF16, bool PAGED>
+template <int DK, int DV, bool SBF16, bool PAGED, bool KONLY>
 __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constant__ DecodeParams p) {
   griddep_launch_dependents();
-  constexpr int CK = DK / 32, CV = DV / 32, CPR = CK + CV;  // chunks per row
+  // (KONLY: the attention kernel dequantizes V itself; only the K plane is written)
+  constexpr int CK = DK / 32, CV = KONLY ? 0 : DV / 32, CPR = CK + CV;  // chunks per row
   constexpr int ITEMS = (kStageRows * CPR + 255) / 256;
   constexpr int NGK = DK / 64, NGV = DV / 64;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -407,6 +414,130 @@ __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constan
   }
 }
 
+// ---------------------------------------------------------------- in-kernel V dequantization
+// The one-tile attention kernel (Dk or Dv > 128) takes K from the stage kernel's fp16 plane
+// but converts its V tiles itself, straight from the Q4 cache: the stage then writes half
+// the bytes (HBM writes bound it), and each V tile crosses from L2 as Q4 (3.5x fewer bytes).
+// One code word (8 elements) becomes one 16-byte operand chunk of fp16 pairs in the order
+// (e0, e4), (e1, e5), (e2, e6), (e3, e7): a nibble pair 16 bits apart, OR-ed into the
+// mantissas of two copies of 1024.0, is exactly (1024 + code) in each half, so one LOP3 and
+// one subtraction give two exact codes, and fma.rn.f16x2 forms code * scale + bias with a
+// single rounding.  O's columns then hold the elements of each 8-element chunk in that
+// order, and the epilogue reads them back in element order.
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;\n" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint4 q4_word_f16(uint32_t w, uint32_t s2, uint32_t b2) {
+  constexpr uint32_t kLo = 0x000F000Fu, k1024 = 0x64006400u;
+  const uint32_t x0 = (w & kLo) | k1024, x1 = ((w >> 4) & kLo) | k1024;
+  const uint32_t x2 = ((w >> 8) & kLo) | k1024, x3 = ((w >> 12) & kLo) | k1024;
+  return make_uint4(hfma2_u32(hsub2_u32(x0, k1024), s2, b2), hfma2_u32(hsub2_u32(x1, k1024), s2, b2),
+                    hfma2_u32(hsub2_u32(x2, k1024), s2, b2), hfma2_u32(hsub2_u32(x3, k1024), s2, b2));
+}
+
+// The same word the stage kernel's way: code * scale + bias in fp32, saturated at +-65504,
+// rounded once to fp16 (for groups whose values leave the fp16 range).
+__device__ __forceinline__ uint4 q4_word_f32(uint32_t w, float s, float b) {
+  uint32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float c0 = __int_as_float(0x4B000000 | ((w >> (4 * e)) & 15u)) - 8388608.0f;
+    const float c1 = __int_as_float(0x4B000000 | ((w >> (4 * e + 16)) & 15u)) - 8388608.0f;
+    o[e] = pack_half2(fminf(fmaxf(fmaf(c0, s, b), -65504.0f), 65504.0f),
+                      fminf(fmaxf(fmaf(c1, s, b), -65504.0f), 65504.0f));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// A group's scale and bias as floats from (scale | bias << 16).
+__device__ __forceinline__ void q4_group_f32(uint32_t sb, bool sbf16, float& s, float& b) {
+  s = sbf16 ? __uint_as_float(sb << 16) : h2f<false>(static_cast<uint16_t>(sb & 0xffffu));
+  b = sbf16 ? __uint_as_float(sb & 0xffff0000u) : h2f<false>(static_cast<uint16_t>(sb >> 16));
+}
+
+// code * scale + bias is monotonic in the code, so codes 0 and 15 bound a group's values.
+template <int NG>
+__device__ __forceinline__ bool q4_groups_in_f16_range(const uint32_t (&sb)[NG], bool sbf16) {
+  bool ok = true;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    float s, b;
+    q4_group_f32(sb[g], sbf16, s, b);
+    ok = ok && fabsf(b) <= 65504.0f && fabsf(fmaf(15.0f, s, b)) <= 65504.0f;
+  }
+  return ok;
+}
+
+// Dequantize NC 16-byte code chunks (32 elements each, starting at chunk c0 of the row) of
+// one key into its row of a swizzled operand tile: 8-element chunk cc of key `key` lives in
+// slab cc / 8 (SLAB bytes each), row key (128 bytes), 16-byte unit (cc % 8) ^ (key % 8) --
+// the layout a 128-byte-swizzled TMA load of fp16 rows produces.  F16: f16x2 arithmetic
+// (every group of the row inside fp16's range); otherwise the fp32 path that saturates.
+template <int NC, int SLAB, bool F16>
+__device__ __forceinline__ void q4_store_key(uint8_t* tile, const uint4 (&codes)[NC],
+                                             const uint32_t (&sb)[NC / 2], int key, int c0,
+                                             bool sbf16) {
+#pragma unroll
+  for (int g = 0; g < NC / 2; ++g) {
+    float s, b;
+    uint32_t s2 = 0, b2 = 0;
+    if constexpr (F16) {
+      if (sbf16) {
+        q4_group_f32(sb[g], true, s, b);
+        s2 = pack_half2(s, s);
+        b2 = pack_half2(b, b);
+      } else {
+        s2 = __byte_perm(sb[g], 0u, 0x1010);
+        b2 = __byte_perm(sb[g], 0u, 0x3232);
+      }
+    } else {
+      q4_group_f32(sb[g], sbf16, s, b);
+    }
+#pragma unroll
+    for (int c = 2 * g; c < 2 * g + 2; ++c) {
+      const uint32_t w[4] = {codes[c].x, codes[c].y, codes[c].z, codes[c].w};
+#pragma unroll
+      for (int wi = 0; wi < 4; ++wi) {
+        const int cc = (c0 + c) * 4 + wi;
+        const int off = (cc / 8) * SLAB + key * 128 + (((cc % 8) ^ (key & 7)) << 4);
+        *reinterpret_cast<uint4*>(tile + off) = F16 ? q4_word_f16(w[wi], s2, b2) : q4_word_f32(w[wi], s, b);
+      }
+    }
+  }
+}
+
+// One key's share of a V tile as the dequantizing threads hold it: NC 16-byte code chunks and
+// the (scale | bias << 16) words of their NC / 2 groups.
+template <int NC>
+struct Q4Row {
+  uint4 v[NC];
+  uint32_t sb[NC / 2];
+};
+
+// The saturating fp32 conversion of a row, out of line: it runs only for rows with a group
+// beyond fp16's range, and keeping its code out of the streaming loop leaves the
+// instruction cache to the common path.
+template <int NC, int SLAB>
+__device__ __noinline__ void q4_store_key_saturating(uint8_t* tile, Q4Row<NC> r, int key, int c0,
+                                                     bool sbf16) {
+  q4_store_key<NC, SLAB, false>(tile, r.v, r.sb, key, c0, sbf16);
+}
+
+// Element of its 8-element chunk that column `col` of O holds (position 2i: element i,
+// position 2i + 1: element i + 4).
+__host__ __device__ constexpr int q4_chunk_elem(int col) {
+  return (col & ~7) | ((col & 1) << 2) | ((col >> 1) & 3);
+}
+
 // ---------------------------------------------------------------- attention kernel
 // Softmax geometry: CG = BN / CPW warps share each TMEM lane quarter (32 query rows), each
 // owning CPW key columns of every tile, so 4 CG softmax warps overlap one another's
@@ -424,6 +555,25 @@ struct SoftmaxGeom {
   static constexpr int THREADS = 32 * WARPS;
   static constexpr int TMA_WARP = WARPS, MMA_WARP = WARPS + 1;
   static constexpr int CTA_THREADS = THREADS + 64;
+};
+
+// Warp roles of the one-tile kernel: softmax warps, the TMA thread's warp, kVDequantWarps
+// warps that dequantize V tiles from the Q4 cache (QV4), then the MMA thread's warp.
+constexpr int kVDequantWarps = 4;
+
+// Head dims whose V tiles are dequantized in the attention kernel (the stage kernel then
+// writes only the K plane): MLA's 192 / 128, where it measured ~2% faster per layer and
+// saves the V plane (0.57 GB at B 16, 16 heads, 8704 keys).  Gemma-3's 256 / 256 (64-key
+// tiles, two threads per key) measured 2-4% slower and keeps the stage for V.
+template <int DK, int DV>
+constexpr bool kPrefillVInKernel = DK == 192 && DV == 128;
+
+template <int BN, bool QV4>
+struct PrefillRoles {
+  static constexpr int TMA_WARP = SoftmaxGeom<BN>::WARPS;
+  static constexpr int DQ_WARP = TMA_WARP + 1;
+  static constexpr int MMA_WARP = DQ_WARP + (QV4 ? kVDequantWarps : 0);
+  static constexpr int THREADS = 32 * (MMA_WARP + 1);
 };
 
 template <int DK, int DV, int BN, int NS, int NSV>
@@ -508,11 +658,12 @@ __device__ __forceinline__ void rescale_o(uint32_t taddr, float f) {
   }
 }
 
-template <int DK, int DV, int BN, int NS, int NSV, bool DENSE>
-__global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
+template <int DK, int DV, int BN, int NS, int NSV, bool DENSE, bool QV4>
+__global__ void __launch_bounds__(PrefillRoles<BN, QV4>::THREADS, 1)
     prefill_kernel(const __grid_constant__ DecodeParams p) {
   using LY = PrefillLayout<DK, DV, BN, NS, NSV>;
   using SG = SoftmaxGeom<BN>;
+  using RL = PrefillRoles<BN, QV4>;
   static_assert(LY::SMEM <= 232448, "dynamic shared memory of one CTA");
   constexpr int CG = SG::CG;
   constexpr int CPW = SG::CPW;
@@ -562,8 +713,11 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
 
   // ---- setup
   if (tid == 0) {
-    for (int i = 0; i < LY::B_COUNT; ++i)
-      mbar_init(bar(i), (i == LY::B_PFULL || i == LY::B_PFULL + 1) ? SG::THREADS : 1);
+    for (int i = 0; i < LY::B_COUNT; ++i) {
+      const bool pfull = i == LY::B_PFULL || i == LY::B_PFULL + 1;
+      const bool vfull = i >= LY::B_VFULL && i < LY::B_VFULL + NSV;  // QV4: one arrival per dequantizing thread
+      mbar_init(bar(i), pfull ? SG::THREADS : (QV4 && vfull) ? 32 * kVDequantWarps : 1);
+    }
     fence_mbar_init();
     *abort_flag = 0;
   }
@@ -631,7 +785,7 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
   int issued_k = 0, issued_v = 0;  // TMA thread: tiles whose loads were issued
   bool mma_issued = false;         // MMA thread: any tcgen05.mma issued
 
-  if (warp == SG::TMA_WARP) {
+  if (warp == RL::TMA_WARP) {
     // ================================================================ TMA producer
     if (lane == 0 && n_tiles > 0) {
       griddep_wait();  // the stage kernel's workspace rows are complete and visible
@@ -647,6 +801,7 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
           tma_load_2d(sK + s * LY::KSTAGE + x * LY::KSLAB, &p.tmap_kd, x * 128, y0 + j * BN,
                       bar(LY::B_KFULL + s));
         issued_k = j + 1;
+        if constexpr (QV4) continue;  // V tiles come from the dequantizing warps
         const int sv = j % NSV;
         if (j >= NSV) ok = wait_or_abort(bar(LY::B_VEMPTY + sv), ((j - NSV) / NSV) & 1, p.wait_ns, abort_flag);
         if (!ok) break;
@@ -659,7 +814,94 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
       }
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp == SG::MMA_WARP) {
+  } else if (QV4 && warp >= RL::DQ_WARP && warp < RL::MMA_WARP) {
+    // ================================================================ V dequantizing producer
+    // 128 threads, one (BN = 128) or two (BN = 64) per key of a tile: each keeps the code
+    // chunks, scales and biases of its key for three tiles in registers, loading tile j + 2
+    // before it converts tile j into the V ring, then arrives on the slot's full barrier.
+    if constexpr (QV4) {
+      static_assert(32 * kVDequantWarps == 128 && 128 % BN == 0, "one or two threads per key");
+      constexpr int TPK = 128 / BN;
+      constexpr int VC = DV / 32 / TPK;  // 16-byte code chunks (32 elements) per thread
+      static_assert(VC % 2 == 0, "whole 64-element groups per thread");
+      constexpr int NGV = DV / 64;
+      const int dt = tid - 32 * RL::DQ_WARP;
+      const int kk = dt % BN, part = dt / BN;
+      const bool sbf16 = p.scale_bf16 != 0;
+      using Raw = Q4Row<VC>;
+      auto load = [&](int j, Raw& r) {
+        const int t = lo + j * BN + kk;
+        int64_t row = -1;
+        if (t < hi) {
+          if (p.paged) {
+            const int blk_i = t / p.block_tokens;
+            const int32_t blk = blk_i < p.table_stride ? p.table[(int64_t)b * p.table_stride + blk_i] : -1;
+            if (blk < 0 || blk >= p.capacity) {
+              flag_status(p.status, AM_STATUS_BAD_BLOCK);
+            } else {
+              row = ((int64_t)blk * p.hkv + h) * p.block_tokens + t % p.block_tokens;
+            }
+          } else if (t < p.capacity) {
+            row = ((int64_t)b * p.hkv + h) * p.capacity + t;
+          } else {
+            flag_status(p.status, AM_STATUS_BAD_POSITION);
+          }
+        }
+        if (row >= 0) {
+          const uint4* vc = reinterpret_cast<const uint4*>(p.vc + row * (DV / 8)) + part * VC;
+#pragma unroll
+          for (int c = 0; c < VC; ++c) r.v[c] = __ldg(vc + c);
+#pragma unroll
+          for (int g2 = 0; g2 < VC / 2; ++g2) {
+            const int64_t gi = row * NGV + part * (VC / 2) + g2;
+            r.sb[g2] = static_cast<uint32_t>(__ldg(p.vs + gi)) | (static_cast<uint32_t>(__ldg(p.vb + gi)) << 16);
+          }
+        } else {  // past the visible keys or behind a bad block: a zero row (scale = bias = 0)
+#pragma unroll
+          for (int c = 0; c < VC; ++c) r.v[c] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int g2 = 0; g2 < VC / 2; ++g2) r.sb[g2] = 0;
+        }
+      };
+      auto put = [&](int j, const Raw& r) -> bool {
+        const int sv = j % NSV;
+        // the range test runs before the ring-slot wait, off the slot-free -> P . V chain
+        const bool in_range = q4_groups_in_f16_range(r.sb, sbf16);
+        if (j >= NSV &&
+            !wait_or_abort(bar(LY::B_VEMPTY + sv), ((j - NSV) / NSV) & 1, p.wait_ns, abort_flag))
+          return false;
+        uint8_t* tile = smem + LY::OFF_V + sv * LY::VSTAGE;
+        // (the lanes still here vote: a lane that gave up on the wait has left)
+        if (__all_sync(__activemask(), in_range)) {
+          q4_store_key<VC, LY::VSLAB, true>(tile, r.v, r.sb, kk, part * VC, sbf16);
+        } else {  // a group leaves fp16's range: saturate it as the stage kernel does
+          q4_store_key_saturating<VC, LY::VSLAB>(tile, r, kk, part * VC, sbf16);
+        }
+        fence_proxy_async_smem();  // the tensor core reads the tile through the async proxy
+        mbar_arrive(bar(LY::B_VFULL + sv));
+        return true;
+      };
+      if (n_tiles > 0) {
+        griddep_wait();  // the cache rows are complete and visible
+        Raw r0, r1, r2;
+        load(0, r0);
+        if (1 < n_tiles) load(1, r1);
+        bool ok = true;
+        for (int j = 0; j < n_tiles; j += 3) {
+          if (j + 2 < n_tiles) load(j + 2, r2);
+          ok = put(j, r0);
+          if (!ok || j + 1 >= n_tiles) break;
+          if (j + 3 < n_tiles) load(j + 3, r0);
+          ok = put(j + 1, r1);
+          if (!ok || j + 2 >= n_tiles) break;
+          if (j + 4 < n_tiles) load(j + 4, r1);
+          ok = put(j + 2, r2);
+          if (!ok) break;
+        }
+        if (!ok) *abort_flag = 1;
+      }
+    }
+  } else if (warp == RL::MMA_WARP) {
     // ================================================================ MMA issuer
     if (lane == 0) {
       bool ok = true;
@@ -853,45 +1095,49 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
     const bool bad = group_bar_any(qbar, bad0, QBAR_THREADS);
     if (!bad) {
       tc::fence_after();
-      float o_acc[DH];
-      if (n_tiles > 0) {
-        constexpr int C = DH < 32 ? DH : 32;
-#pragma unroll
-        for (int c = 0; c < DH / C; ++c) {
-          float tcv[C];
-          tc::tmem_ld<C>(o_row + cg * DH + c * C, tcv);
-#pragma unroll
-          for (int j2 = 0; j2 < C; ++j2) o_acc[c * C + j2] = tcv[j2];
-        }
-      } else {
-#pragma unroll
-        for (int j2 = 0; j2 < DH; ++j2) o_acc[j2] = 0.0f;
-      }
+      // 32 columns at a time (DH is up to 128 fp32 accumulators per thread)
+      float inv = 0.0f;
       if (row_ok) {
         float l_tot = 0.0f;
 #pragma unroll
         for (int g2 = 0; g2 < CG; ++g2) l_tot += rx[g2 * 128 + r];
         const bool sink = p.sinks != nullptr;
-        const float inv =
-            softmax_out_factor(m_run, l_tot, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
-        const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + cg * DH;
+        inv = softmax_out_factor(m_run, l_tot, sink, sink ? p.sinks[hq] * 1.4426950408889634f : 0.0f);
+      }
+      const int64_t ob = (int64_t)b * p.osb + (int64_t)hq * p.osh + (int64_t)l * p.osl + cg * DH;
+      constexpr int C = DH < 32 ? DH : 32;
+#pragma unroll 1
+      for (int c = 0; c < DH / C; ++c) {
+        float o_acc[C];
+        if (n_tiles > 0) {
+          float tcv[C];
+          __syncwarp();  // tcgen05.ld is warp-collective: converge after the previous chunk's stores
+          tc::tmem_ld<C>(o_row + cg * DH + c * C, tcv);
+#pragma unroll
+          for (int j2 = 0; j2 < C; ++j2)  // (QV4: columns back in element order)
+            o_acc[QV4 ? q4_chunk_elem(j2) : j2] = tcv[j2];
+        } else {
+#pragma unroll
+          for (int j2 = 0; j2 < C; ++j2) o_acc[j2] = 0.0f;
+        }
+        if (!row_ok) continue;  // (no collective below)
         if (p.out_dtype == AM_DTYPE_F32) {
-          float* o = static_cast<float*>(p.out) + ob;
+          float* o = static_cast<float*>(p.out) + ob + c * C;
           if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
-            for (int d = 0; d < DH; d += 4)
+            for (int d = 0; d < C; d += 4)
               *reinterpret_cast<float4*>(o + d) =
                   make_float4(o_acc[d] * inv, o_acc[d + 1] * inv, o_acc[d + 2] * inv, o_acc[d + 3] * inv);
           } else {
 #pragma unroll
-            for (int d = 0; d < DH; ++d) o[d] = o_acc[d] * inv;
+            for (int d = 0; d < C; ++d) o[d] = o_acc[d] * inv;
           }
         } else {
           const bool bf = p.out_dtype == AM_DTYPE_BF16;
-          uint16_t* o = static_cast<uint16_t*>(p.out) + ob;
+          uint16_t* o = static_cast<uint16_t*>(p.out) + ob + c * C;
           if ((reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
-            for (int d = 0; d < DH; d += 8) {
+            for (int d = 0; d < C; d += 8) {
               uint32_t w[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
@@ -903,7 +1149,7 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
             }
           } else {
 #pragma unroll
-            for (int d = 0; d < DH; ++d) o[d] = bf ? f2h<true>(o_acc[d] * inv) : f2h<false>(o_acc[d] * inv);
+            for (int d = 0; d < C; ++d) o[d] = bf ? f2h<true>(o_acc[d] * inv) : f2h<false>(o_acc[d] * inv);
           }
         }
       }
@@ -917,13 +1163,13 @@ __global__ void __launch_bounds__(SoftmaxGeom<BN>::CTA_THREADS, 1)
   __syncthreads();
   if (*abort_flag) {
     constexpr uint64_t kDrainNs = 100000000ull;
-    if (warp == SG::TMA_WARP && lane == 0) {
+    if (warp == RL::TMA_WARP && lane == 0) {
       for (int jj = max(0, issued_k - NS); jj < issued_k; ++jj)
         mbar_wait_bounded(bar(LY::B_KFULL + jj % NS), (jj / NS) & 1, kDrainNs);
-      for (int jj = max(0, issued_v - NSV); jj < issued_v; ++jj)
+      for (int jj = max(0, issued_v - NSV); jj < issued_v; ++jj)  // (QV4: none issued)
         mbar_wait_bounded(bar(LY::B_VFULL + jj % NSV), (jj / NSV) & 1, kDrainNs);
     }
-    if (warp == SG::MMA_WARP && lane == 0 && mma_issued) {
+    if (warp == RL::MMA_WARP && lane == 0 && mma_issued) {
       tc::commit(bar(LY::B_DRAIN));
       mbar_wait_bounded(bar(LY::B_DRAIN), 0, kDrainNs);
     }
@@ -1483,6 +1729,8 @@ bool prefill_supported(int k_dim, int v_dim) {
 // Head dims up to 128 take the two-tile kernel (128-key tiles); the others the one-tile kernel.
 static bool prefill_two_tiles(int k_dim, int v_dim) { return k_dim <= 128 && v_dim <= 128; }
 
+bool prefill_v_in_kernel(int k_dim, int v_dim) { return k_dim == 192 && v_dim == 128; }
+
 int prefill_key_tile(int k_dim, int v_dim) {
   return prefill_two_tiles(k_dim, v_dim) ? 128 : ((k_dim + v_dim) > 384 ? 64 : 128);
 }
@@ -1513,7 +1761,7 @@ static cudaError_t prefill_smem_once(F kfn, int bytes, unsigned long long* done_
 template <int DK, int DV, bool SBF16, bool PAGED>
 static cudaError_t launch_stage_t(const DecodeParams& p, int batch, cudaStream_t stream) {
   dim3 grid((p.nw + kStageRows - 1) / kStageRows, p.hkv, batch);
-  prefill_stage_kernel<DK, DV, SBF16, PAGED><<<grid, 256, 0, stream>>>(p);
+  prefill_stage_kernel<DK, DV, SBF16, PAGED, kPrefillVInKernel<DK, DV>><<<grid, 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -1533,13 +1781,14 @@ static cudaError_t launch_attn_t(const DecodeParams& p, int batch, cudaStream_t 
     cfg.dynamicSmemBytes = C::LY::SMEM;
   } else {
     using C = PrefillCfg<DK, DV>;
-    kfn = prefill_kernel<DK, DV, C::BN, C::NS, C::NSV, DENSE>;
+    constexpr bool QV4 = kPrefillVInKernel<DK, DV>;
+    kfn = prefill_kernel<DK, DV, C::BN, C::NS, C::NSV, DENSE, QV4>;
     static unsigned long long done = 0;
     cudaError_t e = prefill_smem_once(kfn, C::LY::SMEM, &done);
     if (e != cudaSuccess) return e;
     const int tok_per_cta = 128 / p.n_rep;
     cfg.gridDim = dim3((p.q_len + tok_per_cta - 1) / tok_per_cta, p.hkv, batch);
-    cfg.blockDim = dim3(SoftmaxGeom<C::BN>::CTA_THREADS);
+    cfg.blockDim = dim3(PrefillRoles<C::BN, QV4>::THREADS);
     cfg.dynamicSmemBytes = C::LY::SMEM;
   }
   cfg.stream = stream;
@@ -1558,8 +1807,11 @@ static cudaError_t launch_attn_t(const DecodeParams& p, int batch, cudaStream_t 
 }
 
 template <int DK, int DV>
-static cudaError_t launch_prefill_dims(const DecodeParams& p, int batch, bool paged, bool sbf16,
+static cudaError_t launch_prefill_dims(const DecodeParams& p0, int batch, bool paged, bool sbf16,
                                        cudaStream_t stream) {
+  DecodeParams p = p0;  // (the attention kernel's V dequantization reads the cache directly)
+  p.paged = paged ? 1 : 0;
+  p.scale_bf16 = sbf16 ? 1 : 0;
   cudaError_t e = paged ? (sbf16 ? launch_stage_t<DK, DV, true, true>(p, batch, stream)
                                  : launch_stage_t<DK, DV, false, true>(p, batch, stream))
                         : (sbf16 ? launch_stage_t<DK, DV, true, false>(p, batch, stream)

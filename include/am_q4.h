@@ -160,7 +160,8 @@ int am_q4_append(const am_q4_cache* cache, const void* k, const void* v, int32_t
  * Workspace sizing (bytes; 0 = none needed).  am_q4_decode_workspace_bytes: the split-KV
  * partials of am_q4_decode.  am_q4_prefill_workspace_bytes: the fp16 rows of the keys and
  * values a prefill call can see (batch x n_kv_heads x span x (k_dim + v_dim) x 2 bytes, the
- * span being max_kv_len, or window + q_len - 1 with a sliding window).
+ * span being max_kv_len, or window + q_len - 1 with a sliding window; k_dim x 2 bytes per
+ * row for k_dim 192 / v_dim 128, whose values the attention kernel dequantizes itself).
  * am_q4_attention_workspace_bytes: what am_q4_attention needs for the kernel it dispatches
  * to.  The reference's compiled path allocates its intermediates inside mlx
  * (mlx_fused_attention.py:86-109); here the caller owns that memory.
@@ -197,7 +198,8 @@ int am_q4_decode_noalloc(const am_q4_cache* cache, const am_attn_args* args, voi
  * (192, 128), (256, 256).  Two launches on `stream`: the keys and values the query block
  * can see are dequantized once into fp16 rows of `workspace` (256-byte aligned, at least
  * am_q4_prefill_workspace_bytes), then the attention kernel streams them to the tensor
- * cores.  Dequantized values beyond fp16's range saturate at +-65504.
+ * cores (for (192, 128) only the keys: that kernel dequantizes the values from the cache
+ * itself).  Dequantized values beyond fp16's range saturate at +-65504.
  */
 int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* args, void* workspace,
                   size_t workspace_bytes, void* stream);

@@ -210,3 +210,45 @@ def test_prefill_scores_that_jump_between_tiles(cuda, orc, trend, dims):
                                 out_dtype=torch.float32, mode="prefill")
     want = oracle(orc, q, kq, vq, dk ** -0.5, causal=True)
     assert_close(got.cpu().numpy(), want, what=f"prefill {trend} scores {dims}")
+
+
+@pytest.mark.parametrize("geom", [(4, 4, 192, 128), (8, 4, 256, 256)], ids=["k192_v128", "d256"])
+def test_prefill_values_beyond_fp16_saturate(cuda, orc, geom):
+    """A bf16 cache can hold groups whose dequantized values leave fp16's range.  Every
+    prefill path saturates them at +-65504 (the attention kernels' fp16 operands): the K
+    plane in the stage kernel, and for these head dims the V tiles dequantized inside the
+    attention kernel, whose f16x2 conversion hands such groups to an fp32 path.  Keys a
+    query cannot see therefore still contribute exactly 0 (no 0 * inf), and the outputs
+    match an fp64 attention over the saturated values."""
+    Hq, Hkv, dk, dv = geom
+    B, N, L = 1, 300, 100
+    g = torch.Generator().manual_seed(17)
+    k = torch.randn(B, Hkv, N, dk, generator=g)
+    v = torch.randn(B, Hkv, N, dv, generator=g)
+    # keys 250..269 (visible to queries at positions >= 250 only): the first 64-element V
+    # group spans 5e4 .. 9e4, so codes above ~6 dequantize beyond 65504
+    v[:, :, 250:270, :64] = 5.0e4 + 4.0e4 * torch.rand(B, Hkv, 20, 64, generator=g)
+    v[:, :, 250:270, 0] = 5.0e4
+    v[:, :, 250:270, 1] = 9.0e4
+    kq = pkg.quantize(k.bfloat16().to(cuda))
+    vq = pkg.quantize(v.bfloat16().to(cuda))
+    q = torch.randn(B, Hq, L, dk, generator=g).bfloat16()
+    view, n = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), n, dtype=torch.int32, device=cuda)
+    got = pkg.kernels.attention(view, q.to(cuda), dk ** -0.5, kv_len, n, causal=True,
+                                out_dtype=torch.float32, mode="prefill")
+    assert torch.isfinite(got).all()
+    sat = lambda x: np.clip(x.astype(np.float64), -65504.0, 65504.0)
+    kd = sat(orc.dequantize(*(_bits(t) for t in kq), dtype=1))  # [B, Hkv, N, dk]
+    vd = sat(orc.dequantize(*(_bits(t) for t in vq), dtype=1))
+    qf = q.float().numpy().astype(np.float64)
+    n_rep = Hq // Hkv
+    want = np.zeros((B, Hq, L, dv))
+    for hq in range(Hq):
+        s = qf[0, hq] @ kd[0, hq // n_rep].T * dk ** -0.5  # [L, N]
+        pos = N - L + np.arange(L)
+        s[np.arange(N)[None, :] > pos[:, None]] = -np.inf
+        p = np.exp(s - s.max(axis=1, keepdims=True))
+        want[0, hq] = (p / p.sum(axis=1, keepdims=True)) @ vd[0, hq // n_rep]
+    assert np.abs(want).max() > 1.0e4  # the saturated keys carry weight for later queries
+    assert_close(got.cpu().numpy(), want, what=f"prefill {geom}, V beyond the fp16 range")

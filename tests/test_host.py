@@ -148,18 +148,21 @@ def _prefill_desc_args(k_dim, v_dim, hkv, hq, batch, q_len, max_kv_len, window=0
 def test_prefill_workspace_sizing(dims):
     """The prefill workspace holds fp16 rows of every key the block can see, per (sequence,
     KV head): max_kv_len keys, or window + q_len - 1 with a sliding window; K rows first,
-    V rows after them on a 256-byte boundary.  am_q4_attention sizes for the kernel it
-    dispatches to."""
+    V rows after them on a 256-byte boundary -- except for MLA's K192 / V128, whose
+    attention kernel dequantizes V itself (K rows only).  am_q4_attention sizes for the
+    kernel it dispatches to."""
     lib = pkg._lib.load()
     dk, dv = dims
+    v_rows = (dk, dv) != (192, 128)
     d, a = _prefill_desc_args(dk, dv, 8, 32, 2, 512, 4608)
-    want = 2 * 8 * 4608 * (dk + dv) * 2
+    want = 2 * 8 * 4608 * (dk + (dv if v_rows else 0)) * 2
     assert lib.am_q4_prefill_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == want
     assert lib.am_q4_attention_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == want
     a.window = 1024  # window + q_len - 1 = 1535 keys, rounded up to 1536 rows
     rows = 2 * 8 * 1536
     k_bytes = (rows * dk * 2 + 255) // 256 * 256
-    assert lib.am_q4_prefill_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == k_bytes + rows * dv * 2
+    assert lib.am_q4_prefill_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == \
+        k_bytes + (rows * dv * 2 if v_rows else 0)
     a.q_len = 1  # decode-shaped: am_q4_attention takes the split-KV kernel
     assert lib.am_q4_attention_workspace_bytes(ctypes.byref(d), ctypes.byref(a)) == \
         lib.am_q4_decode_workspace_bytes(ctypes.byref(d), ctypes.byref(a))
