@@ -305,6 +305,67 @@ __device__ __forceinline__ void prefill_block_range(const DecodeParams& p, int b
   lo = min(lo, hi);
 }
 
+// ---------------------------------------------------------------- query tiles
+// A thread stages CH 16-byte chunks (8 elements each) of a query row: all loads issued at
+// once (one memory latency per CTA prologue rather than one per chunk), the row's max |q|
+// taken from the registers, then each chunk converted to fp16 times a power of two and
+// stored into the 128-byte-swizzled query tile.
+template <int CH>
+__device__ __forceinline__ void q_chunks_load(const uint16_t* src, bool ok, uint4 (&raw)[CH]) {
+  if (ok) {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) raw[c] = *reinterpret_cast<const uint4*>(src + c * 8);
+  } else {
+#pragma unroll
+    for (int c = 0; c < CH; ++c) raw[c] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int CH>
+__device__ __forceinline__ float q_chunks_amax(const uint4 (&raw)[CH], bool bf16) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const uint32_t u[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      amax = fmaxf(amax, fabsf(h2f_rt(u[i] & 0xffffu, bf16)));
+      amax = fmaxf(amax, fabsf(h2f_rt(u[i] >> 16, bf16)));
+    }
+  }
+  return amax;
+}
+
+// The power of two that puts a row's max |q| just below 2^15 (1 for an empty or non-finite
+// row), negated for a negative softmax scale so the factor back to scaled log2 scores is
+// always positive.
+__device__ __forceinline__ float q_row_prescale(float amax, float scale_log2) {
+  float pw = 1.0f;
+  if (amax > 0.0f && isfinite(amax)) {
+    int e;
+    frexpf(amax, &e);
+    pw = ldexpf(1.0f, 15 - e);
+  }
+  return scale_log2 < 0.0f ? -pw : pw;
+}
+
+// Chunks c0 .. c0 + CH - 1 of row r into a query tile of 64-element slabs (QSLAB bytes).
+template <int CH>
+__device__ __forceinline__ void q_chunks_store(uint8_t* tile, int qslab, const uint4 (&raw)[CH], float pw,
+                                               bool bf16, int r, int c0) {
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const uint32_t u[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+    uint32_t o4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o4[i] = pack_half2(h2f_rt(u[i] & 0xffffu, bf16) * pw, h2f_rt(u[i] >> 16, bf16) * pw);
+    const int cc = c0 + c;
+    const uint32_t off = (cc / 8) * qslab + r * 128 + (cc % 8) * 16;
+    *reinterpret_cast<uint4*>(tile + (off ^ (((off >> 7) & 7u) << 4))) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+  }
+}
+
 // ---------------------------------------------------------------- stage kernel
 // grid (ceil(nw / kStageRows), Hkv, batch), 256 threads.  A block converts kStageRows rows of
 // plane (b, h); the work items are 16-byte chunks of code words (32 elements each, K chunks
@@ -727,52 +788,23 @@ __global__ void __launch_bounds__(PrefillRoles<BN, QV4>::THREADS, 1)
                  "r"(LY::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
   }
-  if (tid < 128) {
-    // query row r -> fp16 with a power-of-two prescale (exact for fp16 / bf16 inputs)
-    const int r = tid;
+  if (tid < 256) {
+    // query row r -> fp16 with a power-of-two prescale (exact for fp16 / bf16 inputs); two
+    // threads per row (adjacent lanes), each staging half of it
+    const int r = tid >> 1, half = tid & 1;
+    constexpr int CH = DK / 16;
     const int rl = r / n_rep;
     const bool row_ok = r < tok_per_cta * n_rep && l0 + rl < p.q_len;
     const int l = l0 + (row_ok ? rl : 0);
     const int hq = h * n_rep + r % n_rep;
     const uint16_t* qrow = p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl;
-    float amax = 0.0f;
-    if (row_ok) {
-#pragma unroll 1
-      for (int c = 0; c < DK / 8; ++c) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          amax = fmaxf(amax, fabsf(h2f_rt(u[i] & 0xffffu, p.q_bf16)));
-          amax = fmaxf(amax, fabsf(h2f_rt(u[i] >> 16, p.q_bf16)));
-        }
-      }
-    }
-    float pw = 1.0f;
-    if (amax > 0.0f && isfinite(amax)) {
-      int e;
-      frexpf(amax, &e);
-      pw = ldexpf(1.0f, 15 - e);
-    }
-    // a negative softmax scale negates the stored query row, so the factor that turns raw
-    // scores into scaled log2 scores is always positive
-    if (p.scale_log2 < 0.0f) pw = -pw;
-    sqf[r] = p.scale_log2 / pw;
-#pragma unroll 1
-    for (int c = 0; c < DK / 8; ++c) {
-      uint4 outv = make_uint4(0, 0, 0, 0);
-      if (row_ok) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-        uint32_t o4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o4[i] = pack_half2(h2f_rt(u[i] & 0xffffu, p.q_bf16) * pw, h2f_rt(u[i] >> 16, p.q_bf16) * pw);
-        outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
-      }
-      const uint32_t off = (c / 8) * LY::QSLAB + r * 128 + (c % 8) * 16;
-      *reinterpret_cast<uint4*>(smem + LY::OFF_Q + (off ^ (((off >> 7) & 7u) << 4))) = outv;
-    }
+    uint4 raw[CH];
+    q_chunks_load<CH>(qrow + half * (DK / 2), row_ok, raw);
+    float amax = q_chunks_amax<CH>(raw, p.q_bf16 != 0);
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    const float pw = q_row_prescale(amax, p.scale_log2);
+    if (half == 0) sqf[r] = p.scale_log2 / pw;
+    q_chunks_store<CH>(smem + LY::OFF_Q, LY::QSLAB, raw, pw, p.q_bf16 != 0, r, half * CH);
   }
   fence_proxy_async_smem();
   tc::fence_before();
@@ -1318,50 +1350,19 @@ __global__ void __launch_bounds__(kTile2Threads, 1) prefill2_kernel(const __grid
   }
   if (tid < 256) {
     // query row R = tid of the CTA (tile R / 128, row R % 128) -> fp16 with a power-of-two
-    // prescale (exact for fp16 / bf16 inputs); a negative softmax scale negates the row, so
-    // the factor back to scaled log2 scores is always positive
+    // prescale (exact for fp16 / bf16 inputs)
     const int qt = tid >> 7, r = tid & 127;
+    constexpr int CH = DK / 8;
     const int rl = r / n_rep;
     const bool row_ok = r < tpq * n_rep && l0 + qt * tpq + rl < p.q_len;
     const int l = l0 + qt * tpq + (row_ok ? rl : 0);
     const int hq = h * n_rep + r % n_rep;
     const uint16_t* qrow = p.q + (int64_t)b * p.qsb + (int64_t)hq * p.qsh + (int64_t)l * p.qsl;
-    float amax = 0.0f;
-    if (row_ok) {
-#pragma unroll 1
-      for (int c = 0; c < DK / 8; ++c) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          amax = fmaxf(amax, fabsf(h2f_rt(u[i] & 0xffffu, p.q_bf16)));
-          amax = fmaxf(amax, fabsf(h2f_rt(u[i] >> 16, p.q_bf16)));
-        }
-      }
-    }
-    float pw = 1.0f;
-    if (amax > 0.0f && isfinite(amax)) {
-      int e;
-      frexpf(amax, &e);
-      pw = ldexpf(1.0f, 15 - e);
-    }
-    if (p.scale_log2 < 0.0f) pw = -pw;
+    uint4 raw[CH];
+    q_chunks_load<CH>(qrow, row_ok, raw);
+    const float pw = q_row_prescale(q_chunks_amax<CH>(raw, p.q_bf16 != 0), p.scale_log2);
     sqf[tid] = p.scale_log2 / pw;
-#pragma unroll 1
-    for (int c = 0; c < DK / 8; ++c) {
-      uint4 outv = make_uint4(0, 0, 0, 0);
-      if (row_ok) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-        uint32_t o4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o4[i] = pack_half2(h2f_rt(u[i] & 0xffffu, p.q_bf16) * pw, h2f_rt(u[i] >> 16, p.q_bf16) * pw);
-        outv = make_uint4(o4[0], o4[1], o4[2], o4[3]);
-      }
-      const uint32_t off = (c / 8) * LY::QSLAB + r * 128 + (c % 8) * 16;
-      *reinterpret_cast<uint4*>(smem + LY::OFF_Q + qt * LY::QTILE + (off ^ (((off >> 7) & 7u) << 4))) = outv;
-    }
+    q_chunks_store<CH>(smem + LY::OFF_Q + qt * LY::QTILE, LY::QSLAB, raw, pw, p.q_bf16 != 0, r, 0);
   }
   fence_proxy_async_smem();
   tc::fence_before();
