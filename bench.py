@@ -7,7 +7,9 @@ random pool offsets through per-agent block tables, one fp16 query token per age
 A step = for every layer: quantize-on-append of the step's new K/V token of every agent,
 then split-KV decode attention of every agent over its blocks.  Agents are partitioned
 across ranks by balanced token count (greedy LPT); there is no collective on the data
-path (strong scaling: the 256 agents are fixed, each rank decodes its share).
+path.  Weak scaling by default: a job on N GPUs is N x 256 agents drawn from the same
+distribution and LPT-partitioned, so each rank decodes ~256 agents (the configuration's
+per-GPU size); `--scaling strong` keeps the 256 agents fixed and gives each rank its share.
 
 Other workloads (--workload): llama_layer, gemma, mla (single-instance decode), prefill
 (Llama chunked prefill), gemma_prefill, mla_prefill (512-token chunks on the Gemma-3 and
@@ -49,7 +51,10 @@ def parse():
     p.add_argument("--workload", default="multi_agent",
                    choices=["multi_agent", "llama_layer", "gemma", "mla", "prefill",
                             "gemma_prefill", "mla_prefill"])
-    p.add_argument("--agents", type=int, default=256)
+    p.add_argument("--agents", type=int, default=256,
+                   help="agents per GPU (weak scaling) or in total (strong scaling)")
+    p.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                   help="weak: N GPUs decode N x --agents agents; strong: --agents in total")
     p.add_argument("--layers", type=int, default=None)
     p.add_argument("--min-len", type=int, default=1024)
     p.add_argument("--max-len", type=int, default=32768)
@@ -199,6 +204,11 @@ def agent_lengths(n_agents, lo, hi, seed):
     return rng.integers(lo, hi + 1, size=n_agents).tolist()
 
 
+def job_agents(args, world):
+    """Agents in the whole job: --agents per GPU under weak scaling, in total under strong."""
+    return args.agents * world if args.scaling == "weak" else args.agents
+
+
 def q4_bytes_per_token(hkv, dk, dv):
     return hkv * (dk // 2 + dk // 16 + dv // 2 + dv // 16)
 
@@ -221,7 +231,8 @@ def run_ours(args, rank, world, local_rank):
     geo = LLAMA
     layers = args.layers or geo["layers"]
     hq, hkv, dk, dv = geo["hq"], geo["hkv"], geo["dk"], geo["dv"]
-    lengths_all = agent_lengths(args.agents, args.min_len, args.max_len, args.seed)
+    n_total = job_agents(args, world)
+    lengths_all = agent_lengths(n_total, args.min_len, args.max_len, args.seed)
     parts = am.lpt_partition(lengths_all, world)
     mine = sorted(parts[rank])
     lens = [lengths_all[i] for i in mine]
@@ -318,7 +329,7 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms_max = float(tt.item())
     ms_per_step = ms_max / args.steps
-    tokens_per_step = args.agents if world > 1 or A == args.agents else A
+    tokens_per_step = n_total if world > 1 or A == n_total else A
     value = tokens_per_step / (ms_per_step / 1e3)
 
     # roofline of the decode attention call (split-KV kernel, plus the combine kernel when
@@ -437,10 +448,10 @@ def run_ours(args, rank, world, local_rank):
             "metric": "Q4-KV decode attention tokens/s (whole job) and achieved HBM GB/s vs peak",
             "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f16",
             "data": "synthetic: seeded N(0,1) fp16 K/V/queries, Q4 group-64 (no dataset)",
             "config": {"workload": "multi_agent_block_pool_decode", "model_shape": "Llama-3.1-8B KV",
-                       "agents": args.agents, "agents_this_rank0": A, "layers": layers,
+                       "agents": n_total, "agents_this_rank0": A, "layers": layers,
                        "n_q_heads": hq, "n_kv_heads": hkv, "head_dim": dk,
                        "context": f"U[{args.min_len},{args.max_len}] seed {args.seed}",
                        "total_context_tokens": int(sum(lengths_all)), "block_tokens": bt,
@@ -471,7 +482,7 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line))
 
 
-def measure_config(w, am, dev, steps=5, warmup=3, seed=0):
+def measure_config(w, am, dev, steps=5, warmup=3, seed=0, layers_override=None):
     """One of the single-instance configurations, timed on this GPU; returns its record.
 
     llama_layer / gemma / mla: decode attention over a contiguous Q4 cache (one Llama layer,
@@ -502,6 +513,8 @@ def measure_config(w, am, dev, steps=5, warmup=3, seed=0):
         return measure_prefill(am, dev, steps, warmup, gen, w)
     else:
         raise ValueError(w)
+    if layers_override and w != "llama_layer":
+        layers = layers_override  # a shorter step of the same layer shapes (profiling)
     inst = layers * reps
     qdt = torch.float16
     kv = []
@@ -687,7 +700,8 @@ def run_single_workload(args, am, dev, rank, world):
     import torch
     import torch.distributed as dist
 
-    rec = measure_config(args.workload, am, dev, steps=args.steps, warmup=args.warmup, seed=args.seed)
+    rec = measure_config(args.workload, am, dev, steps=args.steps, warmup=args.warmup, seed=args.seed,
+                         layers_override=args.layers)
     ms = rec["ms_per_step"]
     if world > 1:
         tt = torch.tensor([ms], device=dev)
@@ -782,13 +796,13 @@ def run_reference(args, rank, world):
     """The reference arm: the C restatement of the path on the host cores (the reference's own
     CPU backend, mlx, is not installed).  A step is one decode pass of one layer over a sample
     of agents held in a paged Q4 pool, timed as it runs; its tokens/s counts the step as the
-    share of the full job's Q4 bytes it reads (256 agents x 32 layers x 144 B per token per KV
-    head), so ms_per_step is the measured time of the sample step."""
+    share of the full job's Q4 bytes it reads (the job's agents x 32 layers x 144 B per token
+    per KV head), so ms_per_step is the measured time of the sample step."""
     if rank != 0:
         return
     geo = LLAMA
     layers = args.layers or geo["layers"]
-    lengths_all = agent_lengths(args.agents, args.min_len, args.max_len, args.seed)
+    lengths_all = agent_lengths(job_agents(args, world), args.min_len, args.max_len, args.seed)
     sampler = cpu_sampler(lengths_all, layers, geo)  # the sample is built once, then timed
     for _ in range(args.warmup):
         sampler.once()
@@ -805,9 +819,9 @@ def run_reference(args, rank, world):
         "metric": "Q4-KV decode attention tokens/s (whole job) and achieved HBM GB/s vs peak",
         "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: seeded N(0,1) fp16 K/V/queries, Q4 group-64",
-        "config": {"workload": "multi_agent_block_pool_decode", "agents": args.agents,
+        "config": {"workload": "multi_agent_block_pool_decode", "agents": len(lengths_all),
                    "layers": layers, "context": f"U[{args.min_len},{args.max_len}]",
                    "step": f"1 layer of decode over {sampler.sample_agents} agents' paged Q4 "
                            f"blocks ({step_gb:.3f} GB, {100 * sampler.fraction:.3f}% of a full "

@@ -1,7 +1,8 @@
 """World-size-2 gloo run of the multi-GPU harness's host logic on CPU: every rank derives
 the same seeded agent lengths, takes its LPT share, the shares are disjoint and cover all
 agents, and the step time reported is the max over ranks (no collective on the data
-path, only this timing reduction)."""
+path, only this timing reduction).  Under weak scaling the job is 256 agents per rank;
+under strong scaling 256 agents in total."""
 
 import os
 import socket
@@ -20,7 +21,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, scaling):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
     import sys
@@ -34,7 +35,10 @@ def _worker(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
     try:
-        lens = bench.agent_lengths(256, 1024, 32768, 0)
+        import argparse
+
+        job = bench.job_agents(argparse.Namespace(agents=256, scaling=scaling), world)
+        lens = bench.agent_lengths(job, 1024, 32768, 0)
         mine = sorted(am.lpt_partition(lens, world)[rank])
         got = [None] * world
         dist.all_gather_object(got, mine)
@@ -45,11 +49,12 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_two_rank_partition_and_max_timing():
+@pytest.mark.parametrize("scaling,job", [("weak", 512), ("strong", 256)])
+def test_two_rank_partition_and_max_timing(scaling, job):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, scaling)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]
@@ -60,7 +65,7 @@ def test_two_rank_partition_and_max_timing():
     shares = res[0][1]
     assert res[1][1] == shares
     flat = sorted(i for s in shares for i in s)
-    assert flat == list(range(256)) and not set(shares[0]) & set(shares[1])
+    assert flat == list(range(job)) and not set(shares[0]) & set(shares[1])
     assert res[0][2] == res[1][2] == 11.0
     loads = [r[3] for r in res]
     assert max(loads) / min(loads) < 1.01
