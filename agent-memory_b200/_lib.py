@@ -15,7 +15,7 @@ PKG_DIR = Path(__file__).resolve().parent
 LIB_NAME = "libamq4.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # Status codes / enums (mirrors include/am_q4.h)
 AM_OK = 0
@@ -40,6 +40,8 @@ EXPORTED_SYMBOLS = (
     "am_q4_attention_workspace_bytes",
     "am_q4_decode",
     "am_q4_prefill",
+    "am_q4_prefill_stage",
+    "am_q4_prefill_attend",
     "am_q4_attention",
     "am_q4_decode_noalloc",
     "am_q4_blocks_pack",
@@ -162,11 +164,14 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
         f = getattr(lib, fn)
         f.argtypes = [ctypes.POINTER(Q4CacheDesc), ctypes.POINTER(AttnArgs)]
         f.restype = c_size_t
-    for fn in ("am_q4_decode", "am_q4_prefill", "am_q4_attention"):
+    for fn in ("am_q4_decode", "am_q4_prefill", "am_q4_prefill_attend", "am_q4_attention"):
         f = getattr(lib, fn)
         f.argtypes = [ctypes.POINTER(Q4CacheDesc), ctypes.POINTER(AttnArgs), c_void_p, c_size_t,
                       c_void_p]
         f.restype = c_int32
+    lib.am_q4_prefill_stage.argtypes = [ctypes.POINTER(Q4CacheDesc), ctypes.POINTER(AttnArgs),
+                                        c_int32, c_int32, c_void_p, c_size_t, c_void_p]
+    lib.am_q4_prefill_stage.restype = c_int32
     lib.am_q4_decode_noalloc.argtypes = [ctypes.POINTER(Q4CacheDesc), ctypes.POINTER(AttnArgs),
                                          c_void_p]
     lib.am_q4_decode_noalloc.restype = c_int32

@@ -486,27 +486,34 @@ int am_q4_decode(const am_q4_cache* cache, const am_attn_args* a, void* workspac
                      "am_q4_decode");
 }
 
-int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
-                  size_t workspace_bytes, void* stream) {
+// One prefill call: the stage kernel over the keys in [key_lo, key_hi) and/or the attention
+// kernel (parts), with the checks every prefill entry point shares.
+static int prefill_call(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
+                        size_t workspace_bytes, void* stream, int key_lo, int key_hi, int parts,
+                        const char* fn) {
   clear_error();
-  int rc = check_cache(cache, "am_q4_prefill");
+  int rc = check_cache(cache, fn);
   if (rc) return rc;
-  rc = check_args(cache, a, "am_q4_prefill");
+  rc = check_args(cache, a, fn);
   if (rc) return rc;
   if (!prefill_supported(cache->k_dim, cache->v_dim)) {
-    set_error("am_q4_prefill: no kernel for k_dim=%d v_dim=%d", cache->k_dim, cache->v_dim);
+    set_error("%s: no kernel for k_dim=%d v_dim=%d", fn, cache->k_dim, cache->v_dim);
     return AM_ERR_UNSUPPORTED;
+  }
+  if (key_lo < 0 || key_hi < key_lo) {
+    set_error("%s: key range [%d, %d) is not a range of key positions", fn, key_lo, key_hi);
+    return AM_ERR_INVALID;
   }
   if (a->batch == 0 || a->q_len == 0) return AM_OK;
   const PrefillPlanes pl = prefill_planes(cache, a);
   const size_t need = pl.k_bytes + pl.v_bytes;
   if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256)) {
-    set_error("am_q4_prefill: a 256-byte aligned workspace of %zu bytes is required (got %zu)", need,
+    set_error("%s: a 256-byte aligned workspace of %zu bytes is required (got %zu)", fn, need,
               workspace_bytes);
     return AM_ERR_WORKSPACE;
   }
   if (pl.rows <= 0 || pl.rows > INT_MAX) {
-    set_error("am_q4_prefill: %lld workspace rows (sequences x KV heads x keys) outside (0, 2^31)",
+    set_error("%s: %lld workspace rows (sequences x KV heads x keys) outside (0, 2^31)", fn,
               static_cast<long long>(pl.rows));
     return AM_ERR_UNSUPPORTED;
   }
@@ -515,17 +522,37 @@ int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* workspa
   p.kd = static_cast<uint16_t*>(workspace);
   p.vd = pl.v_bytes > 0 ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + pl.k_bytes) : nullptr;
   p.nw = pl.nw;
+  p.stage_lo = key_lo;
+  p.stage_hi = key_hi;
   const int bn = prefill_key_tile(cache->k_dim, cache->v_dim);
   if (!encode_codes_map(&p.tmap_kd, p.kd, pl.rows, cache->k_dim * 2, 128, bn) ||
       (pl.v_bytes > 0 && !encode_codes_map(&p.tmap_vd, p.vd, pl.rows, cache->v_dim * 2, 128, bn))) {
-    set_error("am_q4_prefill: cannot describe the workspace as tensor maps (a driver with "
-              "cuTensorMapEncodeTiled is required)");
+    set_error("%s: cannot describe the workspace as tensor maps (a driver with "
+              "cuTensorMapEncodeTiled is required)", fn);
     return AM_ERR_CUDA;
   }
   return cuda_status(launch_prefill(p, a->batch, cache->layout == AM_LAYOUT_PAGED,
-                                    cache->scale_dtype == AM_DTYPE_BF16,
+                                    cache->scale_dtype == AM_DTYPE_BF16, parts,
                                     static_cast<cudaStream_t>(stream)),
-                     "am_q4_prefill");
+                     fn);
+}
+
+int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  return prefill_call(cache, a, workspace, workspace_bytes, stream, 0, INT_MAX,
+                      kPrefillStage | kPrefillAttend, "am_q4_prefill");
+}
+
+int am_q4_prefill_stage(const am_q4_cache* cache, const am_attn_args* a, int32_t key_lo,
+                        int32_t key_hi, void* workspace, size_t workspace_bytes, void* stream) {
+  return prefill_call(cache, a, workspace, workspace_bytes, stream, key_lo, key_hi, kPrefillStage,
+                      "am_q4_prefill_stage");
+}
+
+int am_q4_prefill_attend(const am_q4_cache* cache, const am_attn_args* a, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  return prefill_call(cache, a, workspace, workspace_bytes, stream, 0, INT_MAX, kPrefillAttend,
+                      "am_q4_prefill_attend");
 }
 
 int am_q4_attention(const am_q4_cache* cache, const am_attn_args* a, void* workspace,

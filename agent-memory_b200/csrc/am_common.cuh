@@ -374,6 +374,10 @@ struct DecodeParams {
   uint16_t* kd;
   uint16_t* vd;
   int32_t nw;  // rows per (sequence, KV head) plane
+  // The stage kernel writes only the rows of keys in [stage_lo, stage_hi) (absolute key
+  // positions); am_q4_prefill stages every row, am_q4_prefill_stage a range of them.
+  int32_t stage_lo;
+  int32_t stage_hi;
   // Prefill kernels that dequantize V tiles themselves read the cache directly: block-pool
   // layout (table, block_tokens) or contiguous rows, and the scale / bias type.
   int32_t paged;

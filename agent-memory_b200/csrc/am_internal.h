@@ -33,9 +33,11 @@ bool prefill_supported(int k_dim, int v_dim);
 int prefill_key_tile(int k_dim, int v_dim);
 // True when the attention kernel dequantizes V itself (the workspace then holds K rows only).
 bool prefill_v_in_kernel(int k_dim, int v_dim);
-// Stage kernel (Q4 -> fp16 workspace rows) then attention kernel; p.kd / p.vd / p.nw and the
+// Stage kernel (Q4 -> fp16 workspace rows of the keys in [p.stage_lo, p.stage_hi)) and/or
+// attention kernel (parts: kPrefillStage | kPrefillAttend); p.kd / p.vd / p.nw and the
 // tensor maps tmap_kd / tmap_vd describe the workspace.
-cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16,
+constexpr int kPrefillStage = 1, kPrefillAttend = 2;
+cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16, int parts,
                            cudaStream_t stream);
 
 // Split size (tokens per CTA chunk), number of chunks and merge mode (1: in-cluster merge)

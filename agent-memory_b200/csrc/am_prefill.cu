@@ -395,6 +395,8 @@ __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constan
     if (blockIdx.x == 0 && h == 0 && threadIdx.x == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
     hi = lo + p.nw;
   }
+  // rows of keys outside [stage_lo, stage_hi) belong to another stage call: left untouched
+  if (lo + r0 >= p.stage_hi || lo + r0 + kStageRows <= p.stage_lo) return;
   uint4 code[ITEMS];
   uint16_t sc[ITEMS], bi[ITEMS];
   bool live[ITEMS];
@@ -406,7 +408,7 @@ __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constan
     live[k] = false;
     code[k] = make_uint4(0, 0, 0, 0);
     sc[k] = bi[k] = 0;
-    if (item < kStageRows * CPR && r < p.nw && t < hi) {
+    if (item < kStageRows * CPR && r < p.nw && t < hi && t >= p.stage_lo && t < p.stage_hi) {
       int64_t row = -1;
       if constexpr (PAGED) {
         const int blk_i = t / p.block_tokens;
@@ -441,7 +443,7 @@ __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constan
   for (int k = 0; k < ITEMS; ++k) {
     const int item = threadIdx.x + 256 * k;
     const int r = r0 + item / CPR, c = item % CPR;
-    if (item >= kStageRows * CPR || r >= p.nw) continue;
+    if (item >= kStageRows * CPR || r >= p.nw || lo + r < p.stage_lo || lo + r >= p.stage_hi) continue;
     const int64_t plane_row = ((int64_t)b * p.hkv + h) * p.nw + r;
     uint16_t* dst = c < CK ? p.kd + plane_row * DK + c * 32 : p.vd + plane_row * DV + (c - CK) * 32;
     const float s = h2f<SBF16>(sc[k]), bias = h2f<SBF16>(bi[k]);
@@ -1809,27 +1811,30 @@ static cudaError_t launch_attn_t(const DecodeParams& p, int batch, cudaStream_t 
 
 template <int DK, int DV>
 static cudaError_t launch_prefill_dims(const DecodeParams& p0, int batch, bool paged, bool sbf16,
-                                       cudaStream_t stream) {
+                                       int parts, cudaStream_t stream) {
   DecodeParams p = p0;  // (the attention kernel's V dequantization reads the cache directly)
   p.paged = paged ? 1 : 0;
   p.scale_bf16 = sbf16 ? 1 : 0;
-  cudaError_t e = paged ? (sbf16 ? launch_stage_t<DK, DV, true, true>(p, batch, stream)
-                                 : launch_stage_t<DK, DV, false, true>(p, batch, stream))
-                        : (sbf16 ? launch_stage_t<DK, DV, true, false>(p, batch, stream)
-                                 : launch_stage_t<DK, DV, false, false>(p, batch, stream));
-  if (e != cudaSuccess) return e;
+  if (parts & kPrefillStage) {
+    cudaError_t e = paged ? (sbf16 ? launch_stage_t<DK, DV, true, true>(p, batch, stream)
+                                   : launch_stage_t<DK, DV, false, true>(p, batch, stream))
+                          : (sbf16 ? launch_stage_t<DK, DV, true, false>(p, batch, stream)
+                                   : launch_stage_t<DK, DV, false, false>(p, batch, stream));
+    if (e != cudaSuccess) return e;
+  }
+  if (!(parts & kPrefillAttend)) return cudaSuccess;
   return p.mask_kind != AM_MASK_NONE ? launch_attn_t<DK, DV, true>(p, batch, stream)
                                      : launch_attn_t<DK, DV, false>(p, batch, stream);
 }
 
-cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16,
+cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16, int parts,
                            cudaStream_t stream) {
   if (p.n_rep < 1 || p.n_rep > 128) return cudaErrorNotSupported;
-  if (p.k_dim == 128 && p.v_dim == 128) return launch_prefill_dims<128, 128>(p, batch, paged, scale_bf16, stream);
-  if (p.k_dim == 64 && p.v_dim == 64) return launch_prefill_dims<64, 64>(p, batch, paged, scale_bf16, stream);
-  if (p.k_dim == 128 && p.v_dim == 64) return launch_prefill_dims<128, 64>(p, batch, paged, scale_bf16, stream);
-  if (p.k_dim == 192 && p.v_dim == 128) return launch_prefill_dims<192, 128>(p, batch, paged, scale_bf16, stream);
-  if (p.k_dim == 256 && p.v_dim == 256) return launch_prefill_dims<256, 256>(p, batch, paged, scale_bf16, stream);
+  if (p.k_dim == 128 && p.v_dim == 128) return launch_prefill_dims<128, 128>(p, batch, paged, scale_bf16, parts, stream);
+  if (p.k_dim == 64 && p.v_dim == 64) return launch_prefill_dims<64, 64>(p, batch, paged, scale_bf16, parts, stream);
+  if (p.k_dim == 128 && p.v_dim == 64) return launch_prefill_dims<128, 64>(p, batch, paged, scale_bf16, parts, stream);
+  if (p.k_dim == 192 && p.v_dim == 128) return launch_prefill_dims<192, 128>(p, batch, paged, scale_bf16, parts, stream);
+  if (p.k_dim == 256 && p.v_dim == 256) return launch_prefill_dims<256, 256>(p, batch, paged, scale_bf16, parts, stream);
   return cudaErrorNotSupported;
 }
 

@@ -307,19 +307,14 @@ def decode_workspace_bytes(view: CacheView, batch: int, n_q_heads: int, q_len: i
     return int(_lib.load().am_q4_attention_workspace_bytes(ctypes.byref(view.desc), ctypes.byref(a)))
 
 
-def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torch.Tensor,
-              max_kv_len: int, *, kv_start: torch.Tensor | None = None, causal: bool = False,
-              window: int = 0, mask: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
-              out: torch.Tensor | None = None, status: torch.Tensor | None = None,
-              mode: str = "auto", sinks: torch.Tensor | None = None) -> torch.Tensor:
-    """Attention of queries [B, Hq, L, Dk] over the cache -> [B, Hq, L, Dv].
-
-    kv_len/kv_start: int32 device tensors [B].  mode: "auto" (library dispatch), "decode"
-    (split-KV kernel) or "prefill" (tcgen05 kernel).  sinks: optional [Hq] attention-sink
-    logits (scaled-score units).  The workspace the chosen kernel needs (split-KV partials,
-    or the prefill kernel's fp16 rows of the visible keys and values) is allocated here from
-    the caching allocator, on the call's stream.
-    """
+def attention_args(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torch.Tensor,
+                   max_kv_len: int, *, kv_start: torch.Tensor | None = None, causal: bool = False,
+                   window: int = 0, mask: torch.Tensor | None = None,
+                   out_dtype: torch.dtype | None = None, out: torch.Tensor | None = None,
+                   status: torch.Tensor | None = None, sinks: torch.Tensor | None = None):
+    """The am_attn_args of an attention call (arguments as for `attention`) -> (args, keep,
+    out): `keep` holds the tensors the args point into, which must outlive every call made
+    with them.  Callers that issue the same call repeatedly build the args once."""
     dev = _require_cuda(queries, kv_len)
     B, Hq, L, Dk = queries.shape
     if Dk != view.k_dim:
@@ -363,18 +358,72 @@ def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torc
         a.sinks = sk.data_ptr()
     else:
         a.sinks = None
+    return a, keep, out
+
+
+def attention(view: CacheView, queries: torch.Tensor, scale: float, kv_len: torch.Tensor,
+              max_kv_len: int, *, kv_start: torch.Tensor | None = None, causal: bool = False,
+              window: int = 0, mask: torch.Tensor | None = None, out_dtype: torch.dtype | None = None,
+              out: torch.Tensor | None = None, status: torch.Tensor | None = None,
+              mode: str = "auto", sinks: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None,
+              stage_keys: tuple[int, int] | None = None) -> torch.Tensor:
+    """Attention of queries [B, Hq, L, Dk] over the cache -> [B, Hq, L, Dv].
+
+    kv_len/kv_start: int32 device tensors [B].  mode: "auto" (library dispatch), "decode"
+    (split-KV kernel) or "prefill" (tcgen05 kernel); "prefill_stage" dequantizes only the
+    keys at positions stage_keys = (lo, hi) (default: all) into `workspace`, and
+    "prefill_attend" runs only the attention kernel over a workspace that stage calls have
+    filled (am_q4_prefill_stage / am_q4_prefill_attend).  sinks: optional [Hq]
+    attention-sink logits (scaled-score units).  workspace: a contiguous uint8 device tensor
+    of at least the call's workspace bytes (256-byte aligned); by default the workspace the
+    chosen kernel needs (split-KV partials, or the prefill kernel's fp16 rows of the visible
+    keys and values) is allocated here from the caching allocator, on the call's stream.
+    """
+    a, keep, out = attention_args(view, queries, scale, kv_len, max_kv_len, kv_start=kv_start,
+                                  causal=causal, window=window, mask=mask, out_dtype=out_dtype,
+                                  out=out, status=status, sinks=sinks)
+    dev = out.device
     L_ = _lib.load()
-    fn = {"decode": "am_q4_decode", "prefill": "am_q4_prefill"}.get(mode, "am_q4_attention")
+    fn = {"decode": "am_q4_decode", "prefill": "am_q4_prefill",
+          "prefill_stage": "am_q4_prefill_stage",
+          "prefill_attend": "am_q4_prefill_attend"}.get(mode, "am_q4_attention")
     sizing = {"am_q4_decode": L_.am_q4_decode_workspace_bytes,
-              "am_q4_prefill": L_.am_q4_prefill_workspace_bytes,
-              "am_q4_attention": L_.am_q4_attention_workspace_bytes}[fn]
+              "am_q4_attention": L_.am_q4_attention_workspace_bytes}.get(
+                  fn, L_.am_q4_prefill_workspace_bytes)
     ws_bytes = int(sizing(ctypes.byref(view.desc), ctypes.byref(a)))
-    # the caching allocator's blocks are 512-byte aligned (the prefill workspace needs 256)
-    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev) if ws_bytes else None
+    if workspace is not None:
+        if (workspace.device != dev or workspace.dtype != torch.uint8
+                or not workspace.is_contiguous() or workspace.numel() < ws_bytes):
+            raise ValueError(f"workspace must be a contiguous uint8 tensor of at least {ws_bytes} "
+                             f"bytes on {dev}")
+        ws = workspace
+    else:
+        # the caching allocator's blocks are 512-byte aligned (the prefill workspace needs 256)
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev) if ws_bytes else None
     ws_ptr = ws.data_ptr() if ws is not None else None
-    rc = getattr(L_, fn)(ctypes.byref(view.desc), ctypes.byref(a), ws_ptr, ws_bytes, _stream(dev))
+    if fn == "am_q4_prefill_stage":
+        lo, hi = stage_keys if stage_keys is not None else (0, 2 ** 31 - 1)
+        rc = L_.am_q4_prefill_stage(ctypes.byref(view.desc), ctypes.byref(a), int(lo), int(hi),
+                                    ws_ptr, ws.numel() if ws is not None else 0, _stream(dev))
+    else:
+        rc = getattr(L_, fn)(ctypes.byref(view.desc), ctypes.byref(a), ws_ptr,
+                             ws.numel() if workspace is not None else ws_bytes, _stream(dev))
     check(fn, rc)
     return out
+
+
+def prefill_workspace_bytes(view: CacheView, batch: int, n_q_heads: int, q_len: int,
+                            max_kv_len: int, *, window: int = 0) -> int:
+    """Workspace bytes of a prefill call of this shape (fp16 rows of the visible keys and
+    values), for callers that keep their own workspaces (mode "prefill_stage" /
+    "prefill_attend")."""
+    a = AttnArgs()
+    a.batch, a.n_q_heads, a.q_len = int(batch), int(n_q_heads), int(q_len)
+    a.max_kv_len = int(max_kv_len)
+    a.window = int(window or 0)
+    a.scale = 1.0
+    return int(_lib.load().am_q4_prefill_workspace_bytes(ctypes.byref(view.desc), ctypes.byref(a)))
 
 
 # ----------------------------------------------------------------------------- pool blocks

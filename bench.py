@@ -23,6 +23,7 @@ reference's own MLX CPU path cannot run here: mlx is not installed) on a bounded
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -624,17 +625,56 @@ def measure_prefill(am, dev, steps, warmup, gen, workload="prefill"):
     out = torch.empty(layers, B, hq, L, dv, device=dev, dtype=bf)
     pos = torch.full((B,), P, dtype=torch.int32, device=dev)
     kv_len = torch.full((B,), N, dtype=torch.int32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    # The cached prefix of layer l + 1 is dequantized into the workspace on a side stream
+    # while layer l runs (am_q4_prefill_stage over keys [0, P)); on the layer's own path
+    # only the appended chunk is staged (keys [P, end)) before the attention kernel
+    # (am_q4_prefill_attend).  Two workspaces alternate between layers.  The layers run on
+    # a high-priority stream, so the side stream's stage blocks only take SMs the layer's
+    # kernels leave free.
+    lib = am._lib.load()
+    lowest, highest = torch.cuda.Stream.priority_range()
+    stream = torch.cuda.Stream(dev, priority=highest)
+    side = torch.cuda.Stream(dev, priority=lowest)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    prev_stream = torch.cuda.current_stream(dev)
+    torch.cuda.set_stream(stream)
+    win = [0 if is_global[l] else window for l in range(layers)]
+    args = [am.kernels.attention_args(views[l], q[l], dk ** -0.5, kv_len, N, causal=True,
+                                      window=win[l], out=out[l]) for l in range(layers)]
+    nbytes = max(am.kernels.prefill_workspace_bytes(views[l], B, hq, L, N, window=win[l])
+                 for l in range(layers))
+    ws = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+    pre_done = [torch.cuda.Event() for _ in range(layers)]
+    chunk_done = [torch.cuda.Event() for _ in range(layers)]
+    s_main, s_side = stream.cuda_stream, side.cuda_stream
+
+    def stage(l, lo, hi, st):
+        rc = lib.am_q4_prefill_stage(ctypes.byref(views[l].desc), ctypes.byref(args[l][0]), lo, hi,
+                                     ws[l % 2].data_ptr(), nbytes, st)
+        am._lib.check("am_q4_prefill_stage", rc)
 
     def step(ev=None):
+        side.wait_stream(stream)  # the previous step's layers are done with both workspaces
+        stage(0, 0, P, s_side)
+        pre_done[0].record(side)
         for l in range(layers):
             if ev is not None:
                 ev[l][0].record(stream)
             am.kernels.append(views[l], kc[l], vc[l], pos)
             if ev is not None:
                 ev[l][1].record(stream)
-            am.kernels.attention(views[l], q[l], dk ** -0.5, kv_len, N, causal=True, out=out[l],
-                                 window=0 if is_global[l] else window, mode="prefill")
+            stream.wait_event(pre_done[l])
+            stage(l, P, 2 ** 31 - 1, s_main)
+            chunk_done[l].record(stream)
+            rc = lib.am_q4_prefill_attend(ctypes.byref(views[l].desc), ctypes.byref(args[l][0]),
+                                          ws[l % 2].data_ptr(), nbytes, s_main)
+            am._lib.check("am_q4_prefill_attend", rc)
+            if l + 1 < layers:
+                # from here on the layer's stream runs only the attention kernel, and
+                # workspace (l + 1) % 2 is free (layer l - 1's attention came before)
+                side.wait_event(chunk_done[l])
+                stage(l + 1, 0, P, s_side)
+                pre_done[l + 1].record(side)
             if ev is not None:
                 ev[l][2].record(stream)
 
@@ -657,6 +697,7 @@ def measure_prefill(am, dev, steps, warmup, gen, workload="prefill"):
                              for l in range(layers)]))
     app_ms = float(np.mean([evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(steps)
                             for l in range(layers)]))
+    torch.cuda.set_stream(prev_stream)
     hbm, _, tf_sus, kind = peaks()
     # visible (query, key) pairs per (sequence, head): causal over prefix + chunk, and for a
     # window layer only the last `window` positions up to each query
@@ -674,10 +715,13 @@ def measure_prefill(am, dev, steps, warmup, gen, workload="prefill"):
                        "n_kv_heads": hkv, "k_dim": dk, "v_dim": dv,
                        "window": window, "global_layers": sum(is_global),
                        "cache": "256-token paged blocks at shuffled offsets",
-                       "step": "per layer: append the chunk (am_q4_append) + causal attention "
-                               "(am_q4_prefill)",
-                       "timing": "eager launches, CUDA events around every call"},
-            "roofline": {"kernel": "am_q4_prefill (prefill_stage_kernel + %s)" % (
+                       "step": "per layer: append the chunk (am_q4_append), dequantize its rows "
+                               "(am_q4_prefill_stage) and attend (am_q4_prefill_attend); the cached "
+                               "prefix of the next layer is dequantized on a side stream meanwhile",
+                       "timing": "eager launches; CUDA events around every append and every "
+                                 "stage + attention on the layer's stream"},
+            "roofline": {"kernel": "am_q4_prefill_stage (chunk rows) + am_q4_prefill_attend (%s), "
+                                   "prefix staged on a side stream" % (
                              "prefill2_kernel" if dk <= 128 and dv <= 128 else "prefill_kernel"),
                          "flops_per_launch_note": "layer mean of 2 * B * Hq * (Dk + Dv) * visible pairs",
                          "bound": "tensor", "achieved": round(flops / (attn_ms / 1e3) / 1e12, 2),

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define AM_ABI_VERSION 3
+#define AM_ABI_VERSION 4
 
 enum {
   AM_OK = 0,
@@ -203,6 +203,29 @@ int am_q4_decode_noalloc(const am_q4_cache* cache, const am_attn_args* args, voi
  */
 int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* args, void* workspace,
                   size_t workspace_bytes, void* stream);
+
+/*
+ * am_q4_prefill in two parts, so a serving loop can dequantize a layer's cached prefix
+ * ahead of time (on another stream, while the previous layer's attention runs) and only
+ * the newly appended chunk on the layer's critical path.  The reference has no such split:
+ * its chunked prefill (batch_engine.py:339-456) hands the whole Q4 cache to the compiled
+ * quantized SDPA (mlx_fused_attention.py:144-207), which dequantizes inside the call.
+ *
+ * am_q4_prefill_stage: the stage kernel alone, writing into `workspace` the fp16 rows of
+ * the visible keys (and values) at positions [key_lo, key_hi) of every sequence (rows of
+ * other positions are left untouched; positions at or past kv_len inside the range are
+ * written as zeros).  `args` describe the attention call the rows are for (the same
+ * batch, q_len, kv_len, kv_start, window, mask kind and max_kv_len as the later
+ * am_q4_prefill_attend); its query and output pointers are not read.
+ * am_q4_prefill_attend: the attention kernel alone, over a workspace in which stage calls
+ * covering [0, INT_MAX) together (e.g. [0, prefix) then [prefix, INT_MAX)) have written
+ * every row since the cache last changed.  Stage + attend over the same workspace give
+ * exactly the outputs of am_q4_prefill.
+ */
+int am_q4_prefill_stage(const am_q4_cache* cache, const am_attn_args* args, int32_t key_lo,
+                        int32_t key_hi, void* workspace, size_t workspace_bytes, void* stream);
+int am_q4_prefill_attend(const am_q4_cache* cache, const am_attn_args* args, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /*
  * quantized_scaled_dot_product_attention (mlx_fused_attention.py:462-484): dispatches to

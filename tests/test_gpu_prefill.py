@@ -252,3 +252,30 @@ def test_prefill_values_beyond_fp16_saturate(cuda, orc, geom):
         want[0, hq] = (p / p.sum(axis=1, keepdims=True)) @ vd[0, hq // n_rep]
     assert np.abs(want).max() > 1.0e4  # the saturated keys carry weight for later queries
     assert_close(got.cpu().numpy(), want, what=f"prefill {geom}, V beyond the fp16 range")
+
+
+@pytest.mark.parametrize("geom", [(2, 32, 8, 128, 128, 1112, 512, 0, 600),
+                                  (2, 16, 16, 192, 128, 520, 190, 0, 333),
+                                  (2, 16, 8, 256, 256, 620, 200, 128, 517)],
+                         ids=["llama_d128", "mla_k192_v128", "gemma_d256_window"])
+def test_prefill_stage_then_attend_matches_prefill(cuda, geom):
+    """am_q4_prefill_stage over two key ranges (the later range first, split inside a stage
+    CTA's rows) then am_q4_prefill_attend give exactly am_q4_prefill's outputs, over a
+    workspace filled with all-ones bytes (NaN as fp16) beforehand, so a row that no stage
+    call wrote would show."""
+    B, Hq, Hkv, Dk, Dv, N, L, window, split = geom
+    q, kq, vq = make_case(B, Hq, Hkv, N, Dk, Dv, L=L, cuda=cuda, seed=17)
+    view, n = pkg.kernels.contiguous_view(kq, vq)
+    kv_len = torch.full((B,), N, dtype=torch.int32, device=cuda)
+    qd = q.to(cuda)
+    kw = dict(causal=True, window=window, out_dtype=torch.float32)
+    want = pkg.kernels.attention(view, qd, Dk ** -0.5, kv_len, N, mode="prefill", **kw)
+    nbytes = pkg.kernels.prefill_workspace_bytes(view, B, Hq, L, N, window=window)
+    ws = torch.full((nbytes,), 255, dtype=torch.uint8, device=cuda)
+    for keys in ((split, 2 ** 31 - 1), (0, split)):
+        pkg.kernels.attention(view, qd, Dk ** -0.5, kv_len, N, mode="prefill_stage",
+                              workspace=ws, stage_keys=keys, **kw)
+    got = pkg.kernels.attention(view, qd, Dk ** -0.5, kv_len, N, mode="prefill_attend",
+                                workspace=ws, **kw)
+    torch.cuda.synchronize(cuda)
+    assert torch.equal(got, want), (got - want).abs().max()
