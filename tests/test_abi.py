@@ -96,3 +96,18 @@ def test_kernels_refuse_cpu_tensors():
     torch = pytest.importorskip("torch")
     with pytest.raises(ValueError, match="CUDA"):
         pkg.quantize(torch.zeros(2, 64, dtype=torch.float16))
+
+
+def test_prefill_stage_rejects_a_reversed_key_range():
+    """am_q4_prefill_stage checks its key range on the host before any device work."""
+    lib = pkg._lib.load()
+    d = pkg._lib.Q4CacheDesc()
+    for f in ("k_codes", "k_scales", "k_biases", "v_codes", "v_scales", "v_biases"):
+        setattr(d, f, 4096)
+    d.scale_dtype, d.layout, d.n_kv_heads, d.k_dim, d.v_dim = 0, 0, 8, 128, 128
+    d.capacity, d.batch = 256, 1
+    a = pkg._lib.AttnArgs()
+    a.q, a.out, a.kv_len, a.batch, a.n_q_heads, a.q_len, a.max_kv_len = 4096, 4096, 4096, 1, 32, 64, 256
+    for lo, hi in ((10, 5), (-1, 5)):
+        rc = lib.am_q4_prefill_stage(ctypes.byref(d), ctypes.byref(a), lo, hi, None, 0, None)
+        assert rc == pkg._lib.AM_ERR_INVALID and b"key range" in lib.am_last_error()
