@@ -735,7 +735,7 @@ def measure_prefill(am, dev, steps, warmup, gen, workload="prefill"):
                                 "frac": round(app_bytes / (app_ms / 1e3) / 1e9 / hbm, 4),
                                 "bytes_per_launch": int(app_bytes),
                                 "avg_launch_ms": round(app_ms, 5)},
-            "gpu_launches": steps * layers * 3, "clocks": clk}
+            "gpu_launches": steps * layers * 4, "clocks": clk}
 
 
 def run_single_workload(args, am, dev, rank, world):
