@@ -522,9 +522,18 @@ static int prefill_call(const am_q4_cache* cache, const am_attn_args* a, void* w
   p.kd = static_cast<uint16_t*>(workspace);
   p.vd = pl.v_bytes > 0 ? reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + pl.k_bytes) : nullptr;
   p.nw = pl.nw;
-  p.stage_lo = key_lo;
-  p.stage_hi = key_hi;
+  // The attention kernel reads rows up to its last key tile, which ends before key
+  // max_kv_len + tile: rows of later keys are never read and not staged.  A range narrower
+  // than the plane gets a grid of its own row blocks only (one more for the alignment of
+  // the first).
   const int bn = prefill_key_tile(cache->k_dim, cache->v_dim);
+  const int64_t hi_eff = std::min<int64_t>(key_hi, static_cast<int64_t>(a->max_kv_len) + bn);
+  const int64_t range_rows = std::max<int64_t>(hi_eff - key_lo, 0);
+  p.stage_lo = key_lo;
+  p.stage_hi = static_cast<int32_t>(hi_eff);
+  p.stage_blocks = range_rows + kStageRowsHost < pl.nw
+                       ? static_cast<int32_t>((range_rows + kStageRowsHost - 1) / kStageRowsHost + 1)
+                       : 0;
   if (!encode_codes_map(&p.tmap_kd, p.kd, pl.rows, cache->k_dim * 2, 128, bn) ||
       (pl.v_bytes > 0 && !encode_codes_map(&p.tmap_vd, p.vd, pl.rows, cache->v_dim * 2, 128, bn))) {
     set_error("%s: cannot describe the workspace as tensor maps (a driver with "

@@ -378,6 +378,9 @@ struct DecodeParams {
   // positions); am_q4_prefill stages every row, am_q4_prefill_stage a range of them.
   int32_t stage_lo;
   int32_t stage_hi;
+  // Row blocks of the stage grid (grid.x): 0 = every block of the plane; otherwise the grid
+  // covers only the blocks from the one holding key stage_lo on.
+  int32_t stage_blocks;
   // Prefill kernels that dequantize V tiles themselves read the cache directly: block-pool
   // layout (table, block_tokens) or contiguous rows, and the scale / bias type.
   int32_t paged;

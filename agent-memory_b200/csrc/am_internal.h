@@ -37,6 +37,8 @@ bool prefill_v_in_kernel(int k_dim, int v_dim);
 // attention kernel (parts: kPrefillStage | kPrefillAttend); p.kd / p.vd / p.nw and the
 // tensor maps tmap_kd / tmap_vd describe the workspace.
 constexpr int kPrefillStage = 1, kPrefillAttend = 2;
+// Workspace rows per block of the stage kernel's grid.
+constexpr int kStageRowsHost = 128;
 cudaError_t launch_prefill(const DecodeParams& p, int batch, bool paged, bool scale_bf16, int parts,
                            cudaStream_t stream);
 

@@ -371,7 +371,7 @@ __device__ __forceinline__ void q_chunks_store(uint8_t* tile, int qslab, const u
 // plane (b, h); the work items are 16-byte chunks of code words (32 elements each, K chunks
 // then V chunks of a row), and each thread issues the loads of all its items (codes, scale,
 // bias) before converting any, so enough bytes are in flight to stream at HBM speed.
-constexpr int kStageRows = 128;
+constexpr int kStageRows = kStageRowsHost;
 
 // One 32-byte store of 8 words (p 32-byte aligned).
 __device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&v)[8]) {
@@ -388,9 +388,12 @@ __global__ void __launch_bounds__(256) prefill_stage_kernel(const __grid_constan
   constexpr int ITEMS = (kStageRows * CPR + 255) / 256;
   constexpr int NGK = DK / 64, NGV = DV / 64;
   const int h = blockIdx.y, b = blockIdx.z;
-  const int r0 = blockIdx.x * kStageRows;
   int lo, hi;
   prefill_block_range(p, b, lo, hi);
+  // a grid sized for a key range starts at the row block holding key stage_lo
+  const int r_base =
+      p.stage_blocks > 0 ? (min(max(p.stage_lo - lo, 0), p.nw) & ~(kStageRows - 1)) : 0;
+  const int r0 = r_base + blockIdx.x * kStageRows;
   if (hi - lo > p.nw) {  // kv_len beyond the max_kv_len the workspace was sized for
     if (blockIdx.x == 0 && h == 0 && threadIdx.x == 0) flag_status(p.status, AM_STATUS_BAD_POSITION);
     hi = lo + p.nw;
@@ -1763,7 +1766,8 @@ static cudaError_t prefill_smem_once(F kfn, int bytes, unsigned long long* done_
 
 template <int DK, int DV, bool SBF16, bool PAGED>
 static cudaError_t launch_stage_t(const DecodeParams& p, int batch, cudaStream_t stream) {
-  dim3 grid((p.nw + kStageRows - 1) / kStageRows, p.hkv, batch);
+  const int plane_blocks = (p.nw + kStageRows - 1) / kStageRows;
+  dim3 grid(p.stage_blocks > 0 ? min(p.stage_blocks, plane_blocks) : plane_blocks, p.hkv, batch);
   prefill_stage_kernel<DK, DV, SBF16, PAGED, kPrefillVInKernel<DK, DV>><<<grid, 256, 0, stream>>>(p);
   return cudaGetLastError();
 }

@@ -213,8 +213,9 @@ int am_q4_prefill(const am_q4_cache* cache, const am_attn_args* args, void* work
  *
  * am_q4_prefill_stage: the stage kernel alone, writing into `workspace` the fp16 rows of
  * the visible keys (and values) at positions [key_lo, key_hi) of every sequence (rows of
- * other positions are left untouched; positions at or past kv_len inside the range are
- * written as zeros).  `args` describe the attention call the rows are for (the same
+ * other positions are left untouched; positions from kv_len up to the attention kernel's
+ * last key tile, which ends before max_kv_len + 128, are written as zeros, and later rows,
+ * which no attention call reads, are not written).  `args` describe the attention call the rows are for (the same
  * batch, q_len, kv_len, kv_start, window, mask kind and max_kv_len as the later
  * am_q4_prefill_attend); its query and output pointers are not read.
  * am_q4_prefill_attend: the attention kernel alone, over a workspace in which stage calls
