@@ -279,3 +279,48 @@ def test_prefill_stage_then_attend_matches_prefill(cuda, geom):
                                 workspace=ws, **kw)
     torch.cuda.synchronize(cuda)
     assert torch.equal(got, want), (got - want).abs().max()
+
+
+@pytest.mark.parametrize("geom", [(2, 32, 8, 128, 128, 700, 300, 0),
+                                  (2, 16, 8, 256, 256, 420, 200, 96),
+                                  (2, 16, 16, 192, 128, 330, 190, 0)],
+                         ids=["llama_d128", "gemma_d256_window", "mla_k192_v128"])
+def test_paged_prefill_stage_before_append_then_attend(cuda, geom):
+    """The serving order of the split prefill on the paged pool (bf16 scales, shuffled
+    256-token blocks): the cached prefix is staged BEFORE the chunk's K/V are appended (as
+    the bench's side stream does while the previous layer runs), then the chunk is appended,
+    its rows staged and attended; the outputs equal am_q4_prefill's after the append, bit
+    for bit, over a workspace filled with NaN bytes beforehand."""
+    A, Hq, Hkv, Dk, Dv, P, L, window = geom
+    bt = 256
+    spec = pkg.ModelCacheSpec(n_layers=1, n_kv_heads=Hkv, head_dim=Dk, block_tokens=bt,
+                              layer_types=["global"], v_head_dim=Dv)
+    alloc = pkg.shuffled_allocator(spec, 32, seed=3)
+    pool = pkg.PagedQ4Pool.for_spec(spec, 32, torch.bfloat16, cuda)
+    layer = pkg.PagedLayerCache(pool, alloc, 0, ["a0", "a1"][:A], P + L)
+    g = torch.Generator().manual_seed(5)
+    layer.append(torch.randn(A, Hkv, P, Dk, generator=g).bfloat16().to(cuda),
+                 torch.randn(A, Hkv, P, Dv, generator=g).bfloat16().to(cuda))
+    kc = torch.randn(A, Hkv, L, Dk, generator=g).bfloat16().to(cuda)
+    vc = torch.randn(A, Hkv, L, Dv, generator=g).bfloat16().to(cuda)
+    q = torch.randn(A, Hq, L, Dk, generator=g).bfloat16().to(cuda)
+    N = P + L
+    for r in range(A):
+        layer.reserve(r, N)
+    kv_len = torch.full((A,), N, dtype=torch.int32, device=cuda)
+    out = torch.empty(A, Hq, L, Dv, dtype=torch.float32, device=cuda)
+    kw = dict(causal=True, window=window, out=out)
+    nbytes = pkg.kernels.prefill_workspace_bytes(layer.view(), A, Hq, L, N, window=window)
+    ws = torch.full((nbytes,), 255, dtype=torch.uint8, device=cuda)
+    pkg.kernels.attention(layer.view(), q, Dk ** -0.5, kv_len, N, mode="prefill_stage",
+                          workspace=ws, stage_keys=(0, P), **kw)
+    layer.append(kc, vc)  # writes positions P .. N - 1 only
+    pkg.kernels.attention(layer.view(), q, Dk ** -0.5, kv_len, N, mode="prefill_stage",
+                          workspace=ws, stage_keys=(P, 2 ** 31 - 1), **kw)
+    pkg.kernels.attention(layer.view(), q, Dk ** -0.5, kv_len, N, mode="prefill_attend",
+                          workspace=ws, **kw)
+    got = out.clone()
+    want = pkg.kernels.attention(layer.view(), q, Dk ** -0.5, kv_len, N, mode="prefill",
+                                 causal=True, window=window, out_dtype=torch.float32)
+    torch.cuda.synchronize(cuda)
+    assert torch.equal(got, want), (got - want).abs().max()
