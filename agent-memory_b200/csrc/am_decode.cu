@@ -918,6 +918,19 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
   if (nc <= 1) return;
   const float* base = p.ws + ((int64_t)b * rows_total + row) * p.max_chunks * PF;
 
+  // the first eight chunks' slices are loaded together with the chunk maxima (independent
+  // loads, one round trip)
+  float4 x0[8][PER];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const float4* src = reinterpret_cast<const float4*>(base + (int64_t)u * PF + kPartialHead);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int v = lane + 32 * k;
+      x0[u][k] = (u < nc && (V4 % 32 == 0 || v < V4)) ? src[v] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+  }
+
   // (max, sum) over this lane's chunks, online, then across the warp
   float m = -INFINITY, l = 0.0f, m_first = -INFINITY;
   for (int c = lane; c < nc; c += 32) {
@@ -956,7 +969,10 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
           const int v = lane + 32 * k;
-          x[u][k] = (j0 + u < cnt && (V4 % 32 == 0 || v < V4)) ? src[v] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          if (c0 == 0 && j0 == 0)
+            x[u][k] = x0[u][k];  // (loaded above; zeros past nc)
+          else
+            x[u][k] = (j0 + u < cnt && (V4 % 32 == 0 || v < V4)) ? src[v] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
       }
 #pragma unroll
