@@ -638,66 +638,68 @@ def measure_prefill(am, dev, steps, warmup, gen, workload="prefill"):
     stream.wait_stream(torch.cuda.current_stream(dev))
     prev_stream = torch.cuda.current_stream(dev)
     torch.cuda.set_stream(stream)
-    win = [0 if is_global[l] else window for l in range(layers)]
-    args = [am.kernels.attention_args(views[l], q[l], dk ** -0.5, kv_len, N, causal=True,
-                                      window=win[l], out=out[l]) for l in range(layers)]
-    nbytes = max(am.kernels.prefill_workspace_bytes(views[l], B, hq, L, N, window=win[l])
-                 for l in range(layers))
-    ws = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(2)]
-    pre_done = [torch.cuda.Event() for _ in range(layers)]
-    chunk_done = [torch.cuda.Event() for _ in range(layers)]
-    s_main, s_side = stream.cuda_stream, side.cuda_stream
+    try:
+        win = [0 if is_global[l] else window for l in range(layers)]
+        args = [am.kernels.attention_args(views[l], q[l], dk ** -0.5, kv_len, N, causal=True,
+                                          window=win[l], out=out[l]) for l in range(layers)]
+        nbytes = max(am.kernels.prefill_workspace_bytes(views[l], B, hq, L, N, window=win[l])
+                     for l in range(layers))
+        ws = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+        pre_done = [torch.cuda.Event() for _ in range(layers)]
+        chunk_done = [torch.cuda.Event() for _ in range(layers)]
+        s_main, s_side = stream.cuda_stream, side.cuda_stream
 
-    def stage(l, lo, hi, st):
-        rc = lib.am_q4_prefill_stage(ctypes.byref(views[l].desc), ctypes.byref(args[l][0]), lo, hi,
-                                     ws[l % 2].data_ptr(), nbytes, st)
-        am._lib.check("am_q4_prefill_stage", rc)
+        def stage(l, lo, hi, st):
+            rc = lib.am_q4_prefill_stage(ctypes.byref(views[l].desc), ctypes.byref(args[l][0]), lo, hi,
+                                         ws[l % 2].data_ptr(), nbytes, st)
+            am._lib.check("am_q4_prefill_stage", rc)
 
-    def step(ev=None):
-        side.wait_stream(stream)  # the previous step's layers are done with both workspaces
-        stage(0, 0, P, s_side)
-        pre_done[0].record(side)
-        for l in range(layers):
-            if ev is not None:
-                ev[l][0].record(stream)
-            am.kernels.append(views[l], kc[l], vc[l], pos)
-            if ev is not None:
-                ev[l][1].record(stream)
-            stream.wait_event(pre_done[l])
-            stage(l, P, 2 ** 31 - 1, s_main)
-            chunk_done[l].record(stream)
-            rc = lib.am_q4_prefill_attend(ctypes.byref(views[l].desc), ctypes.byref(args[l][0]),
-                                          ws[l % 2].data_ptr(), nbytes, s_main)
-            am._lib.check("am_q4_prefill_attend", rc)
-            if l + 1 < layers:
-                # from here on the layer's stream runs only the attention kernel, and
-                # workspace (l + 1) % 2 is free (layer l - 1's attention came before)
-                side.wait_event(chunk_done[l])
-                stage(l + 1, 0, P, s_side)
-                pre_done[l + 1].record(side)
-            if ev is not None:
-                ev[l][2].record(stream)
+        def step(ev=None):
+            side.wait_stream(stream)  # the previous step's layers are done with both workspaces
+            stage(0, 0, P, s_side)
+            pre_done[0].record(side)
+            for l in range(layers):
+                if ev is not None:
+                    ev[l][0].record(stream)
+                am.kernels.append(views[l], kc[l], vc[l], pos)
+                if ev is not None:
+                    ev[l][1].record(stream)
+                stream.wait_event(pre_done[l])
+                stage(l, P, 2 ** 31 - 1, s_main)
+                chunk_done[l].record(stream)
+                rc = lib.am_q4_prefill_attend(ctypes.byref(views[l].desc), ctypes.byref(args[l][0]),
+                                              ws[l % 2].data_ptr(), nbytes, s_main)
+                am._lib.check("am_q4_prefill_attend", rc)
+                if l + 1 < layers:
+                    # from here on the layer's stream runs only the attention kernel, and
+                    # workspace (l + 1) % 2 is free (layer l - 1's attention came before)
+                    side.wait_event(chunk_done[l])
+                    stage(l + 1, 0, P, s_side)
+                    pre_done[l + 1].record(side)
+                if ev is not None:
+                    ev[l][2].record(stream)
 
-    for _ in range(warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(layers)]
-           for _ in range(steps)]
-    clocks = ClockSampler(dev.index)
-    clocks.start()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for s in range(steps):
-        step(evs[s])
-    t1.record(stream)
-    torch.cuda.synchronize(dev)
-    clk = clocks.stop()
-    ms = t0.elapsed_time(t1) / steps
-    attn_ms = float(np.mean([evs[s][l][1].elapsed_time(evs[s][l][2]) for s in range(steps)
-                             for l in range(layers)]))
-    app_ms = float(np.mean([evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(steps)
-                            for l in range(layers)]))
-    torch.cuda.set_stream(prev_stream)
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(layers)]
+               for _ in range(steps)]
+        clocks = ClockSampler(dev.index)
+        clocks.start()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for s in range(steps):
+            step(evs[s])
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        clk = clocks.stop()
+        ms = t0.elapsed_time(t1) / steps
+        attn_ms = float(np.mean([evs[s][l][1].elapsed_time(evs[s][l][2]) for s in range(steps)
+                                 for l in range(layers)]))
+        app_ms = float(np.mean([evs[s][l][0].elapsed_time(evs[s][l][1]) for s in range(steps)
+                                for l in range(layers)]))
+    finally:
+        torch.cuda.set_stream(prev_stream)
     hbm, _, tf_sus, kind = peaks()
     # visible (query, key) pairs per (sequence, head): causal over prefix + chunk, and for a
     # window layer only the last `window` positions up to each query
